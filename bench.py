@@ -1,0 +1,363 @@
+"""Decode throughput of the B200 path on the BASELINE workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--model llama-3.1-8b] [--batch B] [--prompt 128]
+
+Workload (the north-star config): Llama-3.1-8B-shaped
+decoder, random-init N(0, 0.02) bf16 weights generated on the device (no
+checkpoint), a 128-token uniform-random prompt, then greedy decode at batch 1.
+A step is one decode token for every slot: the whole model's weights stream
+from HBM once (15 GB > L2, so no step is served from L2).  N > 1 runs the
+same model tensor-parallel over N GPUs (strong scaling: the tokens are the
+same, the per-GPU work shrinks).
+
+Prints ONE JSON line (rank 0).  `value` is device-timed (CUDA events on the
+decode stream around K steps, inputs already in HBM, max over ranks); `e2e`
+is the same steps through the public C ABI with host buffers (seed upload and
+id readback inside the timed region); `roofline` is the dominant kernel
+(gate/up GEMV) against the measured HBM copy bandwidth; `cpu_baseline` is the
+CPU restatement of the reference's f32 host forward on this box's cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "reciprocating-engine_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            out = ""
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# --------------------------------------------------------------- CPU arm --
+
+def cpu_sample(cfg_full, tokens=32, layers=2, threads=0, seed=0, repeats=1):
+    """Time the oracle (CPU f32 forward restating the reference's
+    model_forward_cpu) on a layer-truncated model of the workload's widths:
+    per-layer time and LM-head time over `tokens` teacher-forced tokens,
+    scaled to the full depth.  Returns (tok/s, cores, sample description)."""
+    import numpy as np
+    import oracle
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = cfg_full
+    w = random_weights(cfg, seed=seed, layers=layers)
+    sin, cos = rope_caches_for(cfg, tokens)
+    base = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_heads=cfg.num_attention_heads,
+                n_kv_heads=cfg.n_kv_heads(), head_dim=cfg.head_dim(), vocab=cfg.vocab_size,
+                eps=cfg.rms_norm_eps, attn_scale=cfg.attention_scale(), has_bias=int(cfg.has_bias()))
+    ids = prompt_ids(tokens, cfg.vocab_size, seed=seed)
+    m_layers = oracle.Model(dict(base, n_layers=layers), w["layers"], w["final_gamma"],
+                            w["lm_head"], w["embed"])
+    m_head = oracle.Model(dict(base, n_layers=0), [], w["final_gamma"], w["lm_head"], w["embed"])
+    cores = oracle.lib().orc_max_threads() if threads <= 0 else threads
+    best = None
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        m_layers.forward(ids, sin, cos, logits_from=tokens, threads=threads)
+        t1 = time.perf_counter()
+        m_head.forward(ids, sin, cos, logits_from=0, threads=threads)
+        t2 = time.perf_counter()
+        per_layer = (t1 - t0) / layers
+        t_full = per_layer * cfg.num_hidden_layers + (t2 - t1)
+        tps = tokens / t_full
+        best = tps if best is None else max(best, tps)
+    sample = ("f32 host forward (oracle/forward_oracle.c, OpenMP) of a %d-layer model with the "
+              "workload's widths over %d teacher-forced tokens; per-layer time x %d layers + "
+              "LM head" % (layers, tokens, cfg.num_hidden_layers))
+    return best, cores, sample
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    tps = []
+    cores = 0
+    sample = ""
+    for _ in range(args.warmup):
+        cpu_sample(cfg, tokens=args.cpu_tokens)
+    for _ in range(args.steps):
+        v, cores, sample = cpu_sample(cfg, tokens=args.cpu_tokens)
+        tps.append(v)
+    v = statistics.median(tps)
+    line = {
+        "impl": "reference", "metric": "decode tok/s (b%d)" % args.batch, "value": v,
+        "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights, uniform-random prompt ids)",
+        "config": {"workload": args.model + " decode b%d" % args.batch, "prompt": args.prompt},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Rust for Intel Gaudi2 (no cargo/rustc or Gaudi here); its CPU "
+                "path is run as the oracle's C restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm --
+
+def run_ours(args, cfg):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from reng import _lib
+    from reng.model import Engine
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    _lib.lib()
+    nccl_id = None
+    if ws > 1:
+        import ctypes as C
+        buf = (C.c_uint8 * 128)()
+        if rank == 0:
+            _lib.call("reng_tp_unique_id", buf)
+        obj = [bytes(buf)]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+
+    w = random_weights(cfg, seed=args.seed, device=dev)
+    torch.cuda.synchronize()
+    cap = args.prompt + args.warmup + 2 * args.steps + 8
+    eng = Engine(cfg, w, batch=args.batch, capacity=cap, device=local, tp_rank=rank,
+                 tp_world=ws, nccl_id=nccl_id)
+    del w
+    torch.cuda.empty_cache()
+    B = args.batch
+    prompt = prompt_ids(args.prompt, cfg.vocab_size, seed=args.seed)
+
+    def fresh():
+        eng.reset(-1)
+        return [eng.prefill(b, prompt)[0] for b in range(B)]
+
+    st = torch.cuda.Stream(device=dev)
+    seeds = fresh()
+    if args.warmup > 0:
+        eng.decode(seeds, args.warmup)
+    # ---- value: device-timed K steps, inputs resident in HBM ----
+    seeds = fresh()
+    seeds_d = torch.tensor(seeds, dtype=torch.int32, device=dev)
+    out_d = torch.empty((args.steps, B), dtype=torch.int32, device=dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    with torch.cuda.stream(st):
+        e0.record(st)
+        eng.decode_device(seeds_d, args.steps, out_d, st.cuda_stream)
+        e1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if ws > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ids_value = out_d.cpu().numpy()
+    # ---- e2e: the same steps through the host-buffer C ABI call ----
+    seeds = fresh()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ids_e2e = eng.decode(seeds, args.steps)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    same = bool(np.array_equal(ids_value.astype(np.uint32), ids_e2e))
+    # ---- per-kernel timing for the roofline (resets the slots) ----
+    seeds = fresh()
+    eng.decode(seeds, args.steps // 2)
+    kt = eng.time_kernels(iters=max(32, cfg.num_hidden_layers))
+    kpl = eng.last_times().kernels_per_step
+
+    if rank == 0:
+        tokens = args.steps * B
+        value = tokens / (ms / 1e3)
+        peak, peak_kind = peaks()
+        ctx = args.prompt + args.steps // 2
+        bytes_step = (2 * cfg.active_params() / ws +
+                      (1 - 1.0 / ws) * 2 * cfg.hidden_size * cfg.vocab_size +
+                      B * ctx * cfg.kv_bytes_per_token() / ws)
+        h, inter = cfg.hidden_size, cfg.intermediate_size // ws
+        gu_bytes = 2 * inter * h * 2 + B * h * 2 + B * inter * 2
+        gu_ms = kt["gate_up"]
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        step_gbs = bytes_step / (ms / 1e3 / args.steps) / 1e9
+        line = {
+            "metric": "decode tok/s (b%d)" % B, "value": value, "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) bf16 weights, uniform-random prompt ids)",
+            "config": {"workload": "%s decode b%d, prompt %d, %d greedy steps%s" % (
+                args.model, B, args.prompt, args.steps, ", tensor-parallel %d" % ws if ws > 1 else ""),
+                "model": args.model, "batch": B, "prompt": args.prompt,
+                "parallelism": "tp%d" % ws if ws > 1 else "single",
+                "l2": "inputs larger than L2 (weights %.1f GB streamed per step)" % (bytes_step / 1e9)},
+            "clocks": clk,
+            "e2e": {"value": tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B / args.steps,
+                    "d2h_bytes_per_step": 4 * B, "ids_equal_device_run": same},
+            "gpu_launches": kpl * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "gemv<SWIGLU> gate/up (layer-cycled)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None, "bytes_per_launch": gu_bytes},
+            "step_roofline": {"bytes_per_step": bytes_step, "achieved_gbs": step_gbs,
+                              "frac_of_measured": step_gbs / peak,
+                              "frac_of_8tbs_spec": step_gbs / 8000.0},
+            "kernel_ms": kt,
+        }
+        if not args.no_cpu and ws == 1:
+            v, cores, sample = cpu_sample(cfg, tokens=args.cpu_tokens)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                                    "sample": sample}
+        if args.fp8:
+            line["fp8_quant"] = fp8_quant_bench(dev)
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def fp8_quant_bench(dev, iters=20):
+    """Config 0: bf16 [4096, 4096] -> E4M3 per-channel, GB/s of algorithmic
+    bytes (2 B in + 1 B out per element + 4 B per row), device-timed over a
+    rotation of matrices larger than L2 together."""
+    import torch
+    from reng import fp8
+    from reng.synth import fp8_config0_matrix
+    import numpy as np
+    rows = cols = 4096
+    w = torch.from_numpy(fp8_config0_matrix(rows, cols, seed=0).view(np.int16)).to(dev)
+    n = 16  # 16 x 48 MB > L2
+    ws = [w.clone() for _ in range(n)]
+    codes = [torch.empty((rows, cols), dtype=torch.uint8, device=dev) for _ in range(n)]
+    scales = [torch.empty(rows, dtype=torch.float32, device=dev) for _ in range(n)]
+    for i in range(n):
+        fp8.quantize_device(ws[i], rows, cols, 0, 0, codes=codes[i], scales=scales[i])
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        j = i % n
+        fp8.quantize_device(ws[j], rows, cols, 0, 0, codes=codes[j], scales=scales[j])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    b = rows * cols * 3 + rows * 4
+    peak, kind = peaks()
+    return {"matrix": "bf16 [4096,4096] N(0,0.02) 0.1%% x50 -> e4m3 pcs", "ms": ms,
+            "gbs": b / (ms / 1e3) / 1e9, "frac": b / (ms / 1e3) / 1e9 / peak, "peak_kind": kind}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama-3.1-8b")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-tokens", type=int, default=32)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--fp8", action="store_true", default=True)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    from reng.config import SHAPES
+    cfg = SHAPES[args.model]()
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

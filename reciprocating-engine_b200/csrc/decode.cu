@@ -1,0 +1,635 @@
+// Decode-step kernels for B200 (sm_100a): packed-weight GEMV with fused
+// RMSNorm and epilogues, split-K flash-decode GQA attention, embedding
+// gather, and weight packing.
+//
+// Reference op sequence (crates/reng-synapse/src/model.rs:1172-1944 and the
+// head at :2535-2664): rms1 -> q,k,v (+bias) -> RoPE -> KV write -> GQA
+// attention -> o_proj -> +res -> rms2 -> gate,up -> SiLU*up -> down -> +res;
+// final rms -> LM head -> bf16 logits -> argmax.  Here that is five kernels
+// per layer plus an embedding gather and the LM head:
+//
+//   embed      x_res = embed[id]; norm partials of x_res
+//   gemv<QKV>  rms1 (from partials) fused into the x fragments; q/k/v rows
+//              paired (d, d+hd/2) per tile so RoPE is lane-local; k and v
+//              written straight into the KV cache, q to a buffer
+//   attn       split-K flash decode over the cache, last CTA combines
+//   gemv<RES>  o_proj, x_res += bf16(o) in bf16, norm partials of x_res
+//   gemv<SWIGLU> rms2 fused; gate/up rows paired per tile, silu(g)*u
+//   gemv<RES>  down_proj, x_res += bf16(d), norm partials
+//   gemv<LOGITS> final rms fused; bf16 logits; argmax partials, the last
+//              CTA picks the ids (first index of the max), advances the
+//              positions and the step counter
+#include <algorithm>
+
+#include "decode.cuh"
+
+namespace reng {
+
+// ------------------------------------------------------------------ GEMV --
+
+// The x fragment of lane (g, q) for k-chunk c: row g, k = 32c + 8q .. +8,
+// as 4 u32 of packed bf16, RMS-normalised when the args carry a norm.
+__device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, int K, int c, int g, int q,
+                                            float inv) {
+    uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    const int k = c * kChunkK + q * 8;
+    if (g >= a.M || k >= K) return z;
+    uint4 v = ldg_nc(a.x + (size_t)g * a.ldx + k);
+    if (a.ss_in == nullptr) return v;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain + k));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain + k + 4));
+    uint4 r;
+    r.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+    r.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+    r.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+    r.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+    return r;
+}
+
+// Lexicographic argmax step: larger value, then lower index.
+__device__ __forceinline__ void am_take(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__device__ __forceinline__ void am_reduce_g(float& bv, int& bi) {
+    // across the 8 lanes that share q (xor over the g bits 2,3,4 of the lane id)
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        am_take(bv, bi, ov, oi);
+    }
+}
+
+template <int EPI, int NWARP>
+__global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a) {
+    const int K = a.K;
+    __shared__ float4 red[NWARP > 1 ? NWARP : 1][32];
+    __shared__ float inv_s[kMaxRows];
+    __shared__ int s_ids[kMaxRows];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int kc_per = (a.kc + NWARP - 1) / NWARP;
+    const int c0 = min(a.kc, warp * kc_per), c1 = min(a.kc, c0 + kc_per);
+
+    // Independent of the predecessor: pull this warp's first weight range
+    // into L2 while the previous kernel drains.
+    if (lane == 0 && blockIdx.x < a.tiles && c1 > c0) {
+        const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * kBlockBytes;
+        uint32_t bytes = (uint32_t)(c1 - c0) * kBlockBytes;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+    }
+    pdl_wait();
+    pdl_launch();
+
+    if (a.ss_in != nullptr) {
+        for (int m = warp; m < a.M; m += NWARP) {
+            float s = 0.0f;
+            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kMaxRows + m];
+            s = warp_sum(s);
+            if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
+        }
+        __syncthreads();
+    }
+    const float inv = (a.ss_in != nullptr && g < a.M) ? inv_s[g] : 1.0f;
+
+    float best_v[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0, 0};
+
+    constexpr int U = 8;
+    for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
+        const uint8_t* wt = a.w + (size_t)tile * a.kc * kBlockBytes + lane * 16;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = c0; c < c1; c += U) {
+            uint4 wa[U], wb[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (c + u < c1) {
+                    wa[u] = ldg_stream(wt + (size_t)(c + u) * kBlockBytes);
+                    wb[u] = ldg_stream(wt + (size_t)(c + u) * kBlockBytes + 512);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (c + u < c1) {
+                    uint4 xf = x_fragment(a, K, c + u, g, q, inv);
+                    mma_bf16_16816(acc, wa[u].x, wb[u].x, wa[u].y, wb[u].y, xf.x, xf.y);
+                    mma_bf16_16816(acc, wa[u].z, wb[u].z, wa[u].w, wb[u].w, xf.z, xf.w);
+                }
+            }
+        }
+        if (NWARP > 1) {
+            __syncthreads();
+            red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (warp != 0) continue;
+#pragma unroll
+            for (int w = 1; w < NWARP; w++) {
+                float4 r = red[w][lane];
+                acc[0] += r.x; acc[1] += r.y; acc[2] += r.z; acc[3] += r.w;
+            }
+        }
+        // ---- epilogue (warp 0): acc = rows {g, g+8} x cols {2q, 2q+1} ----
+        const int m0 = 2 * q, m1 = 2 * q + 1;
+        if (EPI == EPI_RESID) {
+            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+            float s0 = 0.f, s1 = 0.f;
+            if (m0 < a.M) {
+                uint16_t* o = a.out + (size_t)m0 * a.ldo;
+                float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[0]));
+                float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[2]));
+                o[r0] = f32_to_bf16_bits(x0);
+                o[r1] = f32_to_bf16_bits(x1);
+                s0 = x0 * x0 + x1 * x1;
+            }
+            if (m1 < a.M) {
+                uint16_t* o = a.out + (size_t)m1 * a.ldo;
+                float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[1]));
+                float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[3]));
+                o[r0] = f32_to_bf16_bits(x0);
+                o[r1] = f32_to_bf16_bits(x1);
+                s1 = x0 * x0 + x1 * x1;
+            }
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            }
+            if (g == 0) {
+                if (m0 < a.M) a.ss_out[tile * kMaxRows + m0] = s0;
+                if (m1 < a.M) a.ss_out[tile * kMaxRows + m1] = s1;
+            }
+        } else if (EPI == EPI_F32) {
+            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+            if (m0 < a.M) {
+                a.out_f32[(size_t)m0 * a.ldo + r0] = acc[0];
+                a.out_f32[(size_t)m0 * a.ldo + r1] = acc[2];
+            }
+            if (m1 < a.M) {
+                a.out_f32[(size_t)m1 * a.ldo + r0] = acc[1];
+                a.out_f32[(size_t)m1 * a.ldo + r1] = acc[3];
+            }
+        } else if (EPI == EPI_SWIGLU) {
+            const int j = tile * 8 + g;
+            if (m0 < a.M) {
+                float gt = acc[0], up = acc[2];
+                a.out[(size_t)m0 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
+            }
+            if (m1 < a.M) {
+                float gt = acc[1], up = acc[3];
+                a.out[(size_t)m1 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
+            }
+        } else if (EPI == EPI_QKV) {
+            const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;  // pair tiles per head
+            const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
+            if (tile < a.q_tiles + a.k_tiles) {
+                const bool is_q = tile < a.q_tiles;
+                const int t = is_q ? tile : tile - a.q_tiles;
+                const int h = t / ppt, d = (t % ppt) * 8 + g, d2 = d + half;
+                const int brow = is_q ? h * hd : q_dim + h * hd;
+                float b1 = a.bias ? a.bias[brow + d] : 0.f, b2 = a.bias ? a.bias[brow + d2] : 0.f;
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int m = e ? m1 : m0;
+                    if (m >= a.M) continue;
+                    const int pos = a.row_pos[m];
+                    if (pos >= a.cap) continue;
+                    float x1 = (e ? acc[1] : acc[0]) + b1;
+                    float x2 = (e ? acc[3] : acc[2]) + b2;
+                    const float* cs = a.rope_cos + (size_t)pos * hd;
+                    const float* sn = a.rope_sin + (size_t)pos * hd;
+                    float y1 = x1 * cs[d] - x2 * sn[d];
+                    float y2 = x2 * cs[d2] + x1 * sn[d2];
+                    if (is_q) {
+                        uint16_t* o = a.out + (size_t)m * a.ldo + h * hd;
+                        o[d] = f32_to_bf16_bits(y1);
+                        o[d2] = f32_to_bf16_bits(y2);
+                    } else {
+                        const int slot = a.row_slot[m];
+                        uint16_t* kc = a.kcache + (((size_t)slot * a.n_kv + h) * a.cap + pos) * hd;
+                        kc[d] = f32_to_bf16_bits(y1);
+                        kc[d2] = f32_to_bf16_bits(y2);
+                    }
+                }
+            } else {
+                const int vt = tile - a.q_tiles - a.k_tiles;
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int r = vt * kTileRows + g + rr * 8;
+                    const int h = r / hd, d = r % hd;
+                    const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int m = e ? m1 : m0;
+                        if (m >= a.M) continue;
+                        const int pos = a.row_pos[m];
+                        if (pos >= a.cap) continue;
+                        const int slot = a.row_slot[m];
+                        float val = acc[rr * 2 + e] + b;
+                        a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] =
+                            f32_to_bf16_bits(val);
+                    }
+                }
+            }
+        } else if (EPI == EPI_LOGITS) {
+            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int m = e ? m1 : m0;
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                if (m < a.M) {
+                    if (r0 < a.vocab) {
+                        uint16_t b = f32_to_bf16_bits(acc[e]);
+                        a.out[(size_t)m * a.ldo + r0] = b;
+                        am_take(bv, bi, bf16_bits_to_f32(b), r0);
+                    }
+                    if (r1 < a.vocab) {
+                        uint16_t b = f32_to_bf16_bits(acc[2 + e]);
+                        a.out[(size_t)m * a.ldo + r1] = b;
+                        am_take(bv, bi, bf16_bits_to_f32(b), r1);
+                    }
+                }
+                am_reduce_g(bv, bi);
+                am_take(best_v[e], best_i[e], bv, bi);
+            }
+        }
+    }
+
+    if (EPI == EPI_LOGITS) {
+        if (warp == 0 && g == 0) {
+            if (2 * q < kMaxRows) {
+                a.am_val[blockIdx.x * kMaxRows + 2 * q] = best_v[0];
+                a.am_idx[blockIdx.x * kMaxRows + 2 * q] = best_i[0];
+                a.am_val[blockIdx.x * kMaxRows + 2 * q + 1] = best_v[1];
+                a.am_idx[blockIdx.x * kMaxRows + 2 * q + 1] = best_i[1];
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = (atomicAdd(a.am_count, 1u) == gridDim.x - 1);
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        // the last CTA: reduce the per-CTA partials of every row (warp m)
+        for (int m = warp; m < a.M; m += NWARP) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int b = lane; b < (int)gridDim.x; b += 32)
+                am_take(bv, bi, __ldcg(a.am_val + b * kMaxRows + m), __ldcg(a.am_idx + b * kMaxRows + m));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                am_take(bv, bi, ov, oi);
+            }
+            if (bi == 0x7fffffff) bi = 0;  // all NaN: the reference's initial index
+            s_ids[m] = bi;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (a.mode == 0) {
+                const int s = *a.step;
+                for (int m = 0; m < a.M; m++) {
+                    a.ids_ring[(size_t)(s + 1) * a.batch + m] = (uint32_t)s_ids[m];
+                    a.pos[m] += 1;
+                }
+                *a.step = s + 1;
+            } else {
+                *a.next_id = (uint32_t)s_ids[a.M - 1];
+            }
+            *a.am_count = 0u;
+            __threadfence();
+        }
+    }
+}
+
+template <int EPI>
+static cudaError_t launch_gemv_t(const GemvArgs& a, int nwarp, int grid, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(nwarp * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    switch (nwarp) {
+        case 4: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 4>, a);
+        case 8: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 8>, a);
+        case 16: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 16>, a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int EPI>
+static int blocks_t(int nwarp) {
+    int n = 0;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4>, 128, 0);
+    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8>, 256, 0);
+    if (nwarp == 16) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 16>, 512, 0);
+    return e == cudaSuccess ? n : 1;
+}
+
+int gemv_blocks_per_sm(int epi, int nwarp) {
+    switch (epi) {
+        case EPI_QKV: return blocks_t<EPI_QKV>(nwarp);
+        case EPI_RESID: return blocks_t<EPI_RESID>(nwarp);
+        case EPI_SWIGLU: return blocks_t<EPI_SWIGLU>(nwarp);
+        case EPI_LOGITS: return blocks_t<EPI_LOGITS>(nwarp);
+        case EPI_F32: return blocks_t<EPI_F32>(nwarp);
+        default: return 1;
+    }
+}
+
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int grid, bool pdl, cudaStream_t st) {
+    switch (epi) {
+        case EPI_QKV: return launch_gemv_t<EPI_QKV>(a, nwarp, grid, pdl, st);
+        case EPI_RESID: return launch_gemv_t<EPI_RESID>(a, nwarp, grid, pdl, st);
+        case EPI_SWIGLU: return launch_gemv_t<EPI_SWIGLU>(a, nwarp, grid, pdl, st);
+        case EPI_LOGITS: return launch_gemv_t<EPI_LOGITS>(a, nwarp, grid, pdl, st);
+        case EPI_F32: return launch_gemv_t<EPI_F32>(a, nwarp, grid, pdl, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ------------------------------------------------------------- attention --
+// One CTA per (split of kAttnChunk keys, KV group, row).  All hpg query
+// heads of the group share each K/V tile (GQA reuse).  f32 online softmax
+// per split; the last CTA of a (row, group) combines the splits.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxHpg = 8;
+constexpr int kAttnMaxHd = 128;
+constexpr int kAttnMaxSplits = 128;
+
+__global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
+    constexpr int CH = kAttnChunk;
+    constexpr int KP = kAttnMaxHd + 8;  // padded row (bf16)
+    __shared__ __align__(16) uint16_t Ks[CH * KP];
+    __shared__ __align__(16) uint16_t Vs[CH * KP];
+    __shared__ __align__(16) float Qs[kAttnMaxHpg * kAttnMaxHd];
+    __shared__ float Ps[kAttnMaxHpg][CH];
+    __shared__ float Ms[kAttnMaxHpg], Ls[kAttnMaxHpg];
+    __shared__ float Wc[kAttnMaxHpg][kAttnMaxSplits];
+    __shared__ int s_last;
+
+    const int s = blockIdx.x, grp = blockIdx.y, m = blockIdx.z;
+    const int hd = a.hd, hpg = a.hpg, tid = threadIdx.x;
+    pdl_wait();
+    pdl_launch();
+    const int pos = a.row_pos[m];
+    const int nkeys = min(pos + 1, a.cap);
+    const int nsplit = (nkeys + CH - 1) / CH;
+    if (s >= nsplit) return;
+    const int slot = a.row_slot[m];
+    const int k0 = s * CH, kn = min(CH, nkeys - k0);
+    const size_t cache_off = (((size_t)slot * a.n_kv + grp) * a.cap + k0) * hd;
+    const int q_dim = a.n_kv * hpg * hd;
+
+    // stage q (hpg heads) as f32, and the K/V chunk
+    const uint16_t* qrow = a.q + (size_t)m * q_dim + (size_t)grp * hpg * hd;
+    for (int i = tid; i < hpg * hd; i += kAttnThreads) Qs[i] = bf16_bits_to_f32(qrow[i]);
+    const int vec_per_row = hd / 8;
+    for (int i = tid; i < kn * vec_per_row; i += kAttnThreads) {
+        const int j = i / vec_per_row, v = i % vec_per_row;
+        uint4 kv = ldg_nc(a.kcache + cache_off + (size_t)j * hd + v * 8);
+        uint4 vv = ldg_nc(a.vcache + cache_off + (size_t)j * hd + v * 8);
+        *reinterpret_cast<uint4*>(&Ks[j * KP + v * 8]) = kv;
+        *reinterpret_cast<uint4*>(&Vs[j * KP + v * 8]) = vv;
+    }
+    __syncthreads();
+
+    // scores: thread -> key j, heads h = hh, hh+2, ...
+    {
+        const int j = tid % CH, hh = tid / CH;
+        for (int h = hh; h < hpg; h += kAttnThreads / CH) {
+            float sc = -INFINITY;
+            if (j < kn) {
+                float acc = 0.f;
+                const float* qh = Qs + h * hd;
+                for (int d = 0; d < hd; d += 8) {
+                    uint4 kv = *reinterpret_cast<const uint4*>(&Ks[j * KP + d]);
+                    acc += qh[d + 0] * bf16lo(kv.x) + qh[d + 1] * bf16hi(kv.x) +
+                           qh[d + 2] * bf16lo(kv.y) + qh[d + 3] * bf16hi(kv.y) +
+                           qh[d + 4] * bf16lo(kv.z) + qh[d + 5] * bf16hi(kv.z) +
+                           qh[d + 6] * bf16lo(kv.w) + qh[d + 7] * bf16hi(kv.w);
+                }
+                sc = acc;
+            }
+            Ps[h][j] = sc;
+        }
+    }
+    __syncthreads();
+    // softmax statistics per head (warp h, h+4, ...)
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int h = warp; h < hpg; h += kAttnThreads / 32) {
+            float mx = -INFINITY;
+            for (int j = lane; j < CH; j += 32) mx = fmaxf(mx, Ps[h][j]);
+            mx = warp_max(mx);
+            float sum = 0.f;
+            for (int j = lane; j < CH; j += 32) {
+                float p = (j < kn) ? expf(Ps[h][j] - mx) : 0.f;
+                Ps[h][j] = p;
+                sum += p;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                Ms[h] = mx;
+                Ls[h] = sum;
+            }
+        }
+    }
+    __syncthreads();
+    // P @ V: each thread four output dims of one head
+    const int per_head = hd / 4;
+    const size_t pbase = (((size_t)m * a.n_kv + grp) * a.nsplit_max + s) * hpg;
+    for (int o = tid; o < hpg * per_head; o += kAttnThreads) {
+        const int h = o / per_head, d = (o % per_head) * 4;
+        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+        for (int j = 0; j < kn; j++) {
+            const float p = Ps[h][j];
+            uint2 vv = *reinterpret_cast<const uint2*>(&Vs[j * KP + d]);
+            acc0 += p * bf16lo(vv.x);
+            acc1 += p * bf16hi(vv.x);
+            acc2 += p * bf16lo(vv.y);
+            acc3 += p * bf16hi(vv.y);
+        }
+        if (nsplit == 1) {
+            const float il = 1.0f / Ls[h];
+            uint16_t* out = a.out + (size_t)m * q_dim + ((size_t)grp * hpg + h) * hd + d;
+            out[0] = f32_to_bf16_bits(acc0 * il);
+            out[1] = f32_to_bf16_bits(acc1 * il);
+            out[2] = f32_to_bf16_bits(acc2 * il);
+            out[3] = f32_to_bf16_bits(acc3 * il);
+        } else {
+            float* po = a.part_o + (pbase + h) * hd + d;
+            *reinterpret_cast<float4*>(po) = make_float4(acc0, acc1, acc2, acc3);
+        }
+    }
+    if (nsplit == 1) return;
+    if (tid < hpg) {
+        a.part_ml[(pbase + tid) * 2 + 0] = Ms[tid];
+        a.part_ml[(pbase + tid) * 2 + 1] = Ls[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned int* cnt = a.count + (size_t)m * a.n_kv + grp;
+    if (tid == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(nsplit - 1));
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // combine: weights w[h][s] = exp(m_s - M) / sum_s exp(m_s - M) l_s
+    const size_t base0 = (((size_t)m * a.n_kv + grp) * a.nsplit_max) * hpg;
+    for (int h = tid; h < hpg; h += kAttnThreads) {
+        float mx = -INFINITY;
+        for (int t = 0; t < nsplit; t++) mx = fmaxf(mx, __ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2));
+        float den = 0.f;
+        for (int t = 0; t < nsplit; t++) {
+            float e = expf(__ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2) - mx);
+            Wc[h][t] = e;
+            den += e * __ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2 + 1);
+        }
+        const float iden = 1.0f / den;
+        for (int t = 0; t < nsplit; t++) Wc[h][t] *= iden;
+    }
+    __syncthreads();
+    for (int o = tid; o < hpg * hd; o += kAttnThreads) {
+        const int h = o / hd, d = o % hd;
+        float acc = 0.f;
+        for (int t = 0; t < nsplit; t++)
+            acc += Wc[h][t] * __ldcg(a.part_o + (base0 + (size_t)t * hpg + h) * hd + d);
+        a.out[(size_t)m * q_dim + ((size_t)grp * hpg + h) * hd + d] = f32_to_bf16_bits(acc);
+    }
+    if (tid == 0) *cnt = 0u;
+}
+
+cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t st) {
+    if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.nsplit_max > kAttnMaxSplits)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(a.nsplit_max, a.n_kv, a.M);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn, a);
+}
+
+// ----------------------------------------------------------------- embed --
+__global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
+    const int m = blockIdx.x;
+    pdl_wait();
+    pdl_launch();
+    int slot, pos;
+    uint32_t id;
+    if (a.mode == 0) {
+        slot = m;
+        pos = a.pos[m];
+        id = a.ids_ring[(size_t)(*a.step) * a.batch + m];
+    } else {
+        slot = a.slot;
+        pos = a.pos[a.slot] + m;
+        id = a.prefill_ids[m];
+    }
+    if (id >= (uint32_t)a.vocab) id = 0;  // the host refuses such ids; never read out of range
+    if (threadIdx.x == 0) {
+        a.row_slot[m] = slot;
+        a.row_pos[m] = pos;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(a.table + (size_t)id * a.hidden);
+    uint4* dst = reinterpret_cast<uint4*>(a.x_res + (size_t)m * a.hidden);
+    const int nv = a.hidden / 8;  // hidden % 16 == 0: pairs of chunks are whole tiles
+    for (int base = 0; base < nv; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        float ss = 0.f;
+        if (i < nv) {
+            uint4 v = ldg_nc(src + i);
+            dst[i] = v;
+            float t[8] = {bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y),
+                          bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)};
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss += t[e] * t[e];
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        if (i < nv && (i & 1) == 0) a.ss_out[(i >> 1) * kMaxRows + m] = ss;
+    }
+}
+
+cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(a.M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_embed, a);
+}
+
+// ------------------------------------------------------------------ pack --
+// One thread per (block, half, lane) 16-byte piece of the packed layout.
+__global__ void k_pack(PackArgs a) {
+    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(i & 31), h = (int)((i >> 5) & 1);
+        const int64_t blk = i >> 6;
+        const int c = (int)(blk % a.kc);
+        const int tile = (int)(blk / a.kc);
+        const int prow = tile * kTileRows + h * 8 + (lane >> 2);
+        const int srow = a.rowmap[prow];
+        const int k0 = c * kChunkK + (lane & 3) * 8;
+        uint16_t v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            uint16_t b = 0;
+            if (srow >= 0 && k0 + e < a.K) {
+                b = a.src[(int64_t)srow * a.ld + k0 + e];
+                if (a.scale != 0.0f && srow < a.scale_rows)
+                    b = f32_to_bf16_bits(bf16_bits_to_f32(b) * a.scale);
+            }
+            v[e] = b;
+        }
+        uint4 o;
+        o.x = v[0] | ((uint32_t)v[1] << 16);
+        o.y = v[2] | ((uint32_t)v[3] << 16);
+        o.z = v[4] | ((uint32_t)v[5] << 16);
+        o.w = v[6] | ((uint32_t)v[7] << 16);
+        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytes + h * 512 + lane * 16) = o;
+    }
+}
+
+cudaError_t launch_pack(const PackArgs& a, cudaStream_t st) {
+    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+    k_pack<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+__global__ void k_bf16_to_f32(const uint16_t* s, float* d, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        d[i] = bf16_bits_to_f32(s[i]);
+}
+
+cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, int64_t n, cudaStream_t st) {
+    int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+    if (grid < 1) grid = 1;
+    k_bf16_to_f32<<<grid, 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+}  // namespace reng

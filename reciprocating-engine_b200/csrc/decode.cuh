@@ -1,0 +1,127 @@
+// Kernel interfaces of the decode step (see decode.cu for the kernels).
+#pragma once
+#include "common.cuh"
+
+namespace reng {
+
+// Packed weight block: 16 rows x 32 k of bf16 = 1024 bytes.  Lane l of a
+// warp holds, in half h (rows 8h..8h+7), the 8 values of row 8h + l/4 at
+// k = 32c + 8*(l%4) .. +8, stored at byte h*512 + l*16 of block (tile, c).
+constexpr int kTileRows = 16;
+constexpr int kChunkK = 32;
+constexpr int kBlockBytes = 1024;
+constexpr int kMaxRows = 8;  // activation rows per GEMV launch (mma N)
+
+enum Epi : int {
+    EPI_QKV = 0,     // bias + RoPE, q to a buffer, k/v into the KV cache
+    EPI_RESID = 1,   // x_res += bf16(acc) (bf16), norm partials of x_res
+    EPI_SWIGLU = 2,  // act = silu(gate) * up
+    EPI_LOGITS = 3,  // bf16 logits + argmax partials, last CTA picks the ids
+    EPI_F32 = 4,     // f32 partial out (tensor-parallel o_proj / down_proj)
+};
+
+struct GemvArgs {
+    // weights
+    const uint8_t* w;  // packed blocks
+    int tiles;         // 16-row tiles
+    int kc;            // 32-wide k chunks
+    int K;             // input width (x columns used; the packing zero-pads to kc*32)
+    int M;             // activation rows (<= kMaxRows)
+    // activations x [M][ldx] bf16
+    const uint16_t* x;
+    int ldx;
+    // fused RMSNorm of x: inv[m] = 1/sqrt(sum_t ss_in[t][m] / norm_k + eps),
+    // x' = bf16(x * inv * gain).  ss_in == nullptr: x used as is.
+    const float* ss_in;
+    int ss_tiles;
+    const float* gain;
+    float eps;
+    int norm_k;
+    // per-row bookkeeping
+    const int* row_slot;
+    const int* row_pos;
+    // epilogue outputs
+    uint16_t* out;     // EPI_QKV: q [M][q_dim]; EPI_RESID: x_res [M][ldo];
+                       // EPI_SWIGLU: act [M][ldo]; EPI_LOGITS: logits [M][ldo]
+    float* out_f32;    // EPI_F32: [M][ldo]
+    int ldo;
+    float* ss_out;     // EPI_RESID: norm partials [tiles][kMaxRows]
+    const float* bias; // EPI_QKV: [q_dim + 2 kv_dim] (q part pre-scaled) or null
+    // EPI_QKV
+    int head_dim;
+    int q_tiles, k_tiles;  // tile ranges: [0,q) q pairs, [q,q+k) k pairs, rest v
+    int n_kv;
+    const float* rope_cos;  // [cap][hd]
+    const float* rope_sin;
+    uint16_t* kcache;       // this layer's [B][n_kv][cap][hd]
+    uint16_t* vcache;
+    int cap;
+    // EPI_LOGITS
+    int vocab;
+    float* am_val;          // [gridDim][kMaxRows]
+    int* am_idx;
+    unsigned int* am_count;
+    int mode;               // 0 decode, 1 prefill
+    int slot;               // prefill slot
+    int batch;              // decode slots
+    int* pos;               // [batch] positions
+    int* step;              // decode step counter
+    uint32_t* ids_ring;     // [(cap+1)][batch]
+    uint32_t* next_id;      // prefill: argmax of the last row
+};
+
+struct AttnArgs {
+    const uint16_t* q;      // [M][q_dim]
+    const uint16_t* kcache; // this layer [B][n_kv][cap][hd]
+    const uint16_t* vcache;
+    uint16_t* out;          // [M][q_dim]
+    float* part_o;          // [M][n_kv][nsplit_max][hpg][hd]
+    float* part_ml;         // [M][n_kv][nsplit_max][hpg][2]
+    unsigned int* count;    // [M][n_kv]
+    const int* row_slot;
+    const int* row_pos;
+    int M, n_kv, hpg, hd, cap, nsplit_max;
+};
+
+struct EmbedArgs {
+    const uint16_t* table;  // [vocab][hidden]
+    int hidden, vocab;
+    uint16_t* x_res;        // [M][hidden]
+    float* ss_out;          // [hidden/16][kMaxRows]
+    int* row_slot;
+    int* row_pos;
+    int mode;               // 0 decode: ids from ids_ring[step], rows = slots
+    int M;
+    const int* pos;
+    const int* step;
+    const uint32_t* ids_ring;
+    const uint32_t* prefill_ids;
+    int slot;
+    int batch;
+};
+
+struct PackArgs {
+    const uint16_t* src;   // row-major [rows][ld]
+    int64_t ld;
+    const int* rowmap;     // [tiles*16] source row per packed row, -1 = zero
+    int tiles, K, kc;
+    float scale;           // != 0: rows with rowmap < scale_rows are bf16(w*scale)
+    int scale_rows;
+    uint8_t* dst;
+};
+
+// Launchers (return cudaError of the launch).  `pdl` sets programmatic
+// stream serialization so the kernel may start before its predecessor ends.
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int grid, bool pdl, cudaStream_t st);
+cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
+cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
+cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);
+cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, int64_t n, cudaStream_t st);
+
+int fp8_quantize_device(const uint16_t* w, int64_t rows, int64_t cols, int fmt, int scaling,
+                        float backoff, uint8_t* codes, float* scales, uint32_t* bias_dev,
+                        cudaStream_t st);
+
+constexpr int kAttnChunk = 64;
+
+}  // namespace reng

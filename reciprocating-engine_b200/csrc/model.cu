@@ -1,0 +1,807 @@
+// The decoder model behind the C ABI: weight upload and packing, the
+// HBM-resident KV cache, the per-step kernel sequence, and the decode step
+// captured once as a CUDA graph and replayed per token with the argmax fed
+// back on the device (the reference's device decode loop,
+// crates/reng-synapse/src/cached.rs:19-38, 752-835; batched.rs:1023-1151).
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "decode.cuh"
+
+using namespace reng;
+
+namespace reng {
+int tp_init(reng_model* m, const uint8_t* id);
+void tp_destroy(reng_model* m);
+cudaError_t tp_allreduce(reng_model* m, float* buf, size_t count, cudaStream_t st);
+cudaError_t launch_tp_residual(reng_model* m, const float* part, int M, bool pdl, cudaStream_t st);
+int gemv_blocks_per_sm(int epi, int nwarp);
+}  // namespace reng
+
+struct LayerDev {
+    uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+    float *g1 = nullptr, *g2 = nullptr, *bqkv = nullptr;
+};
+
+struct reng_model {
+    reng_model_desc d{};
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    int sms = 148;
+    // shape (local to this tensor-parallel rank)
+    int hidden = 0, inter = 0, L = 0, nh = 0, nkv = 0, hd = 0, vocab = 0, B = 0, cap = 0;
+    int q_dim = 0, kv_dim = 0, hpg = 0;
+    int qkv_tiles = 0, q_tiles = 0, k_tiles = 0, o_tiles = 0, gu_tiles = 0, d_tiles = 0, lm_tiles = 0;
+    std::vector<LayerDev> layers;
+    uint8_t* lm = nullptr;
+    uint16_t* embed = nullptr;
+    float *final_gamma = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    uint16_t *kcache = nullptr, *vcache = nullptr;
+    size_t layer_kv = 0;  // elements per layer
+    // work buffers
+    uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+    float* ss = nullptr;
+    float* part = nullptr;  // tensor-parallel f32 partials [kMaxRows][hidden]
+    int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
+    uint32_t *ids_ring = nullptr, *prefill_ids = nullptr, *next_id = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned int* attn_count = nullptr;
+    float* am_val = nullptr;
+    int* am_idx = nullptr;
+    unsigned int* am_count = nullptr;
+    int nsplit_max = 0;
+    int lm_grid = 0;
+    // launch shapes per matrix
+    int nw_qkv = 4, nw_o = 8, nw_gu = 4, nw_d = 8, nw_lm = 4;
+    int gr_qkv = 0, gr_o = 0, gr_gu = 0, gr_d = 0;
+    cudaGraphExec_t graph = nullptr;
+    int kernels_per_step = 0;
+    std::vector<int> host_pos;
+    uint32_t* pinned = nullptr;  // small pinned staging
+    size_t bytes = 0;
+    std::vector<void*> allocs;
+    reng_step_times times{};
+    // tensor parallel
+    void* nccl = nullptr;
+    int rank = 0, world = 1;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(reng_model* m, T** p, size_t count) {
+    size_t b = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc((void**)p, b);
+    if (e != cudaSuccess)
+        return fail(RENG_E_NOMEM, "cudaMalloc(" + std::to_string(b) + "): " + cudaGetErrorString(e));
+    m->allocs.push_back(*p);
+    m->bytes += b;
+    return RENG_OK;
+}
+
+#define TRY(x)                  \
+    do {                        \
+        int rc__ = (x);         \
+        if (rc__) return rc__;  \
+    } while (0)
+
+#define CU(x)                                                                               \
+    do {                                                                                    \
+        cudaError_t e__ = (x);                                                              \
+        if (e__ != cudaSuccess)                                                             \
+            return fail(RENG_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e__));     \
+    } while (0)
+
+// Copy `rows` x `cols` bf16 (source pitch `ld` elements) into `dst` (dense).
+int copy_matrix(uint16_t* dst, const uint16_t* src, int64_t rows, int64_t cols, int64_t ld,
+                int mem, cudaStream_t st) {
+    cudaMemcpyKind k = mem == RENG_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    if (ld == cols) {
+        CU(cudaMemcpyAsync(dst, src, (size_t)rows * cols * 2, k, st));
+    } else {
+        CU(cudaMemcpy2DAsync(dst, (size_t)cols * 2, src, (size_t)ld * 2, (size_t)cols * 2, (size_t)rows, k, st));
+    }
+    return RENG_OK;
+}
+
+int pack(reng_model* m, uint8_t** out, const uint16_t* staged, const std::vector<int>& rowmap,
+         int K, float scale, int scale_rows, int* tiles_out) {
+    const int tiles = (int)(rowmap.size() / kTileRows);
+    const int kc = (K + kChunkK - 1) / kChunkK;
+    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytes));
+    int* dmap = nullptr;
+    CU(cudaMallocAsync((void**)&dmap, rowmap.size() * sizeof(int), m->st));
+    CU(cudaMemcpyAsync(dmap, rowmap.data(), rowmap.size() * sizeof(int), cudaMemcpyHostToDevice, m->st));
+    PackArgs a{};
+    a.src = staged;
+    a.ld = K;
+    a.rowmap = dmap;
+    a.tiles = tiles;
+    a.K = K;
+    a.kc = kc;
+    a.scale = scale;
+    a.scale_rows = scale_rows;
+    a.dst = *out;
+    CU(launch_pack(a, m->st));
+    CU(cudaFreeAsync(dmap, m->st));
+    CU(cudaStreamSynchronize(m->st));  // rowmap lives on the host stack
+    if (tiles_out) *tiles_out = tiles;
+    return RENG_OK;
+}
+
+std::vector<int> plain_map(int rows) {
+    int tiles = (rows + kTileRows - 1) / kTileRows;
+    std::vector<int> v((size_t)tiles * kTileRows, -1);
+    for (int r = 0; r < rows; r++) v[r] = r;
+    return v;
+}
+
+int upload_f32(reng_model* m, float** out, const float* src, size_t n, int mem) {
+    TRY(dalloc(m, out, n));
+    if (src == nullptr) {
+        CU(cudaMemsetAsync(*out, 0, n * 4, m->st));
+        return RENG_OK;
+    }
+    CU(cudaMemcpyAsync(*out, src, n * 4,
+                       mem == RENG_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, m->st));
+    return RENG_OK;
+}
+
+void pick_shape(reng_model* m, int epi, int tiles, int kc, int* nwarp, int* grid) {
+    int nw = tiles < 2 * m->sms ? 8 : 4;
+    while (nw > 1 && nw > kc) nw >>= 1;
+    if (nw < 4) nw = 4;
+    int per_sm = gemv_blocks_per_sm(epi, nw);
+    if (per_sm < 1) per_sm = 1;
+    *nwarp = nw;
+    *grid = std::min(tiles, m->sms * per_sm);
+}
+
+int validate(const reng_model_desc* d) {
+    RENG_CHECK_ARG(d != nullptr, "reng_model_create: desc is NULL");
+    RENG_CHECK_ARG(d->hidden > 0 && d->inter > 0 && d->n_layers > 0 && d->n_heads > 0 &&
+                       d->n_kv_heads > 0 && d->head_dim > 0 && d->vocab > 0,
+                   "reng_model_create: every dimension must be positive");
+    RENG_CHECK_ARG(d->batch >= 1 && d->capacity >= 1, "reng_model_create: batch and capacity must be >= 1");
+    RENG_CHECK_ARG(d->tp_world >= 1 && d->tp_rank >= 0 && d->tp_rank < d->tp_world,
+                   "reng_model_create: bad tensor-parallel rank/world");
+    RENG_CHECK_ARG(d->n_heads % d->n_kv_heads == 0, "reng_model_create: n_heads % n_kv_heads != 0");
+    RENG_CHECK_ARG(d->n_heads % d->tp_world == 0 && d->n_kv_heads % d->tp_world == 0 &&
+                       d->inter % d->tp_world == 0,
+                   "reng_model_create: heads " + std::to_string(d->n_heads) + " / kv heads " +
+                       std::to_string(d->n_kv_heads) + " / intermediate " + std::to_string(d->inter) +
+                       " are not divisible by " + std::to_string(d->tp_world));
+    RENG_CHECK_ARG(d->hidden % 16 == 0, "reng_model_create: hidden must be a multiple of 16");
+    RENG_CHECK_ARG(d->head_dim % 16 == 0 && d->head_dim <= 128,
+                   "reng_model_create: head_dim must be a multiple of 16 and <= 128");
+    RENG_CHECK_ARG(d->n_heads / d->n_kv_heads <= 8, "reng_model_create: more than 8 query heads per KV head");
+    RENG_CHECK_ARG((d->inter / d->tp_world) % 8 == 0, "reng_model_create: intermediate per rank must be a multiple of 8");
+    RENG_CHECK_ARG(d->weights == RENG_WEIGHTS_BF16 || d->weights == RENG_WEIGHTS_FP8_E4M3,
+                   "reng_model_create: unknown weight format");
+    RENG_CHECK_ARG(std::isfinite(d->eps) && d->eps >= 0.f && std::isfinite(d->attn_scale),
+                   "reng_model_create: eps / attn_scale not finite");
+    RENG_CHECK_ARG((int64_t)d->capacity <= (int64_t)kAttnChunk * 128,
+                   "reng_model_create: capacity above " + std::to_string(kAttnChunk * 128));
+    if (d->batch > kMaxRows)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) +
+                                            " above " + std::to_string(kMaxRows) + " is not built yet");
+    if (d->weights != RENG_WEIGHTS_BF16)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: fp8 weights are not wired yet");
+    return RENG_OK;
+}
+
+// Launch helpers, one per kernel of the step (all on stream `st`).
+int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
+    EmbedArgs e{};
+    e.table = m->embed;
+    e.hidden = m->hidden;
+    e.vocab = m->vocab;
+    e.x_res = m->x_res;
+    e.ss_out = m->ss;
+    e.row_slot = m->row_slot;
+    e.row_pos = m->row_pos;
+    e.mode = mode;
+    e.M = M;
+    e.pos = m->pos;
+    e.step = m->step;
+    e.ids_ring = m->ids_ring;
+    e.prefill_ids = m->prefill_ids;
+    e.slot = slot;
+    e.batch = m->B;
+    CU(launch_embed(e, true, st));
+    return RENG_OK;
+}
+
+GemvArgs norm_args(reng_model* m, int M, const float* gain) {
+    GemvArgs g{};
+    g.M = M;
+    g.row_slot = m->row_slot;
+    g.row_pos = m->row_pos;
+    g.eps = m->d.eps;
+    g.K = m->hidden;
+    g.kc = (m->hidden + kChunkK - 1) / kChunkK;
+    g.x = m->x_res;
+    g.ldx = m->hidden;
+    g.ss_in = m->ss;
+    g.ss_tiles = m->hidden / kTileRows;
+    g.gain = gain;
+    g.norm_k = m->hidden;
+    return g;
+}
+
+int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    const LayerDev& w = m->layers[l];
+    GemvArgs g = norm_args(m, M, w.g1);
+    g.w = w.wqkv;
+    g.tiles = m->qkv_tiles;
+    g.out = m->qbuf;
+    g.ldo = m->q_dim;
+    g.bias = w.bqkv;
+    g.head_dim = m->hd;
+    g.q_tiles = m->q_tiles;
+    g.k_tiles = m->k_tiles;
+    g.n_kv = m->nkv;
+    g.rope_cos = m->rope_cos;
+    g.rope_sin = m->rope_sin;
+    g.kcache = m->kcache + (size_t)l * m->layer_kv;
+    g.vcache = m->vcache + (size_t)l * m->layer_kv;
+    g.cap = m->cap;
+    CU(launch_gemv(g, EPI_QKV, m->nw_qkv, m->gr_qkv, true, st));
+    return RENG_OK;
+}
+
+int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    AttnArgs at{};
+    at.q = m->qbuf;
+    at.kcache = m->kcache + (size_t)l * m->layer_kv;
+    at.vcache = m->vcache + (size_t)l * m->layer_kv;
+    at.out = m->attn;
+    at.part_o = m->part_o;
+    at.part_ml = m->part_ml;
+    at.count = m->attn_count;
+    at.row_slot = m->row_slot;
+    at.row_pos = m->row_pos;
+    at.M = M;
+    at.n_kv = m->nkv;
+    at.hpg = m->hpg;
+    at.hd = m->hd;
+    at.cap = m->cap;
+    at.nsplit_max = m->nsplit_max;
+    CU(launch_attn(at, kAttnChunk, true, st));
+    return RENG_OK;
+}
+
+// o_proj (which == 0) or down_proj (which == 1) with the residual add; under
+// tensor parallelism the f32 partial, the all-reduce and the residual kernel.
+int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* extra) {
+    const LayerDev& w = m->layers[l];
+    GemvArgs o{};
+    o.M = M;
+    o.w = which == 0 ? w.wo : w.wd;
+    o.tiles = which == 0 ? m->o_tiles : m->d_tiles;
+    o.K = which == 0 ? m->q_dim : m->inter;
+    o.kc = (o.K + kChunkK - 1) / kChunkK;
+    o.x = which == 0 ? m->attn : m->act;
+    o.ldx = o.K;
+    o.out = m->x_res;
+    o.ldo = m->hidden;
+    o.ss_out = m->ss;
+    o.out_f32 = m->part;
+    const int nw = which == 0 ? m->nw_o : m->nw_d, gr = which == 0 ? m->gr_o : m->gr_d;
+    if (m->world > 1) {
+        CU(launch_gemv(o, EPI_F32, nw, gr, true, st));
+        CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, st));
+        CU(launch_tp_residual(m, m->part, M, false, st));
+        if (extra) *extra += 2;
+    } else {
+        CU(launch_gemv(o, EPI_RESID, nw, gr, true, st));
+    }
+    return RENG_OK;
+}
+
+int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    const LayerDev& w = m->layers[l];
+    GemvArgs u = norm_args(m, M, w.g2);
+    u.w = w.wgu;
+    u.tiles = m->gu_tiles;
+    u.out = m->act;
+    u.ldo = m->inter;
+    CU(launch_gemv(u, EPI_SWIGLU, m->nw_gu, m->gr_gu, true, st));
+    return RENG_OK;
+}
+
+int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
+    GemvArgs h = norm_args(m, M, m->final_gamma);
+    h.w = m->lm;
+    h.tiles = m->lm_tiles;
+    h.out = m->logits;
+    h.ldo = m->vocab;
+    h.vocab = m->vocab;
+    h.am_val = m->am_val;
+    h.am_idx = m->am_idx;
+    h.am_count = m->am_count;
+    h.mode = mode;
+    h.slot = slot;
+    h.batch = m->B;
+    h.pos = m->pos;
+    h.step = m->step;
+    h.ids_ring = m->ids_ring;
+    h.next_id = m->next_id;
+    CU(launch_gemv(h, EPI_LOGITS, m->nw_lm, m->lm_grid, true, st));
+    return RENG_OK;
+}
+
+// The kernels of one step.  mode 0: decode over the B slots (rows = slots,
+// ids from the device ring).  mode 1: prefill of `M` ids of slot `slot`
+// starting at the device position of that slot; `head` runs the LM head.
+int enqueue_step(reng_model* m, int mode, int M, int slot, bool head, cudaStream_t st, int* nk) {
+    int kernels = 0;
+    TRY(k_embed_launch(m, mode, M, slot, st));
+    kernels++;
+    for (int l = 0; l < m->L; l++) {
+        TRY(k_qkv_launch(m, l, M, st));
+        TRY(k_attn_launch(m, l, M, st));
+        TRY(k_proj_launch(m, l, M, 0, st, &kernels));
+        TRY(k_gateup_launch(m, l, M, st));
+        TRY(k_proj_launch(m, l, M, 1, st, &kernels));
+        kernels += 5;
+    }
+    if (head) {
+        TRY(k_head_launch(m, mode, M, slot, st));
+        kernels++;
+    }
+    if (nk) *nk = kernels;
+    return RENG_OK;
+}
+
+int build_graph(reng_model* m) {
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, 0, m->B, 0, true, m->st, &m->kernels_per_step);
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return RENG_OK;
+}
+
+void free_model(reng_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->dev);
+    if (m->st) cudaStreamSynchronize(m->st);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    tp_destroy(m);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->pinned) cudaFreeHost(m->pinned);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+int create(const reng_model_desc* d, const reng_layer_weights* layers, const uint16_t* embed,
+           const uint16_t* lm_head, const float* final_gamma, const float* rope_sin,
+           const float* rope_cos, int mem, reng_model* m) {
+    m->d = *d;
+    m->d.nccl_id = nullptr;
+    m->dev = d->device;
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+    m->sms = num_sms(m->dev);
+    m->rank = d->tp_rank;
+    m->world = d->tp_world;
+    const int W = m->world, R = m->rank;
+    m->hidden = d->hidden;
+    m->L = d->n_layers;
+    m->hd = d->head_dim;
+    m->vocab = d->vocab;
+    m->B = d->batch;
+    m->cap = d->capacity;
+    m->nh = d->n_heads / W;
+    m->nkv = d->n_kv_heads / W;
+    m->inter = d->inter / W;
+    m->hpg = m->nh / m->nkv;
+    m->q_dim = m->nh * m->hd;
+    m->kv_dim = m->nkv * m->hd;
+    const int q_full = d->n_heads * m->hd, kv_full = d->n_kv_heads * m->hd;
+    const int H = m->hidden;
+    if (W > 1) TRY(tp_init(m, d->nccl_id));
+
+    // ---- tile maps ----
+    const int ppt = m->hd / 16;  // pair tiles per head
+    std::vector<int> qkv_map;
+    for (int h = 0; h < m->nh; h++)
+        for (int j = 0; j < ppt; j++) {
+            for (int i = 0; i < 8; i++) qkv_map.push_back(h * m->hd + j * 8 + i);
+            for (int i = 0; i < 8; i++) qkv_map.push_back(h * m->hd + j * 8 + i + m->hd / 2);
+        }
+    m->q_tiles = m->nh * ppt;
+    for (int h = 0; h < m->nkv; h++)
+        for (int j = 0; j < ppt; j++) {
+            for (int i = 0; i < 8; i++) qkv_map.push_back(m->q_dim + h * m->hd + j * 8 + i);
+            for (int i = 0; i < 8; i++) qkv_map.push_back(m->q_dim + h * m->hd + j * 8 + i + m->hd / 2);
+        }
+    m->k_tiles = m->nkv * ppt;
+    for (int r = 0; r < m->kv_dim; r++) qkv_map.push_back(m->q_dim + m->kv_dim + r);
+    std::vector<int> gu_map;
+    for (int t = 0; t < m->inter / 8; t++) {
+        for (int i = 0; i < 8; i++) gu_map.push_back(t * 8 + i);
+        for (int i = 0; i < 8; i++) gu_map.push_back(m->inter + t * 8 + i);
+    }
+
+    // ---- staging buffer large enough for any one matrix ----
+    size_t stage_el = std::max<size_t>((size_t)(m->q_dim + 2 * m->kv_dim) * H, (size_t)2 * m->inter * H);
+    stage_el = std::max<size_t>(stage_el, (size_t)m->vocab * H);
+    uint16_t* stage = nullptr;
+    CU(cudaMalloc((void**)&stage, stage_el * 2));
+    struct StageFree {
+        uint16_t* p;
+        ~StageFree() { cudaFree(p); }
+    } sf{stage};
+
+    m->layers.resize(m->L);
+    std::vector<float> bias((size_t)m->q_dim + 2 * m->kv_dim);
+    for (int l = 0; l < m->L; l++) {
+        const reng_layer_weights& s = layers[l];
+        RENG_CHECK_ARG(s.wq && s.wk && s.wv && s.wo && s.wg && s.wu && s.wd && s.g1 && s.g2,
+                       "reng_model_create: layer " + std::to_string(l) + " has a NULL weight");
+        if (d->has_qkv_bias)
+            RENG_CHECK_ARG(s.bq && s.bk && s.bv, "reng_model_create: layer " + std::to_string(l) + " lacks a bias");
+        LayerDev& w = m->layers[l];
+        // q, k, v row blocks of this rank
+        TRY(copy_matrix(stage, s.wq + (size_t)R * m->q_dim * H, m->q_dim, H, H, mem, m->st));
+        TRY(copy_matrix(stage + (size_t)m->q_dim * H, s.wk + (size_t)R * m->kv_dim * H, m->kv_dim, H, H, mem, m->st));
+        TRY(copy_matrix(stage + (size_t)(m->q_dim + m->kv_dim) * H, s.wv + (size_t)R * m->kv_dim * H, m->kv_dim, H, H,
+                        mem, m->st));
+        TRY(pack(m, &w.wqkv, stage, qkv_map, H, d->attn_scale, m->q_dim, &m->qkv_tiles));
+        // o_proj column window
+        TRY(copy_matrix(stage, s.wo + (size_t)R * m->q_dim, H, m->q_dim, q_full, mem, m->st));
+        TRY(pack(m, &w.wo, stage, plain_map(H), m->q_dim, 0.f, 0, &m->o_tiles));
+        // gate, up row blocks
+        TRY(copy_matrix(stage, s.wg + (size_t)R * m->inter * H, m->inter, H, H, mem, m->st));
+        TRY(copy_matrix(stage + (size_t)m->inter * H, s.wu + (size_t)R * m->inter * H, m->inter, H, H, mem, m->st));
+        TRY(pack(m, &w.wgu, stage, gu_map, H, 0.f, 0, &m->gu_tiles));
+        // down column window
+        TRY(copy_matrix(stage, s.wd + (size_t)R * m->inter, H, m->inter, d->inter, mem, m->st));
+        TRY(pack(m, &w.wd, stage, plain_map(H), m->inter, 0.f, 0, &m->d_tiles));
+        TRY(upload_f32(m, &w.g1, s.g1, H, mem));
+        TRY(upload_f32(m, &w.g2, s.g2, H, mem));
+        if (d->has_qkv_bias) {
+            // q bias carries the attention scale (model.rs:2993-3002), in f32
+            std::vector<float> hb((size_t)q_full + 2 * kv_full);
+            auto fetch = [&](float* dst, const float* src, size_t n) -> int {
+                if (mem == RENG_MEM_HOST) memcpy(dst, src, n * 4);
+                else CU(cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost));
+                return RENG_OK;
+            };
+            TRY(fetch(hb.data(), s.bq, q_full));
+            TRY(fetch(hb.data() + q_full, s.bk, kv_full));
+            TRY(fetch(hb.data() + q_full + kv_full, s.bv, kv_full));
+            for (int i = 0; i < m->q_dim; i++) bias[i] = hb[(size_t)R * m->q_dim + i] * d->attn_scale;
+            for (int i = 0; i < m->kv_dim; i++) bias[m->q_dim + i] = hb[q_full + (size_t)R * m->kv_dim + i];
+            for (int i = 0; i < m->kv_dim; i++)
+                bias[m->q_dim + m->kv_dim + i] = hb[q_full + kv_full + (size_t)R * m->kv_dim + i];
+            TRY(upload_f32(m, &w.bqkv, bias.data(), bias.size(), RENG_MEM_HOST));
+            CU(cudaStreamSynchronize(m->st));
+        }
+    }
+    // LM head (replicated) and the embedding table
+    RENG_CHECK_ARG(embed && lm_head && final_gamma && rope_sin && rope_cos, "reng_model_create: NULL table");
+    TRY(copy_matrix(stage, lm_head, m->vocab, H, H, mem, m->st));
+    TRY(pack(m, &m->lm, stage, plain_map(m->vocab), H, 0.f, 0, &m->lm_tiles));
+    TRY(dalloc(m, &m->embed, (size_t)m->vocab * H));
+    TRY(copy_matrix(m->embed, embed, m->vocab, H, H, mem, m->st));
+    TRY(upload_f32(m, &m->final_gamma, final_gamma, H, mem));
+    TRY(upload_f32(m, &m->rope_cos, rope_cos, (size_t)m->cap * m->hd, mem));
+    TRY(upload_f32(m, &m->rope_sin, rope_sin, (size_t)m->cap * m->hd, mem));
+
+    // ---- KV cache and work buffers ----
+    m->layer_kv = (size_t)m->B * m->nkv * m->cap * m->hd;
+    TRY(dalloc(m, &m->kcache, m->layer_kv * m->L));
+    TRY(dalloc(m, &m->vcache, m->layer_kv * m->L));
+    CU(cudaMemsetAsync(m->kcache, 0, m->layer_kv * m->L * 2, m->st));
+    CU(cudaMemsetAsync(m->vcache, 0, m->layer_kv * m->L * 2, m->st));
+    const int MR = kMaxRows;
+    TRY(dalloc(m, &m->x_res, (size_t)MR * H));
+    TRY(dalloc(m, &m->qbuf, (size_t)MR * m->q_dim));
+    TRY(dalloc(m, &m->attn, (size_t)MR * m->q_dim));
+    TRY(dalloc(m, &m->act, (size_t)MR * m->inter));
+    TRY(dalloc(m, &m->logits, (size_t)MR * m->vocab));
+    TRY(dalloc(m, &m->ss, (size_t)(H / kTileRows) * MR));
+    TRY(dalloc(m, &m->part, (size_t)MR * H));
+    TRY(dalloc(m, &m->row_slot, MR));
+    TRY(dalloc(m, &m->row_pos, MR));
+    TRY(dalloc(m, &m->pos, m->B));
+    TRY(dalloc(m, &m->step, 1));
+    TRY(dalloc(m, &m->ids_ring, (size_t)(m->cap + 1) * m->B));
+    TRY(dalloc(m, &m->prefill_ids, MR));
+    TRY(dalloc(m, &m->next_id, 1));
+    m->nsplit_max = (m->cap + kAttnChunk - 1) / kAttnChunk;
+    TRY(dalloc(m, &m->part_o, (size_t)MR * m->nkv * m->nsplit_max * m->hpg * m->hd));
+    TRY(dalloc(m, &m->part_ml, (size_t)MR * m->nkv * m->nsplit_max * m->hpg * 2));
+    TRY(dalloc(m, &m->attn_count, (size_t)MR * m->nkv));
+    CU(cudaMemsetAsync(m->attn_count, 0, (size_t)MR * m->nkv * 4, m->st));
+    CU(cudaMemsetAsync(m->pos, 0, (size_t)m->B * 4, m->st));
+    CU(cudaMemsetAsync(m->step, 0, 4, m->st));
+    CU(cudaMemsetAsync(m->x_res, 0, (size_t)MR * H * 2, m->st));
+    CU(cudaMemsetAsync(m->ss, 0, (size_t)(H / kTileRows) * MR * 4, m->st));
+
+    // launch shapes
+    const int kch = (H + kChunkK - 1) / kChunkK;
+    pick_shape(m, EPI_QKV, m->qkv_tiles, kch, &m->nw_qkv, &m->gr_qkv);
+    pick_shape(m, EPI_RESID, m->o_tiles, (m->q_dim + kChunkK - 1) / kChunkK, &m->nw_o, &m->gr_o);
+    pick_shape(m, EPI_SWIGLU, m->gu_tiles, kch, &m->nw_gu, &m->gr_gu);
+    pick_shape(m, EPI_RESID, m->d_tiles, (m->inter + kChunkK - 1) / kChunkK, &m->nw_d, &m->gr_d);
+    pick_shape(m, EPI_LOGITS, m->lm_tiles, kch, &m->nw_lm, &m->lm_grid);
+    TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * MR));
+    TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
+    TRY(dalloc(m, &m->am_count, 1));
+    CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
+    CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * 64));
+    m->host_pos.assign(m->B, 0);
+    CU(cudaStreamSynchronize(m->st));
+    TRY(build_graph(m));
+    return RENG_OK;
+}
+
+int check_model(const reng_model* m) {
+    RENG_CHECK_ARG(m != nullptr, "model is NULL");
+    return RENG_OK;
+}
+
+int sync_pos(reng_model* m) {
+    for (int b = 0; b < m->B; b++) reinterpret_cast<int*>(m->pinned)[b % 64] = m->host_pos[b];
+    // B <= kMaxRows <= 64
+    CU(cudaMemcpyAsync(m->pos, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    return RENG_OK;
+}
+
+void bf16_to_f32_host(const uint16_t* s, float* d, size_t n) {
+    for (size_t i = 0; i < n; i++) {
+        uint32_t u = (uint32_t)s[i] << 16;
+        memcpy(&d[i], &u, 4);
+    }
+}
+
+}  // namespace
+
+extern "C" int reng_model_create(const reng_model_desc* desc, const reng_layer_weights* layers,
+                                 const uint16_t* embed, const uint16_t* lm_head,
+                                 const float* final_gamma, const float* rope_sin,
+                                 const float* rope_cos, int mem, reng_model** out) {
+    RENG_CHECK_ARG(out != nullptr, "reng_model_create: out is NULL");
+    *out = nullptr;
+    TRY(validate(desc));
+    RENG_CHECK_ARG(layers != nullptr, "reng_model_create: layers is NULL");
+    RENG_CHECK_ARG(mem == RENG_MEM_HOST || mem == RENG_MEM_DEVICE, "reng_model_create: bad mem");
+    if (desc->tp_world > 1) RENG_CHECK_ARG(desc->nccl_id != nullptr, "reng_model_create: tp_world > 1 needs nccl_id");
+    reng_model* m = new (std::nothrow) reng_model();
+    if (!m) return fail(RENG_E_NOMEM, "reng_model_create: host allocation");
+    int rc = create(desc, layers, embed, lm_head, final_gamma, rope_sin, rope_cos, mem, m);
+    if (rc) {
+        std::string msg = reng_last_error();
+        free_model(m);
+        set_error(msg);
+        return rc;
+    }
+    *out = m;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_destroy(reng_model* m) {
+    if (m) free_model(m);
+    return RENG_OK;
+}
+
+extern "C" int reng_model_prefill(reng_model* m, int slot, const uint32_t* ids, int n,
+                                  uint32_t* next_id, float* last_logits, float* all_logits) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(slot >= 0 && slot < m->B, "reng_model_prefill: slot out of range");
+    RENG_CHECK_ARG(ids != nullptr && n >= 1, "reng_model_prefill: empty prompt");
+    RENG_CHECK_ARG((int64_t)m->host_pos[slot] + n <= m->cap,
+                   "reng_model_prefill: " + std::to_string(m->host_pos[slot]) + " + " + std::to_string(n) +
+                       " positions overflow the capacity " + std::to_string(m->cap));
+    for (int i = 0; i < n; i++)
+        RENG_CHECK_ARG(ids[i] < (uint32_t)m->vocab, "reng_model_prefill: token id " + std::to_string(ids[i]) +
+                                                        " out of range");
+    CU(cudaSetDevice(m->dev));
+    std::vector<uint16_t> hl;
+    for (int b0 = 0; b0 < n; b0 += kMaxRows) {
+        const int M = std::min(kMaxRows, n - b0);
+        const bool last = b0 + M == n;
+        memcpy(m->pinned, ids + b0, (size_t)M * 4);
+        CU(cudaMemcpyAsync(m->prefill_ids, m->pinned, (size_t)M * 4, cudaMemcpyHostToDevice, m->st));
+        // positions of this block: pos[slot] on the device is the block base
+        TRY(enqueue_step(m, 1, M, slot, last || all_logits != nullptr, m->st, nullptr));
+        m->host_pos[slot] += M;
+        TRY(sync_pos(m));  // also orders the pinned buffer reuse
+        if (all_logits) {
+            hl.resize((size_t)M * m->vocab);
+            CU(cudaMemcpy(hl.data(), m->logits, hl.size() * 2, cudaMemcpyDeviceToHost));
+            bf16_to_f32_host(hl.data(), all_logits + (size_t)b0 * m->vocab, hl.size());
+        }
+        if (last) {
+            if (last_logits) {
+                hl.resize((size_t)m->vocab);
+                CU(cudaMemcpy(hl.data(), m->logits + (size_t)(M - 1) * m->vocab, (size_t)m->vocab * 2,
+                              cudaMemcpyDeviceToHost));
+                bf16_to_f32_host(hl.data(), last_logits, m->vocab);
+            }
+            uint32_t id = 0;
+            CU(cudaMemcpy(&id, m->next_id, 4, cudaMemcpyDeviceToHost));
+            if (next_id) *next_id = id;
+        }
+    }
+    return RENG_OK;
+}
+
+static int decode_common(reng_model* m, int n, cudaStream_t st) {
+    for (int i = 0; i < n; i++) CU(cudaGraphLaunch(m->graph, st));
+    return RENG_OK;
+}
+
+extern "C" int reng_model_decode_device(reng_model* m, const uint32_t* seeds, int n, uint32_t* ids_out,
+                                        void* stream) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(seeds && ids_out && n >= 1, "reng_model_decode_device: bad arguments");
+    for (int b = 0; b < m->B; b++)
+        RENG_CHECK_ARG((int64_t)m->host_pos[b] + n <= m->cap,
+                       "reng_model_decode_device: slot " + std::to_string(b) + " would overflow the capacity");
+    CU(cudaSetDevice(m->dev));
+    cudaStream_t st = (cudaStream_t)stream;
+    CU(cudaMemcpyAsync(m->ids_ring, seeds, (size_t)m->B * 4, cudaMemcpyDeviceToDevice, st));
+    CU(cudaMemsetAsync(m->step, 0, 4, st));
+    TRY(decode_common(m, n, st));
+    CU(cudaMemcpyAsync(ids_out, m->ids_ring + m->B, (size_t)n * m->B * 4, cudaMemcpyDeviceToDevice, st));
+    for (int b = 0; b < m->B; b++) m->host_pos[b] += n;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_decode(reng_model* m, const uint32_t* seeds, int n, uint32_t* ids_out) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(seeds && ids_out && n >= 1, "reng_model_decode: bad arguments");
+    for (int b = 0; b < m->B; b++) {
+        RENG_CHECK_ARG((int64_t)m->host_pos[b] + n <= m->cap,
+                       "reng_model_decode: slot " + std::to_string(b) + " at " + std::to_string(m->host_pos[b]) +
+                           " + " + std::to_string(n) + " overflows the capacity " + std::to_string(m->cap));
+        RENG_CHECK_ARG(seeds[b] < (uint32_t)m->vocab, "reng_model_decode: seed id out of range");
+    }
+    CU(cudaSetDevice(m->dev));
+    cudaEvent_t ev[4];
+    for (auto& e : ev) CU(cudaEventCreate(&e));
+    CU(cudaEventRecord(ev[0], m->st));
+    memcpy(m->pinned, seeds, (size_t)m->B * 4);
+    CU(cudaMemcpyAsync(m->ids_ring, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
+    CU(cudaMemsetAsync(m->step, 0, 4, m->st));
+    CU(cudaEventRecord(ev[1], m->st));
+    TRY(decode_common(m, n, m->st));
+    CU(cudaEventRecord(ev[2], m->st));
+    CU(cudaMemcpyAsync(ids_out, m->ids_ring + m->B, (size_t)n * m->B * 4, cudaMemcpyDeviceToHost, m->st));
+    CU(cudaEventRecord(ev[3], m->st));
+    CU(cudaEventSynchronize(ev[3]));
+    cudaEventElapsedTime(&m->times.upload_ms, ev[0], ev[1]);
+    cudaEventElapsedTime(&m->times.device_ms, ev[1], ev[2]);
+    cudaEventElapsedTime(&m->times.readback_ms, ev[2], ev[3]);
+    m->times.steps = n;
+    m->times.kernels_per_step = m->kernels_per_step;
+    for (auto& e : ev) cudaEventDestroy(e);
+    for (int b = 0; b < m->B; b++) m->host_pos[b] += n;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_step_logits(reng_model* m, const uint32_t* ids, float* logits, uint32_t* next_ids) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(ids != nullptr, "reng_model_step_logits: ids is NULL");
+    for (int b = 0; b < m->B; b++) {
+        RENG_CHECK_ARG((int64_t)m->host_pos[b] + 1 <= m->cap, "reng_model_step_logits: capacity overflow");
+        RENG_CHECK_ARG(ids[b] < (uint32_t)m->vocab, "reng_model_step_logits: id out of range");
+    }
+    CU(cudaSetDevice(m->dev));
+    memcpy(m->pinned, ids, (size_t)m->B * 4);
+    CU(cudaMemcpyAsync(m->ids_ring, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
+    CU(cudaMemsetAsync(m->step, 0, 4, m->st));
+    CU(cudaGraphLaunch(m->graph, m->st));
+    std::vector<uint16_t> hl((size_t)m->B * m->vocab);
+    CU(cudaMemcpyAsync(hl.data(), m->logits, hl.size() * 2, cudaMemcpyDeviceToHost, m->st));
+    CU(cudaMemcpyAsync(m->pinned, m->ids_ring + m->B, (size_t)m->B * 4, cudaMemcpyDeviceToHost, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    if (logits) bf16_to_f32_host(hl.data(), logits, hl.size());
+    if (next_ids) memcpy(next_ids, m->pinned, (size_t)m->B * 4);
+    for (int b = 0; b < m->B; b++) m->host_pos[b] += 1;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_reset(reng_model* m, int slot) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(slot >= -1 && slot < m->B, "reng_model_reset: slot out of range");
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamSynchronize(m->st));
+    for (int b = 0; b < m->B; b++)
+        if (slot < 0 || slot == b) m->host_pos[b] = 0;
+    return sync_pos(m);
+}
+
+extern "C" int reng_model_position(const reng_model* m, int slot, int* pos) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(pos && slot >= 0 && slot < m->B, "reng_model_position: bad slot");
+    *pos = m->host_pos[slot];
+    return RENG_OK;
+}
+
+extern "C" int reng_model_device_bytes(const reng_model* m, uint64_t* bytes) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(bytes != nullptr, "reng_model_device_bytes: NULL");
+    *bytes = m->bytes;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_last_times(const reng_model* m, reng_step_times* t) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(t != nullptr, "reng_model_last_times: NULL");
+    *t = m->times;
+    return RENG_OK;
+}
+
+extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(ms_out != nullptr && iters >= 1, "reng_model_time_kernels: bad arguments");
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamSynchronize(m->st));
+    const int M = m->B;
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    CU(cudaEventCreate(&e1));
+    // rows as the decode step sees them
+    TRY(k_embed_launch(m, 0, M, 0, m->st));
+    for (int kind = 0; kind < RENG_KERNEL_KINDS; kind++) {
+        // one untimed pass, then `iters` launches cycling over the layers
+        for (int pass = 0; pass < 2; pass++) {
+            const int n = pass == 0 ? std::min(iters, m->L) : iters;
+            if (pass == 1) CU(cudaEventRecord(e0, m->st));
+            for (int i = 0; i < n; i++) {
+                const int l = i % m->L;
+                switch (kind) {
+                    case 0: TRY(k_qkv_launch(m, l, M, m->st)); break;
+                    case 1: TRY(k_attn_launch(m, l, M, m->st)); break;
+                    case 2: TRY(k_proj_launch(m, l, M, 0, m->st, nullptr)); break;
+                    case 3: TRY(k_gateup_launch(m, l, M, m->st)); break;
+                    case 4: TRY(k_proj_launch(m, l, M, 1, m->st, nullptr)); break;
+                    default: TRY(k_head_launch(m, 1, M, 0, m->st)); break;
+                }
+            }
+            if (pass == 1) CU(cudaEventRecord(e1, m->st));
+        }
+        CU(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        CU(cudaEventElapsedTime(&ms, e0, e1));
+        ms_out[kind] = ms / (float)iters;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    // the QKV launches rewrote the cache row at each slot's last position
+    // with other activations: the cached prefix is no longer valid
+    for (int b = 0; b < m->B; b++) m->host_pos[b] = 0;
+    return sync_pos(m);
+}
+
+// ------------------------------------------------------------------- TP --
+// Tensor parallelism is wired through NCCL in tp.cu; these accessors let it
+// reach the model's buffers without exposing the struct.
+namespace reng {
+void* tp_handle(reng_model* m) { return m->nccl; }
+void tp_set_handle(reng_model* m, void* h) { m->nccl = h; }
+int tp_rank_of(reng_model* m) { return m->rank; }
+int tp_world_of(reng_model* m) { return m->world; }
+int tp_device_of(reng_model* m) { return m->dev; }
+uint16_t* tp_x_res(reng_model* m) { return m->x_res; }
+float* tp_ss(reng_model* m) { return m->ss; }
+int tp_hidden(reng_model* m) { return m->hidden; }
+}  // namespace reng

@@ -1,0 +1,205 @@
+"""`LlamaConfig`: the config.json contract of the reference's loader.
+
+Mirrors crates/reng-model/src/lib.rs: `LlamaConfig` (lib.rs:84-193),
+`from_json` (lib.rs:488-618), `n_kv_heads` / `head_dim` / `rotary_dim` /
+`q_dim` / `attention_scale` (lib.rs:666-705) and `shard` (lib.rs:725-742),
+for the decoder families this path runs (Llama, Qwen2 with q/k/v biases).
+A multimodal Gemma-3 style config parses through its `text_config`.
+"""
+import copy
+import json
+import math
+import os
+from dataclasses import dataclass, field
+from typing import Optional
+
+
+@dataclass
+class RopeScaling:
+    rope_type: Optional[str] = None
+    factor: Optional[float] = None
+    low_freq_factor: Optional[float] = None
+    high_freq_factor: Optional[float] = None
+    original_max_position_embeddings: Optional[int] = None
+    max_position_embeddings: Optional[int] = None
+    attention_factor: Optional[float] = None
+    beta_fast: Optional[float] = None
+    beta_slow: Optional[float] = None
+    mscale: Optional[float] = None
+    mscale_all_dim: Optional[float] = None
+    truncate: Optional[bool] = None
+    short_factor: Optional[list] = None
+    long_factor: Optional[list] = None
+
+
+@dataclass
+class LlamaConfig:
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    vocab_size: int
+    num_key_value_heads: Optional[int] = None
+    head_dim_: Optional[int] = None
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    rope_scaling: Optional[RopeScaling] = None
+    partial_rotary_factor: Optional[float] = None
+    tie_word_embeddings: bool = False
+    attention_bias: bool = False
+    model_type: Optional[str] = None
+    max_position_embeddings: Optional[int] = None
+    hidden_act: str = "silu"
+    rope_local_base_freq: Optional[float] = None
+    raw: dict = field(default_factory=dict, repr=False)
+
+    # ----------------------------------------------------------- parsing --
+    @staticmethod
+    def from_dict(d):
+        d = dict(d)
+        if "text_config" in d and isinstance(d["text_config"], dict):
+            # multimodal wrapper (Gemma-3): the text half carries the decoder
+            t = dict(d["text_config"])
+            for k in ("rope_theta", "rope_scaling", "max_position_embeddings"):
+                if k not in t and k in d:
+                    t[k] = d[k]
+            d = t
+        rp = d.get("rope_parameters")
+        rope_theta = d.get("rope_theta")
+        rs = d.get("rope_scaling")
+        if isinstance(rp, dict):  # transformers 5 "rope_parameters" form
+            rope_theta = rope_theta if rope_theta is not None else rp.get("rope_theta")
+            if rs is None and rp.get("rope_type", "default") != "default":
+                rs = rp
+        scaling = None
+        if isinstance(rs, dict):
+            rtype = rs.get("rope_type", rs.get("type"))
+            scaling = RopeScaling(
+                rope_type=rtype, factor=rs.get("factor"),
+                low_freq_factor=rs.get("low_freq_factor"),
+                high_freq_factor=rs.get("high_freq_factor"),
+                original_max_position_embeddings=rs.get(
+                    "original_max_position_embeddings", d.get("original_max_position_embeddings")),
+                max_position_embeddings=d.get("max_position_embeddings"),
+                attention_factor=rs.get("attention_factor"),
+                beta_fast=rs.get("beta_fast"), beta_slow=rs.get("beta_slow"),
+                mscale=rs.get("mscale"), mscale_all_dim=rs.get("mscale_all_dim"),
+                truncate=rs.get("truncate"),
+                short_factor=rs.get("short_factor"), long_factor=rs.get("long_factor"))
+        for k in ("hidden_size", "intermediate_size", "num_hidden_layers",
+                  "num_attention_heads", "vocab_size"):
+            if k not in d:
+                raise ValueError("config.json: missing %s" % k)
+        mt = d.get("model_type")
+        return LlamaConfig(
+            hidden_size=int(d["hidden_size"]), intermediate_size=int(d["intermediate_size"]),
+            num_hidden_layers=int(d["num_hidden_layers"]),
+            num_attention_heads=int(d["num_attention_heads"]), vocab_size=int(d["vocab_size"]),
+            num_key_value_heads=d.get("num_key_value_heads"), head_dim_=d.get("head_dim"),
+            rms_norm_eps=float(d.get("rms_norm_eps", 1e-6)),
+            rope_theta=float(rope_theta if rope_theta is not None else 10000.0),
+            rope_scaling=scaling, partial_rotary_factor=d.get("partial_rotary_factor"),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
+            attention_bias=bool(d.get("attention_bias", mt == "qwen2")),
+            model_type=mt, max_position_embeddings=d.get("max_position_embeddings"),
+            hidden_act=d.get("hidden_act", "silu"),
+            rope_local_base_freq=d.get("rope_local_base_freq"), raw=d)
+
+    @staticmethod
+    def from_json(text):
+        return LlamaConfig.from_dict(json.loads(text))
+
+    @staticmethod
+    def load(model_dir):
+        with open(os.path.join(model_dir, "config.json")) as f:
+            return LlamaConfig.from_json(f.read())
+
+    def to_dict(self):
+        d = dict(self.raw) if self.raw else {}
+        d.update({
+            "hidden_size": self.hidden_size, "intermediate_size": self.intermediate_size,
+            "num_hidden_layers": self.num_hidden_layers,
+            "num_attention_heads": self.num_attention_heads, "vocab_size": self.vocab_size,
+            "num_key_value_heads": self.n_kv_heads(), "head_dim": self.head_dim(),
+            "rms_norm_eps": self.rms_norm_eps, "rope_theta": self.rope_theta,
+            "tie_word_embeddings": self.tie_word_embeddings, "hidden_act": self.hidden_act,
+            "model_type": self.model_type or "llama",
+        })
+        if self.model_type == "qwen2" or self.attention_bias:
+            d["attention_bias"] = self.attention_bias
+        return d
+
+    # ---------------------------------------------------------- geometry --
+    def n_kv_heads(self):
+        return int(self.num_key_value_heads or self.num_attention_heads)
+
+    def head_dim(self):
+        return int(self.head_dim_ or self.hidden_size // self.num_attention_heads)
+
+    def rotary_dim(self):
+        hd = self.head_dim()
+        if self.partial_rotary_factor is None:
+            return hd
+        return int(hd * float(self.partial_rotary_factor))
+
+    def q_dim(self):
+        return self.num_attention_heads * self.head_dim()
+
+    def attention_scale(self):
+        """1/sqrt(head_dim) (lib.rs:701-705), as an f32."""
+        import numpy as np
+        return float(np.float32(1.0) / np.sqrt(np.float32(self.head_dim())))
+
+    def has_bias(self):
+        return bool(self.attention_bias)
+
+    def shard(self, rank, world):
+        """The config of one tensor-parallel shard (lib.rs:725-742)."""
+        if not (world >= 1 and 0 <= rank < world):
+            raise ValueError("rank %d of %d" % (rank, world))
+        nkv = self.n_kv_heads()
+        if (self.num_attention_heads % world or nkv % world or self.intermediate_size % world):
+            raise ValueError("heads %d / kv heads %d / intermediate %d are not divisible by %d"
+                             % (self.num_attention_heads, nkv, self.intermediate_size, world))
+        c = copy.deepcopy(self)
+        c.head_dim_ = self.head_dim()
+        c.num_attention_heads = self.num_attention_heads // world
+        c.num_key_value_heads = nkv // world
+        c.intermediate_size = self.intermediate_size // world
+        return c
+
+    def active_params(self):
+        """Params touched per token: attention + MLP per layer + LM head
+        (reng-ceiling active_params, crates/reng-ceiling/src/lib.rs:184-207)."""
+        h, hd = self.hidden_size, self.head_dim()
+        attn = h * self.q_dim() * 2 + h * self.n_kv_heads() * hd * 2
+        mlp = 3 * h * self.intermediate_size
+        return self.num_hidden_layers * (attn + mlp) + h * self.vocab_size
+
+    def kv_bytes_per_token(self, kv_bytes=2):
+        return 2 * self.n_kv_heads() * self.head_dim() * self.num_hidden_layers * kv_bytes
+
+
+# The BASELINE shapes (random-init weights; synthetic config.json contents).
+def smollm2_135m():
+    return LlamaConfig(hidden_size=576, intermediate_size=1536, num_hidden_layers=30,
+                       num_attention_heads=9, num_key_value_heads=3, head_dim_=64,
+                       vocab_size=49152, rms_norm_eps=1e-5, rope_theta=100000.0,
+                       tie_word_embeddings=True, model_type="llama")
+
+
+def llama31_8b():
+    return LlamaConfig(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim_=128,
+                       vocab_size=128256, rms_norm_eps=1e-5, rope_theta=500000.0,
+                       tie_word_embeddings=False, model_type="llama")
+
+
+def qwen25_32b():
+    return LlamaConfig(hidden_size=5120, intermediate_size=27648, num_hidden_layers=64,
+                       num_attention_heads=40, num_key_value_heads=8, head_dim_=128,
+                       vocab_size=152064, rms_norm_eps=1e-6, rope_theta=1000000.0,
+                       tie_word_embeddings=False, attention_bias=True, model_type="qwen2")
+
+
+SHAPES = {"smollm2-135m": smollm2_135m, "llama-3.1-8b": llama31_8b, "qwen2.5-32b": qwen25_32b}

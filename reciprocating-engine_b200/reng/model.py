@@ -1,0 +1,294 @@
+"""The reference's generator API over libreng_cuda.
+
+`Engine` owns one `reng_model` (the C ABI object that replaces
+reng_synapse::CachedModel / BatchedModel / tp::TpModel).  `Generator`,
+`BatchedGenerator` and `TpGenerator` mirror reng-model's generators
+(crates/reng-model/src/lib.rs:2807-3355) method for method: `feed`,
+`feed_all`, `feed_id`, `generate`, `reset`, `position`, `prefill`,
+`prefill_id`, `step`, `step_ids`, `batch`.  Where the reference panics
+(empty input, cache overflow) these raise ValueError; device failures raise
+reng._lib.RengError.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import _lib
+from .rope import rope_caches_for
+from .weights import MATS
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    return x.data_ptr()
+
+
+def _is_device(w):
+    x = w["embed"]
+    return not isinstance(x, np.ndarray)
+
+
+def fp8_switch(value, flag=False):
+    """RENG_FP8 / --fp8 grammar of reng-model (lib.rs:1693-1782): unset/""/"0"/
+    "off" -> None; "1"/"on"/"e4m3" -> (E4M3, pcs); "<fmt>:<scheme>" otherwise.
+    A bad value raises ValueError, never a silent bf16 run."""
+    from .fp8 import Fp8Format, Scaling
+    if value is None:
+        return ("e4m3", "pcs") if flag else None
+    v = value.strip().lower()
+    if v in ("", "0", "off", "false", "no"):
+        return ("e4m3", "pcs") if flag else None
+    if v in ("1", "on", "true", "yes"):
+        return ("e4m3", "pcs")
+    fmt, _, sch = v.partition(":")
+    if Fp8Format.from_name(fmt) is None:
+        raise ValueError("RENG_FP8=%r: unknown format %r" % (value, fmt))
+    if sch and Scaling.from_name(sch) is None:
+        raise ValueError("RENG_FP8=%r: unknown scheme %r" % (value, sch))
+    return (Fp8Format.from_name(fmt).short_name,
+            Scaling.from_name(sch).short_name if sch else "pcs")
+
+
+class Engine:
+    def __init__(self, cfg, w, batch=1, capacity=1024, device=0, tp_rank=0, tp_world=1,
+                 nccl_id=None, fp8=None):
+        self.cfg = cfg
+        self.batch = batch
+        self.capacity = capacity
+        self.vocab = cfg.vocab_size
+        dev = _is_device(w)
+        mem = _lib.RENG_MEM_DEVICE if dev else _lib.RENG_MEM_HOST
+        sin, cos = rope_caches_for(cfg, capacity)
+        keep = [sin, cos]
+        if dev:
+            import torch
+            d = w["embed"].device
+            sin_t = torch.from_numpy(sin).to(d)
+            cos_t = torch.from_numpy(cos).to(d)
+            keep += [sin_t, cos_t]
+            sin_p, cos_p = sin_t.data_ptr(), cos_t.data_ptr()
+            torch.cuda.synchronize(d)
+        else:
+            sin_p, cos_p = sin.ctypes.data, cos.ctypes.data
+        n = len(w["layers"])
+        arr = (_lib.LayerWeights * n)()
+        for i, lw in enumerate(w["layers"]):
+            for k in MATS + ("g1", "g2", "bq", "bk", "bv"):
+                x = lw.get(k)
+                if x is None:
+                    continue
+                if isinstance(x, np.ndarray):
+                    x = np.ascontiguousarray(x)
+                    keep.append(x)
+                setattr(arr[i], k, _ptr(x))
+        desc = _lib.ModelDesc()
+        desc.hidden = cfg.hidden_size
+        desc.inter = cfg.intermediate_size
+        desc.n_layers = n
+        desc.n_heads = cfg.num_attention_heads
+        desc.n_kv_heads = cfg.n_kv_heads()
+        desc.head_dim = cfg.head_dim()
+        desc.vocab = cfg.vocab_size
+        desc.eps = cfg.rms_norm_eps
+        desc.attn_scale = cfg.attention_scale()
+        desc.has_qkv_bias = 1 if cfg.has_bias() else 0
+        desc.weights = _lib.RENG_WEIGHTS_BF16 if fp8 is None else _lib.RENG_WEIGHTS_FP8_E4M3
+        desc.batch = batch
+        desc.capacity = capacity
+        desc.tp_rank = tp_rank
+        desc.tp_world = tp_world
+        desc.device = device
+        idbuf = None
+        if nccl_id is not None:
+            idbuf = (C.c_uint8 * 128).from_buffer_copy(bytes(nccl_id))
+            desc.nccl_id = C.addressof(idbuf)
+        fg = w["final_gamma"]
+        if isinstance(fg, np.ndarray):
+            fg = np.ascontiguousarray(fg, np.float32)
+            keep.append(fg)
+        emb = w["embed"]
+        lm = w["lm_head"]
+        if isinstance(emb, np.ndarray):
+            emb = np.ascontiguousarray(emb)
+            lm = np.ascontiguousarray(lm)
+            keep += [emb, lm]
+        h = C.c_void_p()
+        _lib.call("reng_model_create", C.byref(desc), arr, _ptr(emb), _ptr(lm), _ptr(fg),
+                  sin_p, cos_p, mem, C.byref(h))
+        self.h = h
+        del keep
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            _lib.lib().reng_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # ------------------------------------------------------------- calls --
+    def prefill(self, slot, ids, last_logits=False, all_logits=False):
+        ids = np.ascontiguousarray(ids, np.uint32).reshape(-1)
+        if ids.size == 0:
+            raise ValueError("empty prompt")
+        nxt = C.c_uint32(0)
+        ll = np.empty(self.vocab, np.float32) if last_logits else None
+        al = np.empty((ids.size, self.vocab), np.float32) if all_logits else None
+        _lib.call("reng_model_prefill", self.h, slot, ids.ctypes.data, ids.size, C.byref(nxt),
+                  _ptr(ll), _ptr(al))
+        return int(nxt.value), ll, al
+
+    def decode(self, seeds, n):
+        seeds = np.ascontiguousarray(seeds, np.uint32).reshape(-1)
+        if seeds.size != self.batch:
+            raise ValueError("%d seeds for batch %d" % (seeds.size, self.batch))
+        if n < 1:
+            raise ValueError("n must be >= 1")
+        out = np.empty((n, self.batch), np.uint32)
+        _lib.call("reng_model_decode", self.h, seeds.ctypes.data, n, out.ctypes.data)
+        return out
+
+    def decode_device(self, seeds_dev, n, out_dev, stream):
+        _lib.call("reng_model_decode_device", self.h, seeds_dev.data_ptr(), n, out_dev.data_ptr(),
+                  stream)
+
+    def step_logits(self, ids):
+        ids = np.ascontiguousarray(ids, np.uint32).reshape(-1)
+        if ids.size != self.batch:
+            raise ValueError("%d ids for batch %d" % (ids.size, self.batch))
+        logits = np.empty((self.batch, self.vocab), np.float32)
+        nxt = np.empty(self.batch, np.uint32)
+        _lib.call("reng_model_step_logits", self.h, ids.ctypes.data, logits.ctypes.data,
+                  nxt.ctypes.data)
+        return logits, nxt
+
+    def reset(self, slot=-1):
+        _lib.call("reng_model_reset", self.h, slot)
+
+    def position(self, slot=0):
+        p = C.c_int(0)
+        _lib.call("reng_model_position", self.h, slot, C.byref(p))
+        return p.value
+
+    def device_bytes(self):
+        b = C.c_uint64(0)
+        _lib.call("reng_model_device_bytes", self.h, C.byref(b))
+        return b.value
+
+    def time_kernels(self, iters=64):
+        """Mean ms per launch of each kernel kind (qkv, attn, o, gate_up,
+        down, lm_head); resets every slot afterwards."""
+        out = np.zeros(6, np.float32)
+        _lib.call("reng_model_time_kernels", self.h, iters, out.ctypes.data)
+        return dict(zip(("qkv", "attn", "o_proj", "gate_up", "down", "lm_head"),
+                        (float(x) for x in out)))
+
+    def last_times(self):
+        t = _lib.StepTimes()
+        _lib.call("reng_model_last_times", self.h, C.byref(t))
+        return t
+
+
+class Generator:
+    """One sequence (reng-model Generator, lib.rs:2807-3023)."""
+
+    def __init__(self, w, cfg, rows=256, decode_rows=1, capacity=1024, device=0):
+        self.cfg = cfg
+        self.rows = rows
+        self.engine = Engine(cfg, w, batch=1, capacity=capacity, device=device)
+
+    def position(self):
+        return self.engine.position(0)
+
+    def device_loop(self):
+        return True
+
+    def reset(self):
+        self.engine.reset(0)
+
+    def feed(self, ids):
+        """Append ids and return the last position's logits."""
+        return self.engine.prefill(0, ids, last_logits=True)[1]
+
+    def feed_all(self, ids):
+        return self.engine.prefill(0, ids, all_logits=True)[2]
+
+    def feed_id(self, ids):
+        if os.environ.get("RENG_HOST_ARGMAX", "0") not in ("", "0"):
+            return int(argmax_rows(self.feed(ids)[None, :])[0])
+        return self.engine.prefill(0, ids)[0]
+
+    def generate(self, seed, n):
+        if n < 1:
+            raise ValueError("n must be >= 1")
+        return [int(x) for x in self.engine.decode([seed], n)[:, 0]]
+
+    def close(self):
+        self.engine.close()
+
+
+class BatchedGenerator:
+    """B sequences in lockstep (reng-model BatchedGenerator, lib.rs:3031-3237)."""
+
+    def __init__(self, w, cfg, batch, rows=256, capacity=1024, device=0):
+        self.cfg = cfg
+        self.engine = Engine(cfg, w, batch=batch, capacity=capacity, device=device)
+
+    def batch(self):
+        return self.engine.batch
+
+    def device_loop(self):
+        return True
+
+    def position(self, b):
+        return self.engine.position(b)
+
+    def reset(self, b=-1):
+        self.engine.reset(b)
+
+    def prefill(self, b, ids):
+        return self.engine.prefill(b, ids, last_logits=True)[1]
+
+    def prefill_id(self, b, ids):
+        return self.engine.prefill(b, ids)[0]
+
+    def step(self, ids):
+        return self.engine.step_logits(ids)[0]
+
+    def step_ids(self, ids):
+        return [int(x) for x in self.engine.step_logits(ids)[1]]
+
+    def generate(self, seeds, n):
+        return [int(x) for x in self.engine.decode(seeds, n).reshape(-1)]
+
+    def close(self):
+        self.engine.close()
+
+
+def argmax_rows(logits):
+    """First index of the max of each row (reng-model argmax_rows, lib.rs:2309-2321)."""
+    logits = np.asarray(logits, np.float32)
+    out = []
+    for row in logits:
+        best, bi = -np.inf, 0
+        # vectorised form of the strict '>' scan: the first maximal index,
+        # NaN never selected
+        r = np.where(np.isnan(row), -np.inf, row)
+        m = r.max()
+        if m > best:
+            bi = int(np.flatnonzero(r == m)[0])
+        out.append(bi)
+    return out

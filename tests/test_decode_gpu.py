@@ -1,0 +1,230 @@
+"""GPU parity of the decode path against the f32 host forward (the oracle).
+
+The reference's bar (crates/reng-synapse/src/bin/cache_test.rs:437,
+batch_test.rs:487; tools/oracle method): per-position logits within rel-L2
+0.05 of the f32 forward, last-position cosine >= 0.999, and greedy ids equal
+to the oracle's except at bf16 near-ties, where the engine's pick must be
+within MARGIN logits of the oracle's best (generate.rs:30, default 0.5).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.999
+REL_L2_MAX = 0.05
+MARGIN = 0.5
+
+
+def small_cfg(bias=False, **kw):
+    from reng.config import LlamaConfig
+    d = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+             num_key_value_heads=2, head_dim_=64, vocab_size=1024, rms_norm_eps=1e-5,
+             rope_theta=10000.0, tie_word_embeddings=False, attention_bias=bias,
+             model_type="qwen2" if bias else "llama")
+    d.update(kw)
+    return LlamaConfig(**d)
+
+
+def oracle_for(cfg, w):
+    import oracle
+    from reng.weights import to_host
+    h = to_host(w)
+    c = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_layers=len(h["layers"]),
+             n_heads=cfg.num_attention_heads, n_kv_heads=cfg.n_kv_heads(), head_dim=cfg.head_dim(),
+             vocab=cfg.vocab_size, eps=cfg.rms_norm_eps, attn_scale=cfg.attention_scale(),
+             has_bias=int(cfg.has_bias()))
+    return oracle.Model(c, h["layers"], h["final_gamma"], h["lm_head"], h["embed"])
+
+
+def cosine(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def rel_l2(got, want):
+    return float(np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want))
+
+
+def check_rows(got, want, what):
+    for i in range(want.shape[0]):
+        assert rel_l2(got[i], want[i]) < REL_L2_MAX, (what, i, rel_l2(got[i], want[i]))
+        assert cosine(got[i], want[i]) >= COS_MIN, (what, i, cosine(got[i], want[i]))
+        gi = int(np.argmax(got[i]))
+        wi = int(np.argmax(want[i]))
+        if gi != wi:
+            assert want[i][wi] - want[i][gi] < MARGIN, (what, i, gi, wi)
+
+
+def check_greedy(ids_engine, oracle_logits):
+    """ids_engine[t] is the engine's pick after position t; oracle_logits[t]
+    the f32 logits there (teacher-forced on the engine's own ids)."""
+    ties = 0
+    for t, e in enumerate(ids_engine):
+        best = int(np.argmax(oracle_logits[t]))
+        if best != e:
+            gap = oracle_logits[t][best] - oracle_logits[t][e]
+            assert gap < MARGIN, (t, e, best, gap)
+            ties += 1
+    return ties
+
+
+@pytest.fixture(scope="module")
+def lib(reng_lib):
+    return reng_lib
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_prefill_logits_match_the_oracle(lib, bias):
+    from reng.model import Generator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg(bias=bias)
+    w = random_weights(cfg, seed=7)
+    ids = prompt_ids(21, cfg.vocab_size, seed=3)
+    g = Generator(w, cfg, capacity=128)
+    got = g.feed_all(ids)
+    sin, cos = rope_caches_for(cfg, 128)
+    want = oracle_for(cfg, w).forward(ids, sin, cos)
+    check_rows(got, want, "prefill")
+    assert g.position() == ids.size
+    g.close()
+
+
+def test_greedy_decode_matches_the_teacher_forced_oracle(lib):
+    from reng.model import Generator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg()
+    w = random_weights(cfg, seed=11)
+    prompt = prompt_ids(17, cfg.vocab_size, seed=5)
+    g = Generator(w, cfg, capacity=128)
+    nxt = g.feed_id(prompt)
+    out = g.generate(nxt, 24)
+    assert g.position() == prompt.size + 24
+    seq = np.concatenate([prompt, [nxt], out[:-1]]).astype(np.uint32)
+    sin, cos = rope_caches_for(cfg, 128)
+    want = oracle_for(cfg, w).forward(seq, sin, cos, logits_from=prompt.size - 1)
+    check_greedy([nxt] + out, want)
+    # reset replays the same ids (the stale cache is masked by the position)
+    g.reset()
+    assert g.position() == 0
+    assert g.feed_id(prompt) == nxt
+    assert g.generate(nxt, 24) == out
+    g.close()
+
+
+def test_decode_step_logits_match(lib):
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg(bias=True)
+    w = random_weights(cfg, seed=2)
+    prompt = prompt_ids(9, cfg.vocab_size, seed=1)
+    e = Engine(cfg, w, batch=1, capacity=64)
+    nxt, _, _ = e.prefill(0, prompt)
+    seq = list(prompt) + [nxt]
+    got = []
+    for _ in range(6):
+        lg, n = e.step_logits([seq[-1]])
+        got.append(lg[0])
+        seq.append(int(n[0]))
+    sin, cos = rope_caches_for(cfg, 64)
+    want = oracle_for(cfg, w).forward(np.array(seq[:-1], np.uint32), sin, cos,
+                                      logits_from=prompt.size)
+    check_rows(np.array(got), want, "step")
+    e.close()
+
+
+@pytest.mark.parametrize("batch", [2, 8])
+def test_batched_decode_with_staggered_prompts(lib, batch):
+    from reng.model import BatchedGenerator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg()
+    w = random_weights(cfg, seed=4)
+    cap = 96
+    g = BatchedGenerator(w, cfg, batch, capacity=cap)
+    prompts = [prompt_ids(12 - (b % 3), cfg.vocab_size, seed=100 + b) for b in range(batch)]
+    seeds = [g.prefill_id(b, prompts[b]) for b in range(batch)]
+    n = 10
+    ids = np.array(g.generate(seeds, n)).reshape(n, batch)
+    sin, cos = rope_caches_for(cfg, cap)
+    orc = oracle_for(cfg, w)
+    for b in range(batch):
+        assert g.position(b) == prompts[b].size + n
+        seq = np.concatenate([prompts[b], [seeds[b]], ids[:-1, b]]).astype(np.uint32)
+        want = orc.forward(seq, sin, cos, logits_from=prompts[b].size - 1)
+        check_greedy([seeds[b]] + list(ids[:, b]), want)
+    g.close()
+
+
+def test_smollm2_shape_full_depth(lib):
+    from reng.config import smollm2_135m
+    from reng.model import Generator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = smollm2_135m()
+    w = random_weights(cfg, seed=0)
+    prompt = prompt_ids(32, cfg.vocab_size, seed=0)
+    g = Generator(w, cfg, capacity=256)
+    last = g.feed(prompt)
+    nxt = int(np.argmax(last))
+    out = g.generate(nxt, 16)
+    seq = np.concatenate([prompt, [nxt], out[:-1]]).astype(np.uint32)
+    sin, cos = rope_caches_for(cfg, 256)
+    want = oracle_for(cfg, w).forward(seq, sin, cos, logits_from=prompt.size - 1)
+    assert cosine(last, want[0]) >= COS_MIN
+    check_greedy([nxt] + out, want)
+    g.close()
+
+
+def test_llama8b_shape_two_layers(lib):
+    """The Llama-3.1-8B widths (hidden 4096, GQA 32/8, hd 128, inter 14336,
+    vocab 128256) on a layer-truncated model."""
+    from reng.config import llama31_8b
+    from reng.model import Generator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = llama31_8b()
+    w = random_weights(cfg, seed=1, layers=2)
+    cfg.num_hidden_layers = 2
+    prompt = prompt_ids(12, cfg.vocab_size, seed=9)
+    g = Generator(w, cfg, capacity=128)
+    last = g.feed(prompt)
+    nxt = int(np.argmax(last))
+    out = g.generate(nxt, 6)
+    seq = np.concatenate([prompt, [nxt], out[:-1]]).astype(np.uint32)
+    sin, cos = rope_caches_for(cfg, 128)
+    want = oracle_for(cfg, w).forward(seq, sin, cos, logits_from=prompt.size - 1)
+    assert cosine(last, want[0]) >= COS_MIN
+    assert rel_l2(last, want[0]) < REL_L2_MAX
+    check_greedy([nxt] + out, want)
+    g.close()
+
+
+def test_errors_are_reported_not_aborted(lib):
+    from reng._lib import RengError
+    from reng.model import Engine
+    from reng.weights import random_weights
+    cfg = small_cfg()
+    w = random_weights(cfg, seed=1)
+    e = Engine(cfg, w, batch=1, capacity=16)
+    with pytest.raises(RengError):
+        e.prefill(0, np.arange(17, dtype=np.uint32))       # overflows the capacity
+    with pytest.raises(RengError):
+        e.prefill(0, np.array([cfg.vocab_size], np.uint32))  # id out of range
+    with pytest.raises(RengError):
+        e.prefill(1, np.array([1], np.uint32))              # no such slot
+    e.prefill(0, np.arange(10, dtype=np.uint32))
+    with pytest.raises(RengError):
+        e.decode([1], 7)                                    # 10 + 7 > 16
+    assert e.position(0) == 10
+    e.close()
