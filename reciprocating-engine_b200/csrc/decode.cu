@@ -20,6 +20,7 @@
 //              CTA picks the ids (first index of the max), advances the
 //              positions and the step counter
 #include <algorithm>
+#include <cstdlib>
 
 #include "decode.cuh"
 
@@ -28,22 +29,34 @@ namespace reng {
 // ------------------------------------------------------------------ GEMV --
 
 // The x fragment of lane (g, q) for k-chunk c: row g, k = 32c + 8q .. +8,
-// as 4 u32 of packed bf16, RMS-normalised when the args carry a norm.
-__device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, int K, int c, int g, int q,
-                                            float inv) {
-    uint4 z = make_uint4(0u, 0u, 0u, 0u);
+// as 4 u32 of packed bf16.  From the CTA's shared copy when it was staged,
+// else straight from global memory (rows too long for shared memory; only
+// un-normalised inputs take that path).
+__device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, const uint16_t* xs, int xstride,
+                                            int K, int c, int g, int q) {
     const int k = c * kChunkK + q * 8;
-    if (g >= a.M || k >= K) return z;
-    uint4 v = ldg_nc(a.x + (size_t)g * a.ldx + k);
-    if (a.ss_in == nullptr) return v;
-    const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain + k));
-    const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain + k + 4));
-    uint4 r;
-    r.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
-    r.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
-    r.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
-    r.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
-    return r;
+    if (g >= a.M || k >= K) return make_uint4(0u, 0u, 0u, 0u);
+    if (xs != nullptr) return *reinterpret_cast<const uint4*>(xs + g * xstride + k);
+    return ldg_nc(a.x + (size_t)g * a.ldx + k);
+}
+
+// RMS-normalise the staged x rows in place: x' = bf16(x * inv[m] * gain[k]).
+__device__ __forceinline__ void normalise_x(const GemvArgs& a, uint16_t* xs, int xstride, int K,
+                                            const float* inv_s) {
+    const int nv = K / 8;
+    for (int i = threadIdx.x; i < a.M * nv; i += blockDim.x) {
+        const int m = i / nv, k = (i % nv) * 8;
+        uint4* p = reinterpret_cast<uint4*>(xs + m * xstride + k);
+        uint4 v = *p;
+        const float inv = inv_s[m];
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain + k));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain + k + 4));
+        v.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+        v.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+        v.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+        v.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+        *p = v;
+    }
 }
 
 // Lexicographic argmax step: larger value, then lower index.
@@ -64,200 +77,402 @@ __device__ __forceinline__ void am_reduce_g(float& bv, int& bi) {
     }
 }
 
-template <int EPI, int NWARP>
-__global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a) {
-    const int K = a.K;
-    __shared__ float4 red[NWARP > 1 ? NWARP : 1][32];
-    __shared__ float inv_s[kMaxRows];
-    __shared__ int s_ids[kMaxRows];
-    __shared__ int s_last;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, q = lane & 3;
-    const int kc_per = (a.kc + NWARP - 1) / NWARP;
-    const int c0 = min(a.kc, warp * kc_per), c1 = min(a.kc, c0 + kc_per);
+// Row stride (elements) of the shared x copy: 32 elements of padding put
+// consecutive rows 64 bytes apart, so the fragment loads of a warp hit 32
+// distinct banks.
+__host__ __device__ __forceinline__ int gemv_xstride(int K) { return K + 32; }
 
-    // Independent of the predecessor: pull this warp's first weight range
-    // into L2 while the previous kernel drains.
-    if (lane == 0 && blockIdx.x < a.tiles && c1 > c0) {
-        const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * kBlockBytes;
-        uint32_t bytes = (uint32_t)(c1 - c0) * kBlockBytes;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-    }
-    pdl_wait();
-    pdl_launch();
-
-    if (a.ss_in != nullptr) {
-        for (int m = warp; m < a.M; m += NWARP) {
-            float s = 0.0f;
-            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kMaxRows + m];
-            s = warp_sum(s);
-            if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
+// The epilogue of one 16-row tile on warp 0: acc holds rows {g, g+8} x
+// activation rows {2q, 2q+1}.
+template <int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const float (&acc)[4], int g,
+                                              int q, float (&best_v)[2], int (&best_i)[2]) {
+    // ---- epilogue (warp 0): acc = rows {g, g+8} x cols {2q, 2q+1} ----
+    const int m0 = 2 * q, m1 = 2 * q + 1;
+    if (EPI == EPI_RESID) {
+        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+        float s0 = 0.f, s1 = 0.f;
+        if (m0 < a.M) {
+            uint16_t* o = a.out + (size_t)m0 * a.ldo;
+            float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[0]));
+            float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[2]));
+            o[r0] = f32_to_bf16_bits(x0);
+            o[r1] = f32_to_bf16_bits(x1);
+            s0 = x0 * x0 + x1 * x1;
         }
-        __syncthreads();
-    }
-    const float inv = (a.ss_in != nullptr && g < a.M) ? inv_s[g] : 1.0f;
-
-    float best_v[2] = {-INFINITY, -INFINITY};
-    int best_i[2] = {0, 0};
-
-    constexpr int U = 8;
-    for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
-        const uint8_t* wt = a.w + (size_t)tile * a.kc * kBlockBytes + lane * 16;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c = c0; c < c1; c += U) {
-            uint4 wa[U], wb[U];
+        if (m1 < a.M) {
+            uint16_t* o = a.out + (size_t)m1 * a.ldo;
+            float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[1]));
+            float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[3]));
+            o[r0] = f32_to_bf16_bits(x0);
+            o[r1] = f32_to_bf16_bits(x1);
+            s1 = x0 * x0 + x1 * x1;
+        }
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                if (c + u < c1) {
-                    wa[u] = ldg_stream(wt + (size_t)(c + u) * kBlockBytes);
-                    wb[u] = ldg_stream(wt + (size_t)(c + u) * kBlockBytes + 512);
+        for (int o = 4; o < 32; o <<= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        if (g == 0) {
+            if (m0 < a.M) a.ss_out[tile * kMaxRows + m0] = s0;
+            if (m1 < a.M) a.ss_out[tile * kMaxRows + m1] = s1;
+        }
+    } else if (EPI == EPI_F32) {
+        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+        if (m0 < a.M) {
+            a.out_f32[(size_t)m0 * a.ldo + r0] = acc[0];
+            a.out_f32[(size_t)m0 * a.ldo + r1] = acc[2];
+        }
+        if (m1 < a.M) {
+            a.out_f32[(size_t)m1 * a.ldo + r0] = acc[1];
+            a.out_f32[(size_t)m1 * a.ldo + r1] = acc[3];
+        }
+    } else if (EPI == EPI_SWIGLU) {
+        const int j = tile * 8 + g;
+        if (m0 < a.M) {
+            float gt = acc[0], up = acc[2];
+            a.out[(size_t)m0 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
+        }
+        if (m1 < a.M) {
+            float gt = acc[1], up = acc[3];
+            a.out[(size_t)m1 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
+        }
+    } else if (EPI == EPI_QKV) {
+        const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;  // pair tiles per head
+        const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
+        if (tile < a.q_tiles + a.k_tiles) {
+            const bool is_q = tile < a.q_tiles;
+            const int t = is_q ? tile : tile - a.q_tiles;
+            const int h = t / ppt, d = (t % ppt) * 8 + g, d2 = d + half;
+            const int brow = is_q ? h * hd : q_dim + h * hd;
+            float b1 = a.bias ? a.bias[brow + d] : 0.f, b2 = a.bias ? a.bias[brow + d2] : 0.f;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int m = e ? m1 : m0;
+                if (m >= a.M) continue;
+                const int pos = a.row_pos[m];
+                if (pos >= a.cap) continue;
+                float x1 = (e ? acc[1] : acc[0]) + b1;
+                float x2 = (e ? acc[3] : acc[2]) + b2;
+                const float* cs = a.rope_cos + (size_t)pos * hd;
+                const float* sn = a.rope_sin + (size_t)pos * hd;
+                float y1 = x1 * cs[d] - x2 * sn[d];
+                float y2 = x2 * cs[d2] + x1 * sn[d2];
+                if (is_q) {
+                    uint16_t* o = a.out + (size_t)m * a.ldo + h * hd;
+                    o[d] = f32_to_bf16_bits(y1);
+                    o[d2] = f32_to_bf16_bits(y2);
+                } else {
+                    const int slot = a.row_slot[m];
+                    uint16_t* kc = a.kcache + (((size_t)slot * a.n_kv + h) * a.cap + pos) * hd;
+                    kc[d] = f32_to_bf16_bits(y1);
+                    kc[d2] = f32_to_bf16_bits(y2);
                 }
             }
+        } else {
+            const int vt = tile - a.q_tiles - a.k_tiles;
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                if (c + u < c1) {
-                    uint4 xf = x_fragment(a, K, c + u, g, q, inv);
-                    mma_bf16_16816(acc, wa[u].x, wb[u].x, wa[u].y, wb[u].y, xf.x, xf.y);
-                    mma_bf16_16816(acc, wa[u].z, wb[u].z, wa[u].w, wb[u].w, xf.z, xf.w);
-                }
-            }
-        }
-        if (NWARP > 1) {
-            __syncthreads();
-            red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            __syncthreads();
-            if (warp != 0) continue;
-#pragma unroll
-            for (int w = 1; w < NWARP; w++) {
-                float4 r = red[w][lane];
-                acc[0] += r.x; acc[1] += r.y; acc[2] += r.z; acc[3] += r.w;
-            }
-        }
-        // ---- epilogue (warp 0): acc = rows {g, g+8} x cols {2q, 2q+1} ----
-        const int m0 = 2 * q, m1 = 2 * q + 1;
-        if (EPI == EPI_RESID) {
-            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-            float s0 = 0.f, s1 = 0.f;
-            if (m0 < a.M) {
-                uint16_t* o = a.out + (size_t)m0 * a.ldo;
-                float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[0]));
-                float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[2]));
-                o[r0] = f32_to_bf16_bits(x0);
-                o[r1] = f32_to_bf16_bits(x1);
-                s0 = x0 * x0 + x1 * x1;
-            }
-            if (m1 < a.M) {
-                uint16_t* o = a.out + (size_t)m1 * a.ldo;
-                float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[1]));
-                float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[3]));
-                o[r0] = f32_to_bf16_bits(x0);
-                o[r1] = f32_to_bf16_bits(x1);
-                s1 = x0 * x0 + x1 * x1;
-            }
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-            }
-            if (g == 0) {
-                if (m0 < a.M) a.ss_out[tile * kMaxRows + m0] = s0;
-                if (m1 < a.M) a.ss_out[tile * kMaxRows + m1] = s1;
-            }
-        } else if (EPI == EPI_F32) {
-            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-            if (m0 < a.M) {
-                a.out_f32[(size_t)m0 * a.ldo + r0] = acc[0];
-                a.out_f32[(size_t)m0 * a.ldo + r1] = acc[2];
-            }
-            if (m1 < a.M) {
-                a.out_f32[(size_t)m1 * a.ldo + r0] = acc[1];
-                a.out_f32[(size_t)m1 * a.ldo + r1] = acc[3];
-            }
-        } else if (EPI == EPI_SWIGLU) {
-            const int j = tile * 8 + g;
-            if (m0 < a.M) {
-                float gt = acc[0], up = acc[2];
-                a.out[(size_t)m0 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
-            }
-            if (m1 < a.M) {
-                float gt = acc[1], up = acc[3];
-                a.out[(size_t)m1 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
-            }
-        } else if (EPI == EPI_QKV) {
-            const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;  // pair tiles per head
-            const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
-            if (tile < a.q_tiles + a.k_tiles) {
-                const bool is_q = tile < a.q_tiles;
-                const int t = is_q ? tile : tile - a.q_tiles;
-                const int h = t / ppt, d = (t % ppt) * 8 + g, d2 = d + half;
-                const int brow = is_q ? h * hd : q_dim + h * hd;
-                float b1 = a.bias ? a.bias[brow + d] : 0.f, b2 = a.bias ? a.bias[brow + d2] : 0.f;
+            for (int rr = 0; rr < 2; rr++) {
+                const int r = vt * kTileRows + g + rr * 8;
+                const int h = r / hd, d = r % hd;
+                const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int m = e ? m1 : m0;
                     if (m >= a.M) continue;
                     const int pos = a.row_pos[m];
                     if (pos >= a.cap) continue;
-                    float x1 = (e ? acc[1] : acc[0]) + b1;
-                    float x2 = (e ? acc[3] : acc[2]) + b2;
-                    const float* cs = a.rope_cos + (size_t)pos * hd;
-                    const float* sn = a.rope_sin + (size_t)pos * hd;
-                    float y1 = x1 * cs[d] - x2 * sn[d];
-                    float y2 = x2 * cs[d2] + x1 * sn[d2];
-                    if (is_q) {
-                        uint16_t* o = a.out + (size_t)m * a.ldo + h * hd;
-                        o[d] = f32_to_bf16_bits(y1);
-                        o[d2] = f32_to_bf16_bits(y2);
-                    } else {
-                        const int slot = a.row_slot[m];
-                        uint16_t* kc = a.kcache + (((size_t)slot * a.n_kv + h) * a.cap + pos) * hd;
-                        kc[d] = f32_to_bf16_bits(y1);
-                        kc[d2] = f32_to_bf16_bits(y2);
-                    }
+                    const int slot = a.row_slot[m];
+                    float val = acc[rr * 2 + e] + b;
+                    a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] =
+                        f32_to_bf16_bits(val);
                 }
-            } else {
-                const int vt = tile - a.q_tiles - a.k_tiles;
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int r = vt * kTileRows + g + rr * 8;
-                    const int h = r / hd, d = r % hd;
-                    const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int m = e ? m1 : m0;
-                        if (m >= a.M) continue;
-                        const int pos = a.row_pos[m];
-                        if (pos >= a.cap) continue;
-                        const int slot = a.row_slot[m];
-                        float val = acc[rr * 2 + e] + b;
-                        a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] =
-                            f32_to_bf16_bits(val);
-                    }
-                }
-            }
-        } else if (EPI == EPI_LOGITS) {
-            const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int m = e ? m1 : m0;
-                float bv = -INFINITY;
-                int bi = 0x7fffffff;
-                if (m < a.M) {
-                    if (r0 < a.vocab) {
-                        uint16_t b = f32_to_bf16_bits(acc[e]);
-                        a.out[(size_t)m * a.ldo + r0] = b;
-                        am_take(bv, bi, bf16_bits_to_f32(b), r0);
-                    }
-                    if (r1 < a.vocab) {
-                        uint16_t b = f32_to_bf16_bits(acc[2 + e]);
-                        a.out[(size_t)m * a.ldo + r1] = b;
-                        am_take(bv, bi, bf16_bits_to_f32(b), r1);
-                    }
-                }
-                am_reduce_g(bv, bi);
-                am_take(best_v[e], best_i[e], bv, bi);
             }
         }
+    } else if (EPI == EPI_LOGITS) {
+        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int m = e ? m1 : m0;
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            if (m < a.M) {
+                if (r0 < a.vocab) {
+                    uint16_t b = f32_to_bf16_bits(acc[e]);
+                    a.out[(size_t)m * a.ldo + r0] = b;
+                    am_take(bv, bi, bf16_bits_to_f32(b), r0);
+                }
+                if (r1 < a.vocab) {
+                    uint16_t b = f32_to_bf16_bits(acc[2 + e]);
+                    a.out[(size_t)m * a.ldo + r1] = b;
+                    am_take(bv, bi, bf16_bits_to_f32(b), r1);
+                }
+            }
+            am_reduce_g(bv, bi);
+            am_take(best_v[e], best_i[e], bv, bi);
+        }
+    }
+}
+
+// ---- weight pipelines ----------------------------------------------------
+// Each warp walks a flat sequence of chunks (its k-range of a tile, tile
+// after tile of the CTA) so the stream never restarts at a tile boundary.
+//
+// PIPE_REG: the next chunk (kRegDepth blocks) is loaded into registers while
+// the current one is multiplied.
+// PIPE_TMA: each warp owns a ring of kTmaStages stages of kTmaBlocks
+// contiguous packed blocks in shared memory, filled by one
+// cp.async.bulk (TMA) copy per stage and an mbarrier with the transaction
+// byte count; lane 0 refills a stage as soon as the warp has read it.  The
+// bytes in flight are bounded by shared memory, not registers.  Every
+// mbarrier wait is bounded by a %globaltimer deadline: on expiry the kernel
+// records RENG_E_TIMEOUT in *a.err, stops issuing copies, drains its own
+// copies (again bounded) and finishes without waiting.
+enum { PIPE_REG = 0, PIPE_TMA = 1 };
+constexpr int kRegDepth = 4;
+constexpr int kTmaStages = 4;
+constexpr int kTmaBlocks = 4;
+constexpr int kTmaRing = kTmaStages * kTmaBlocks * kBlockBytes;  // bytes per warp
+constexpr unsigned long long kWaitNs = 2000000000ull;           // 2 s per wait
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false if the deadline passed first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() - t0 > kWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t saddr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(saddr));
+    return r;
+}
+
+template <int PIPE>
+__host__ __device__ constexpr int gemv_ring_bytes() {
+    return PIPE == PIPE_TMA ? kTmaRing : 0;
+}
+
+template <int EPI, int NWARP, int PIPE>
+__global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
+    extern __shared__ __align__(128) uint8_t smem_dyn[];
+    __shared__ float4 red[NWARP > 1 ? NWARP : 1][32];
+    __shared__ float inv_s[kMaxRows];
+    __shared__ int s_ids[kMaxRows];
+    __shared__ int s_last;
+    __shared__ __align__(8) unsigned long long bars[PIPE == PIPE_TMA ? NWARP * kTmaStages : 1];
+    __shared__ __align__(8) unsigned long long xbar;
+    const int K = a.K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int kc_per = (a.kc + NWARP - 1) / NWARP;
+    const int c0 = min(a.kc, warp * kc_per), c1 = min(a.kc, c0 + kc_per);
+    constexpr int CB = PIPE == PIPE_TMA ? kTmaBlocks : kRegDepth;  // blocks per chunk
+    const int nct = max(1, (c1 - c0 + CB - 1) / CB);
+    const int ntile = blockIdx.x < a.tiles ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nchunks = ntile * nct;
+
+    // chunk j -> its first block and block count (0 for an empty k-range)
+    auto chunk_src = [&](int j, int& nb) -> const uint8_t* {
+        const int tile = blockIdx.x + (j / nct) * gridDim.x;
+        const int b0 = c0 + (j % nct) * CB;
+        nb = max(0, min(CB, c1 - b0));
+        return a.w + ((size_t)tile * a.kc + b0) * kBlockBytes;
+    };
+
+    // ---- start the weight stream (independent of the previous kernel) ----
+    uint4 ra[PIPE == PIPE_REG ? kRegDepth : 1], rb[PIPE == PIPE_REG ? kRegDepth : 1];
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem_dyn) + warp * gemv_ring_bytes<PIPE>();
+    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]) + warp * kTmaStages * 8;
+    bool failed = false;
+    int issued = 0;  // lane 0: chunks whose copy was issued
+    int waited = 0;  // chunks whose copy was waited for
+    auto rload = [&](int j) {
+        if (j >= nchunks) return;
+        int nb;
+        const uint8_t* src = chunk_src(j, nb) + lane * 16;
+#pragma unroll
+        for (int b = 0; b < (PIPE == PIPE_REG ? kRegDepth : 1); b++)
+            if (b < nb) {
+                ra[b] = ldg_stream(src + b * kBlockBytes);
+                rb[b] = ldg_stream(src + b * kBlockBytes + 512);
+            }
+    };
+    auto tma_issue = [&](int j) {  // lane 0 only
+        if (j >= nchunks || failed) return;
+        int nb;
+        const uint8_t* src = chunk_src(j, nb);
+        const uint32_t bar = bar0 + (j % kTmaStages) * 8;
+        const uint32_t bytes = (uint32_t)nb * kBlockBytes;
+        mbar_expect_tx(bar, bytes);
+        if (bytes) tma_load_1d(ring + (j % kTmaStages) * (kTmaBlocks * kBlockBytes), src, bytes, bar);
+        issued = j + 1;
+    };
+    const uint32_t xbar_a = (uint32_t)__cvta_generic_to_shared(&xbar);
+    if (threadIdx.x == 0 && use_smem) {
+        mbar_init(xbar_a, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (PIPE == PIPE_TMA) {
+        if (lane == 0) {
+            for (int s2 = 0; s2 < kTmaStages; s2++) mbar_init(bar0 + s2 * 8, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            for (int j = 0; j < kTmaStages; j++) tma_issue(j);
+        }
+        __syncwarp();
+    } else {
+        if (lane == 0 && nchunks > 0 && c1 > c0) {
+            // the rest of this warp's first tile range into L2
+            const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * kBlockBytes;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p),
+                         "r"((uint32_t)(c1 - c0) * kBlockBytes)
+                         : "memory");
+        }
+        rload(0);
+    }
+
+    pdl_wait();
+    pdl_launch();
+
+    // x rows (written by the previous kernel): one bulk copy per row into
+    // shared memory, while the warps reduce the RMS partials
+    const int xstride = gemv_xstride(K);
+    uint16_t* xsm = reinterpret_cast<uint16_t*>(smem_dyn + NWARP * gemv_ring_bytes<PIPE>());
+    if (use_smem) {
+        __syncthreads();  // barrier init visible to every thread before any wait
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(xbar_a, (uint32_t)(a.M * K * 2));
+            for (int m = 0; m < a.M; m++)
+                tma_load_1d((uint32_t)__cvta_generic_to_shared(xsm + m * xstride), a.x + (size_t)m * a.ldx,
+                            (uint32_t)(K * 2), xbar_a);
+        }
+    }
+    if (a.ss_in != nullptr) {
+        for (int m = warp; m < a.M; m += NWARP) {
+            float s = 0.0f;
+#pragma unroll 8
+            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kMaxRows + m];
+            s = warp_sum(s);
+            if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
+        }
+    }
+    const uint16_t* xs = nullptr;
+    if (use_smem) {
+        if (!mbar_wait_bounded(xbar_a, 0)) {
+            failed = true;
+            if (threadIdx.x == 0) atomicExch(a.err, RENG_E_TIMEOUT);
+        }
+        __syncthreads();
+        if (a.ss_in != nullptr) {
+            normalise_x(a, xsm, xstride, K, inv_s);
+            __syncthreads();
+        }
+        xs = xsm;
+    } else if (a.ss_in != nullptr) {
+        __syncthreads();
+    }
+
+    float best_v[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0, 0};
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < nchunks; j++) {
+        const int b0 = c0 + (j % nct) * CB;
+        if (PIPE == PIPE_TMA) {
+            const uint32_t bar = bar0 + (j % kTmaStages) * 8;
+            if (!failed) {
+                if (mbar_wait_bounded(bar, (uint32_t)((j / kTmaStages) & 1))) {
+                    waited = j + 1;
+                } else {
+                    failed = true;
+                    if (lane == 0) atomicExch(a.err, RENG_E_TIMEOUT);
+                }
+            }
+            const uint32_t st = ring + (j % kTmaStages) * (kTmaBlocks * kBlockBytes) + lane * 16;
+#pragma unroll
+            for (int b = 0; b < kTmaBlocks; b++)
+                if (b0 + b < c1) {
+                    const uint4 wa = lds128(st + b * kBlockBytes);
+                    const uint4 wb = lds128(st + b * kBlockBytes + 512);
+                    const uint4 xf = x_fragment(a, xs, xstride, K, b0 + b, g, q);
+                    mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xf.x, xf.y);
+                    mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xf.z, xf.w);
+                }
+            // the stage is read: let the async proxy refill it
+            __syncwarp();
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tma_issue(j + kTmaStages);
+            }
+            __syncwarp();
+        } else {
+            uint4 wa[kRegDepth], wb[kRegDepth];
+#pragma unroll
+            for (int b = 0; b < kRegDepth; b++) {
+                wa[b] = ra[b];
+                wb[b] = rb[b];
+            }
+            rload(j + 1);
+#pragma unroll
+            for (int b = 0; b < kRegDepth; b++)
+                if (b0 + b < c1) {
+                    const uint4 xf = x_fragment(a, xs, xstride, K, b0 + b, g, q);
+                    mma_bf16_16816(acc, wa[b].x, wb[b].x, wa[b].y, wb[b].y, xf.x, xf.y);
+                    mma_bf16_16816(acc, wa[b].z, wb[b].z, wa[b].w, wb[b].w, xf.z, xf.w);
+                }
+        }
+        if ((j % nct) != nct - 1) continue;
+        // ---- a tile is complete: reduce the warps' k-slices on warp 0 ----
+        const int tile = blockIdx.x + (j / nct) * gridDim.x;
+        if (NWARP > 1) {
+            __syncthreads();
+            red[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (warp == 0) {
+#pragma unroll
+                for (int w = 1; w < NWARP; w++) {
+                    float4 r = red[w][lane];
+                    acc[0] += r.x;
+                    acc[1] += r.y;
+                    acc[2] += r.z;
+                    acc[3] += r.w;
+                }
+            }
+        }
+        if (warp == 0) gemv_epilogue<EPI>(a, tile, acc, g, q, best_v, best_i);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+    if (PIPE == PIPE_TMA && failed && lane == 0) {
+        // drain this warp's own copies still in flight before exiting (bounded)
+        for (int jj = waited; jj < issued; jj++)
+            if (!mbar_wait_bounded(bar0 + (jj % kTmaStages) * 8, (uint32_t)((jj / kTmaStages) & 1))) break;
     }
 
     if (EPI == EPI_LOGITS) {
@@ -308,22 +523,79 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a) {
     }
 }
 
-template <int EPI>
-static cudaError_t launch_gemv_t(const GemvArgs& a, int nwarp, int grid, bool pdl, cudaStream_t st) {
+// Shared x copy of a launch: staged when it fits (normalised inputs always).
+static size_t gemv_xbytes(const GemvArgs& a) {
+    size_t b = (size_t)a.M * gemv_xstride(a.K) * 2;
+    const bool need = a.ss_in != nullptr;
+    if (b <= kGemvMaxSmem || need) return b;
+    return 0;
+}
+
+template <int EPI, int NW>
+static cudaError_t prepare_one() {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    return e;
+}
+
+template <int EPI, int NW, int PIPE>
+static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStream_t st, int* grid_out) {
+    const size_t xbytes = gemv_xbytes(a);
+    const size_t smem = (size_t)NW * gemv_ring_bytes<PIPE>() + xbytes;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    int per_sm = 0, dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    sms = num_sms(dev);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<EPI, NW, PIPE>, NW * 32, smem);
+    if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+    int cap = sms * per_sm;
+    if (max_grid > 0 && max_grid < cap) cap = max_grid;
+    // balanced persistent grid: every CTA gets the same number of tiles
+    const int per = (a.tiles + cap - 1) / cap;
+    const int grid = (a.tiles + per - 1) / per;
+    if (grid_out) *grid_out = grid;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(nwarp * 32);
-    cfg.dynamicSmemBytes = 0;
+    cfg.blockDim = dim3(NW * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    switch (nwarp) {
-        case 4: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 4>, a);
-        case 8: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 8>, a);
-        case 16: return cudaLaunchKernelEx(&cfg, k_gemv<EPI, 16>, a);
+    return cudaLaunchKernelEx(&cfg, k_gemv<EPI, NW, PIPE>, a, xbytes > 0 ? 1 : 0);
+}
+
+template <int EPI>
+static cudaError_t prepare_t() {
+    cudaError_t e = prepare_one<EPI, 4>();
+    if (e == cudaSuccess) e = prepare_one<EPI, 8>();
+    return e;
+}
+
+// Allow the large dynamic shared memory of every GEMV instantiation on the
+// current device (must run before a stream capture).
+cudaError_t gemv_prepare() {
+    cudaError_t e = prepare_t<EPI_QKV>();
+    if (e == cudaSuccess) e = prepare_t<EPI_RESID>();
+    if (e == cudaSuccess) e = prepare_t<EPI_SWIGLU>();
+    if (e == cudaSuccess) e = prepare_t<EPI_LOGITS>();
+    if (e == cudaSuccess) e = prepare_t<EPI_F32>();
+    return e;
+}
+
+// shape = warps per CTA (4 or 8) + 100 * pipeline (0 registers, 1 TMA ring)
+template <int EPI>
+static cudaError_t launch_gemv_t(const GemvArgs& a, int shape, int max_grid, bool pdl, cudaStream_t st,
+                                 int* grid_out) {
+    switch (shape) {
+        case 4: return launch_one<EPI, 4, PIPE_REG>(a, max_grid, pdl, st, grid_out);
+        case 8: return launch_one<EPI, 8, PIPE_REG>(a, max_grid, pdl, st, grid_out);
+        case 104: return launch_one<EPI, 4, PIPE_TMA>(a, max_grid, pdl, st, grid_out);
+        case 108: return launch_one<EPI, 8, PIPE_TMA>(a, max_grid, pdl, st, grid_out);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -332,9 +604,8 @@ template <int EPI>
 static int blocks_t(int nwarp) {
     int n = 0;
     cudaError_t e = cudaErrorInvalidValue;
-    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4>, 128, 0);
-    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8>, 256, 0);
-    if (nwarp == 16) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 16>, 512, 0);
+    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4, PIPE_REG>, 128, 0);
+    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8, PIPE_REG>, 256, 0);
     return e == cudaSuccess ? n : 1;
 }
 
@@ -349,13 +620,16 @@ int gemv_blocks_per_sm(int epi, int nwarp) {
     }
 }
 
-cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int grid, bool pdl, cudaStream_t st) {
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int shape, int max_grid, bool pdl, cudaStream_t st,
+                        int* grid_out) {
+    const int nwarp = shape % 100;
+    (void)nwarp;
     switch (epi) {
-        case EPI_QKV: return launch_gemv_t<EPI_QKV>(a, nwarp, grid, pdl, st);
-        case EPI_RESID: return launch_gemv_t<EPI_RESID>(a, nwarp, grid, pdl, st);
-        case EPI_SWIGLU: return launch_gemv_t<EPI_SWIGLU>(a, nwarp, grid, pdl, st);
-        case EPI_LOGITS: return launch_gemv_t<EPI_LOGITS>(a, nwarp, grid, pdl, st);
-        case EPI_F32: return launch_gemv_t<EPI_F32>(a, nwarp, grid, pdl, st);
+        case EPI_QKV: return launch_gemv_t<EPI_QKV>(a, shape, max_grid, pdl, st, grid_out);
+        case EPI_RESID: return launch_gemv_t<EPI_RESID>(a, shape, max_grid, pdl, st, grid_out);
+        case EPI_SWIGLU: return launch_gemv_t<EPI_SWIGLU>(a, shape, max_grid, pdl, st, grid_out);
+        case EPI_LOGITS: return launch_gemv_t<EPI_LOGITS>(a, shape, max_grid, pdl, st, grid_out);
+        case EPI_F32: return launch_gemv_t<EPI_F32>(a, shape, max_grid, pdl, st, grid_out);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -11,6 +11,7 @@ constexpr int kTileRows = 16;
 constexpr int kChunkK = 32;
 constexpr int kBlockBytes = 1024;
 constexpr int kMaxRows = 8;  // activation rows per GEMV launch (mma N)
+constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
 
 enum Epi : int {
     EPI_QKV = 0,     // bias + RoPE, q to a buffer, k/v into the KV cache
@@ -68,6 +69,7 @@ struct GemvArgs {
     int* step;              // decode step counter
     uint32_t* ids_ring;     // [(cap+1)][batch]
     uint32_t* next_id;      // prefill: argmax of the last row
+    int* err;               // device error word (RENG_E_TIMEOUT from a bounded wait)
 };
 
 struct AttnArgs {
@@ -112,7 +114,11 @@ struct PackArgs {
 
 // Launchers (return cudaError of the launch).  `pdl` sets programmatic
 // stream serialization so the kernel may start before its predecessor ends.
-cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int grid, bool pdl, cudaStream_t st);
+// max_grid > 0 caps the persistent grid (else all resident CTAs); the grid
+// actually launched (tiles split evenly over the CTAs) goes to *grid_out.
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int max_grid, bool pdl, cudaStream_t st,
+                        int* grid_out = nullptr);
+cudaError_t gemv_prepare();
 cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
 cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);

@@ -7,6 +7,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -47,6 +48,7 @@ struct reng_model {
     float* ss = nullptr;
     float* part = nullptr;  // tensor-parallel f32 partials [kMaxRows][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
+    int* err = nullptr;  // device error word of the bounded waits
     uint32_t *ids_ring = nullptr, *prefill_ids = nullptr, *next_id = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* attn_count = nullptr;
@@ -55,9 +57,9 @@ struct reng_model {
     unsigned int* am_count = nullptr;
     int nsplit_max = 0;
     int lm_grid = 0;
-    // launch shapes per matrix
-    int nw_qkv = 4, nw_o = 8, nw_gu = 4, nw_d = 8, nw_lm = 4;
-    int gr_qkv = 0, gr_o = 0, gr_gu = 0, gr_d = 0;
+    // GEMV launch shapes per kind (qkv, o, gate/up, down, LM head), for
+    // M <= 2 and M > 2 activation rows
+    int shape[5][2] = {};
     cudaGraphExec_t graph = nullptr;
     int kernels_per_step = 0;
     std::vector<int> host_pos;
@@ -151,14 +153,35 @@ int upload_f32(reng_model* m, float** out, const float* src, size_t n, int mem) 
     return RENG_OK;
 }
 
-void pick_shape(reng_model* m, int epi, int tiles, int kc, int* nwarp, int* grid) {
-    int nw = tiles < 2 * m->sms ? 8 : 4;
-    while (nw > 1 && nw > kc) nw >>= 1;
-    if (nw < 4) nw = 4;
-    int per_sm = gemv_blocks_per_sm(epi, nw);
-    if (per_sm < 1) per_sm = 1;
-    *nwarp = nw;
-    *grid = std::min(tiles, m->sms * per_sm);
+// Launch shape of a GEMV kind (0 qkv, 1 o_proj, 2 gate/up, 3 down, 4 LM
+// head) for few (M <= 2) and many activation rows: warps per CTA (4 or 8)
+// + 100 for the TMA weight ring (else the register pipeline).  Measured on
+// B200 (Llama-8B widths): the TMA ring with 4-warp CTAs streams qkv, gate/up
+// and the LM head fastest at batch 1 and 8-warp CTAs at batch 8; o_proj and
+// down_proj (few tiles, long K) prefer 8-warp register-pipeline CTAs.
+// RENG_GEMV_SHAPES="qkv,o,gu,down,lm" overrides both (a tuning knob).
+void pick_shape(reng_model* m, int kind, int kc, int* shape_small, int* shape_big) {
+    static const int small[5] = {104, 8, 104, 8, 104};
+    static const int big[5] = {108, 8, 108, 8, 108};
+    int ss = small[kind], sb = big[kind];
+    if (kc < 32) {  // short K: 8 warps would leave warps without blocks
+        ss = ss >= 100 ? 104 : 4;
+        sb = sb >= 100 ? 104 : 4;
+    }
+    const char* v = getenv("RENG_GEMV_SHAPES");
+    if (v) {
+        int vals[5] = {0, 0, 0, 0, 0}, n = 0;
+        const char* p = v;
+        while (*p && n < 5) {
+            vals[n++] = atoi(p);
+            while (*p && *p != ',') p++;
+            if (*p == ',') p++;
+        }
+        const int x = kind < n ? vals[kind] : 0;
+        if (x == 4 || x == 8 || x == 104 || x == 108) ss = sb = x;
+    }
+    *shape_small = ss;
+    *shape_big = sb;
 }
 
 int validate(const reng_model_desc* d) {
@@ -216,8 +239,14 @@ int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
     return RENG_OK;
 }
 
-GemvArgs norm_args(reng_model* m, int M, const float* gain) {
+GemvArgs base_args(reng_model* m) {
     GemvArgs g{};
+    g.err = m->err;
+    return g;
+}
+
+GemvArgs norm_args(reng_model* m, int M, const float* gain) {
+    GemvArgs g = base_args(m);
     g.M = M;
     g.row_slot = m->row_slot;
     g.row_pos = m->row_pos;
@@ -250,7 +279,7 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     g.kcache = m->kcache + (size_t)l * m->layer_kv;
     g.vcache = m->vcache + (size_t)l * m->layer_kv;
     g.cap = m->cap;
-    CU(launch_gemv(g, EPI_QKV, m->nw_qkv, m->gr_qkv, true, st));
+    CU(launch_gemv(g, EPI_QKV, m->shape[0][M > 2], 0, true, st));
     return RENG_OK;
 }
 
@@ -279,7 +308,7 @@ int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
 // tensor parallelism the f32 partial, the all-reduce and the residual kernel.
 int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* extra) {
     const LayerDev& w = m->layers[l];
-    GemvArgs o{};
+    GemvArgs o = base_args(m);
     o.M = M;
     o.w = which == 0 ? w.wo : w.wd;
     o.tiles = which == 0 ? m->o_tiles : m->d_tiles;
@@ -291,7 +320,7 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* 
     o.ldo = m->hidden;
     o.ss_out = m->ss;
     o.out_f32 = m->part;
-    const int nw = which == 0 ? m->nw_o : m->nw_d, gr = which == 0 ? m->gr_o : m->gr_d;
+    const int nw = m->shape[which == 0 ? 1 : 3][M > 2], gr = 0;
     if (m->world > 1) {
         CU(launch_gemv(o, EPI_F32, nw, gr, true, st));
         CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, st));
@@ -310,7 +339,7 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
     u.tiles = m->gu_tiles;
     u.out = m->act;
     u.ldo = m->inter;
-    CU(launch_gemv(u, EPI_SWIGLU, m->nw_gu, m->gr_gu, true, st));
+    CU(launch_gemv(u, EPI_SWIGLU, m->shape[2][M > 2], 0, true, st));
     return RENG_OK;
 }
 
@@ -331,7 +360,7 @@ int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
     h.step = m->step;
     h.ids_ring = m->ids_ring;
     h.next_id = m->next_id;
-    CU(launch_gemv(h, EPI_LOGITS, m->nw_lm, m->lm_grid, true, st));
+    CU(launch_gemv(h, EPI_LOGITS, m->shape[4][M > 2], m->lm_grid, true, st));
     return RENG_OK;
 }
 
@@ -395,6 +424,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(cudaSetDevice(m->dev));
     CU(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
     m->sms = num_sms(m->dev);
+    CU(gemv_prepare());
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     const int W = m->world, R = m->rank;
@@ -520,6 +550,8 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->row_pos, MR));
     TRY(dalloc(m, &m->pos, m->B));
     TRY(dalloc(m, &m->step, 1));
+    TRY(dalloc(m, &m->err, 1));
+    CU(cudaMemsetAsync(m->err, 0, 4, m->st));
     TRY(dalloc(m, &m->ids_ring, (size_t)(m->cap + 1) * m->B));
     TRY(dalloc(m, &m->prefill_ids, MR));
     TRY(dalloc(m, &m->next_id, 1));
@@ -535,11 +567,9 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
 
     // launch shapes
     const int kch = (H + kChunkK - 1) / kChunkK;
-    pick_shape(m, EPI_QKV, m->qkv_tiles, kch, &m->nw_qkv, &m->gr_qkv);
-    pick_shape(m, EPI_RESID, m->o_tiles, (m->q_dim + kChunkK - 1) / kChunkK, &m->nw_o, &m->gr_o);
-    pick_shape(m, EPI_SWIGLU, m->gu_tiles, kch, &m->nw_gu, &m->gr_gu);
-    pick_shape(m, EPI_RESID, m->d_tiles, (m->inter + kChunkK - 1) / kChunkK, &m->nw_d, &m->gr_d);
-    pick_shape(m, EPI_LOGITS, m->lm_tiles, kch, &m->nw_lm, &m->lm_grid);
+    const int kcs[5] = {kch, (m->q_dim + kChunkK - 1) / kChunkK, kch, (m->inter + kChunkK - 1) / kChunkK, kch};
+    for (int k = 0; k < 5; k++) pick_shape(m, k, kcs[k], &m->shape[k][0], &m->shape[k][1]);
+    m->lm_grid = m->sms * 32;  // argmax partial slots: an upper bound of the persistent grid
     TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
@@ -561,6 +591,20 @@ int sync_pos(reng_model* m) {
     // B <= kMaxRows <= 64
     CU(cudaMemcpyAsync(m->pos, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
     CU(cudaStreamSynchronize(m->st));
+    return RENG_OK;
+}
+
+// The device error word of the bounded waits: RENG_E_TIMEOUT if a kernel
+// gave up on a wait (its results are then invalid).  Synchronises.
+int check_device_error(reng_model* m) {
+    int* h = reinterpret_cast<int*>(m->pinned) + 63;
+    CU(cudaMemcpyAsync(h, m->err, 4, cudaMemcpyDeviceToHost, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    if (*h != 0) {
+        const int code = *h;
+        CU(cudaMemsetAsync(m->err, 0, 4, m->st));
+        return fail(code, "a kernel of the step gave up on a bounded wait; the results are invalid");
+    }
     return RENG_OK;
 }
 
@@ -640,7 +684,7 @@ extern "C" int reng_model_prefill(reng_model* m, int slot, const uint32_t* ids, 
             if (next_id) *next_id = id;
         }
     }
-    return RENG_OK;
+    return check_device_error(m);
 }
 
 static int decode_common(reng_model* m, int n, cudaStream_t st) {
@@ -694,7 +738,7 @@ extern "C" int reng_model_decode(reng_model* m, const uint32_t* seeds, int n, ui
     m->times.kernels_per_step = m->kernels_per_step;
     for (auto& e : ev) cudaEventDestroy(e);
     for (int b = 0; b < m->B; b++) m->host_pos[b] += n;
-    return RENG_OK;
+    return check_device_error(m);
 }
 
 extern "C" int reng_model_step_logits(reng_model* m, const uint32_t* ids, float* logits, uint32_t* next_ids) {
@@ -716,7 +760,7 @@ extern "C" int reng_model_step_logits(reng_model* m, const uint32_t* ids, float*
     if (logits) bf16_to_f32_host(hl.data(), logits, hl.size());
     if (next_ids) memcpy(next_ids, m->pinned, (size_t)m->B * 4);
     for (int b = 0; b < m->B; b++) m->host_pos[b] += 1;
-    return RENG_OK;
+    return check_device_error(m);
 }
 
 extern "C" int reng_model_reset(reng_model* m, int slot) {
@@ -786,6 +830,7 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
     }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    TRY(check_device_error(m));
     // the QKV launches rewrote the cache row at each slot's last position
     // with other activations: the cached prefix is no longer valid
     for (int b = 0; b < m->B; b++) m->host_pos[b] = 0;

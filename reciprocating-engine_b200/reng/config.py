@@ -14,6 +14,17 @@ from dataclasses import dataclass, field
 from typing import Optional
 
 
+# Gemma3TextConfig's defaults for the keys a multimodal config.json leaves out
+GEMMA3_TEXT_DEFAULTS = {
+    "model_type": "gemma3_text", "vocab_size": 262208, "hidden_size": 2304,
+    "intermediate_size": 9216, "num_hidden_layers": 26, "num_attention_heads": 8,
+    "num_key_value_heads": 4, "head_dim": 256, "hidden_activation": "gelu_pytorch_tanh",
+    "max_position_embeddings": 131072, "rms_norm_eps": 1e-6, "tie_word_embeddings": True,
+    "query_pre_attn_scalar": 256, "sliding_window": 4096, "sliding_window_pattern": 6,
+    "rope_theta": 1000000.0, "rope_local_base_freq": 10000.0,
+}
+
+
 @dataclass
 class RopeScaling:
     rope_type: Optional[str] = None
@@ -56,13 +67,16 @@ class LlamaConfig:
     # ----------------------------------------------------------- parsing --
     @staticmethod
     def from_dict(d):
+        """from_json's rules (lib.rs:488-618): a multimodal Gemma-3 config
+        flattens to its text_config completed with Gemma3TextConfig's
+        defaults; rope_scaling gets the top-level lengths; Phi-3's legacy
+        "su"/"yarn" types mean longrope."""
         d = dict(d)
-        if "text_config" in d and isinstance(d["text_config"], dict):
-            # multimodal wrapper (Gemma-3): the text half carries the decoder
-            t = dict(d["text_config"])
-            for k in ("rope_theta", "rope_scaling", "max_position_embeddings"):
-                if k not in t and k in d:
-                    t[k] = d[k]
+        if d.get("model_type") == "gemma3":
+            if not isinstance(d.get("text_config"), dict):
+                raise ValueError("config.json: gemma3 without text_config")
+            t = dict(GEMMA3_TEXT_DEFAULTS)
+            t.update(d["text_config"])
             d = t
         rp = d.get("rope_parameters")
         rope_theta = d.get("rope_theta")
@@ -74,13 +88,17 @@ class LlamaConfig:
         scaling = None
         if isinstance(rs, dict):
             rtype = rs.get("rope_type", rs.get("type"))
+            if d.get("model_type") == "phi3" and rtype in ("su", "yarn"):
+                rtype = "longrope"
+            max_pos = d.get("max_position_embeddings")
+            orig = d.get("original_max_position_embeddings")
+            if orig is None:
+                orig = rs.get("original_max_position_embeddings", max_pos)
             scaling = RopeScaling(
                 rope_type=rtype, factor=rs.get("factor"),
                 low_freq_factor=rs.get("low_freq_factor"),
                 high_freq_factor=rs.get("high_freq_factor"),
-                original_max_position_embeddings=rs.get(
-                    "original_max_position_embeddings", d.get("original_max_position_embeddings")),
-                max_position_embeddings=d.get("max_position_embeddings"),
+                original_max_position_embeddings=orig, max_position_embeddings=max_pos,
                 attention_factor=rs.get("attention_factor"),
                 beta_fast=rs.get("beta_fast"), beta_slow=rs.get("beta_slow"),
                 mscale=rs.get("mscale"), mscale_all_dim=rs.get("mscale_all_dim"),
@@ -91,7 +109,7 @@ class LlamaConfig:
             if k not in d:
                 raise ValueError("config.json: missing %s" % k)
         mt = d.get("model_type")
-        return LlamaConfig(
+        cfg = LlamaConfig(
             hidden_size=int(d["hidden_size"]), intermediate_size=int(d["intermediate_size"]),
             num_hidden_layers=int(d["num_hidden_layers"]),
             num_attention_heads=int(d["num_attention_heads"]), vocab_size=int(d["vocab_size"]),
@@ -102,8 +120,14 @@ class LlamaConfig:
             tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
             attention_bias=bool(d.get("attention_bias", mt == "qwen2")),
             model_type=mt, max_position_embeddings=d.get("max_position_embeddings"),
-            hidden_act=d.get("hidden_act", "silu"),
+            hidden_act=d.get("hidden_act", d.get("hidden_activation", "silu")),
             rope_local_base_freq=d.get("rope_local_base_freq"), raw=d)
+        if cfg.partial_rotary_factor is not None:
+            f, rd = float(cfg.partial_rotary_factor), cfg.rotary_dim()
+            if not (0.0 < f <= 1.0) or rd == 0 or rd % 2:
+                raise ValueError("config.json: partial_rotary_factor %r rotates %d of %d head dims"
+                                 % (f, rd, cfg.head_dim()))
+        return cfg
 
     @staticmethod
     def from_json(text):

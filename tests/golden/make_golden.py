@@ -12,7 +12,7 @@ Writes, next to this script:
   fields the tests read.  Shared-weight cases keep their ``bf16_from`` link.
 * ``rope_reference.json`` -- the 10 RoPE cases of the reference's
   ``crates/reng-model/testdata/rope_reference.json`` (transformers tables at
-  sampled positions), reduced to the config keys the RoPE code reads.
+  sampled positions, with each case's config.json).
 
 The data are the reference's own golden vectors; this script only selects
 fields, so the fixture files are byte-for-byte reproducible from it.
@@ -26,11 +26,6 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 FP8_KEYS = ("name", "format", "scaling", "exp_bias", "rows", "cols", "bf16_hex",
             "bf16_from", "scale_bits", "codes_hex", "torch_raw_hex",
             "torch_bytes_saturated", "mean_rel", "max_rel")
-
-ROPE_CFG_KEYS = ("model_type", "hidden_size", "num_attention_heads", "head_dim",
-                 "rope_theta", "rope_scaling", "partial_rotary_factor",
-                 "max_position_embeddings", "original_max_position_embeddings",
-                 "rope_local_base_freq", "rope_parameters", "text_config")
 
 
 def fp8(ref):
@@ -57,13 +52,7 @@ def rope(ref):
         doc = json.load(f)
     cases = []
     for c in doc["cases"]:
-        cfg = {k: c["config"][k] for k in ROPE_CFG_KEYS if k in c["config"]}
-        if "text_config" in cfg:
-            cfg["text_config"] = {k: cfg["text_config"][k] for k in ROPE_CFG_KEYS
-                                  if k in cfg["text_config"]}
-        d = {k: c[k] for k in c if k != "config"}
-        d["config"] = cfg
-        cases.append(d)
+        cases.append(dict(c))
     out = {"source": "reference crates/reng-model/testdata/rope_reference.json",
            "transformers": doc["transformers"], "torch": doc["torch"], "cases": cases}
     with open(os.path.join(HERE, "rope_reference.json"), "w") as f:

@@ -41,11 +41,9 @@ def test_config0_matrix_bit_exact_device_memory(fp8, oracle_lib, fmt, scaling):
     got = codes.cpu().numpy().reshape(-1)
     bad = np.flatnonzero(got != codes_o)
     assert bad.size == 0, (bad[:4], got[bad[:4]], codes_o[bad[:4]])
-    # saturation was exercised
-    if scaling == 2 and fmt == 0:
-        pass
-    else:
-        assert (np.count_nonzero((codes_o & 0x7f) == (0x77 if fmt == 0 else 0x7b))) > 0
+    # per-channel scaling puts every row's absmax on the largest finite code
+    if scaling == 0:
+        assert np.count_nonzero((codes_o & 0x7f) == (0x77 if fmt == 0 else 0x7b)) >= rows
 
 
 def _special_row(rng, cols):

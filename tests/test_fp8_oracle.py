@@ -267,3 +267,15 @@ def test_checkpoint_rows_quantize_within_the_formats_resolution(oracle_lib):
             ai = int(np.argmax(np.abs(wf[r])))
             assert abs(back[r, ai] - wf[r, ai]) <= abs(wf[r, ai]) * 1e-6, (c["name"], r)
     assert seen >= 3
+
+
+def test_an_infinite_weight_gives_the_x86_default_nan(oracle_lib):
+    """An inf in a row makes its scale inf; +-inf / inf is a NaN the division
+    generates, which on x86 (where the reference runs) is the negative
+    'real indefinite': both infinities encode to 0xff, finite weights to
+    signed zero."""
+    o = oracle_lib
+    w = bf(o, [math.inf, -math.inf, 1.0, -2.0])
+    codes, scales, _ = o.quantize(w, 1, 4, E4M3, PCS)
+    assert math.isinf(scales[0])
+    assert list(codes) == [0xff, 0xff, 0x00, 0x80]
