@@ -79,6 +79,27 @@ int reng_fp8_quantize(const uint16_t *w, int64_t rows, int64_t cols, int fmt, in
                       float backoff, uint8_t *codes, float *scales, uint32_t *exp_bias,
                       int mem, void *stream);
 
+/*
+ * reng_fp8_quantize for callers that must not allocate device memory: the
+ * same results, host buffers in and out (w, codes, scales, exp_bias as in
+ * reng_fp8_quantize with RENG_MEM_HOST), but the device staging lives in
+ * one fixed array inside the library instead of memory allocated per call.
+ * Meant for code that runs while another allocator has reserved the GPU's
+ * memory, or that must not enter the CUDA allocator on its path (no
+ * cudaMalloc, cudaFree or allocating library call is made here).
+ * Limits: rows <= 65,536 and rows * cols <= 2,097,152; larger matrices are
+ * refused with RENG_E_INVAL.  Every GPU that loads the library holds the
+ * 6.25 MiB array until exit.  The first call on a device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU (two
+ * streams, two host threads) race and must be serialised by the caller.
+ * The call returns after its copies back to the host are complete.
+ * No counterpart in the reference (its quantizer is host code).
+ */
+int reng_fp8_quantize_noalloc(const uint16_t *w, int64_t rows, int64_t cols, int fmt, int scaling,
+                              float backoff, uint8_t *codes, float *scales, uint32_t *exp_bias,
+                              void *stream);
+
 /* Encode n f32 values to fp8 codes, reng_fp8::encode
  * (crates/reng-fp8/src/lib.rs:154-201).  Device pointers. */
 int reng_fp8_encode(const float *x, int64_t n, int fmt, uint8_t *codes, void *stream);

@@ -66,6 +66,8 @@ SIGNATURES = {
     "reng_device_count": ([_P], C.c_int),
     "reng_fp8_quantize": ([_P, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_float, _P, _P, _P,
                            C.c_int, _P], C.c_int),
+    "reng_fp8_quantize_noalloc": ([_P, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_float, _P, _P,
+                                   _P, _P], C.c_int),
     "reng_fp8_encode": ([_P, C.c_int64, C.c_int, _P, _P], C.c_int),
     "reng_fp8_decode": ([_P, C.c_int64, C.c_int, _P, _P], C.c_int),
     "reng_model_create": ([_P, _P, _P, _P, _P, _P, _P, C.c_int, _P], C.c_int),
