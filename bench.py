@@ -222,9 +222,11 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     clocks.start()
     with torch.cuda.stream(st):
+        torch.cuda.nvtx.range_push("decode_timed")
         e0.record(st)
         eng.decode_device(seeds_d, args.steps, out_d, st.cuda_stream)
         e1.record(st)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop()
     if ws > 1:
@@ -348,7 +350,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--fp8", action="store_true", default=True)
+    ap.add_argument("--no-fp8", dest="fp8", action="store_false",
+                    help="skip the FP8 quantizer line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     from reng.config import SHAPES
