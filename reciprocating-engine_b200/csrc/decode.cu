@@ -22,6 +22,8 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include <cooperative_groups.h>
+
 #include "decode.cuh"
 
 namespace reng {
@@ -635,168 +637,162 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int shape, int max_grid, boo
 }
 
 // ------------------------------------------------------------- attention --
-// One CTA per (split of kAttnChunk keys, KV group, row).  All hpg query
-// heads of the group share each K/V tile (GQA reuse).  f32 online softmax
-// per split; the last CTA of a (row, group) combines the splits.
-constexpr int kAttnThreads = 128;
+// Decode attention over the KV cache.  One thread-block cluster of
+// kAttnCluster CTAs per (row, KV group): CTA s takes the s-th contiguous
+// slice of the row's keys 0..pos and runs an f32 online softmax over it in
+// kAttnChunk-key shared-memory tiles, for all hpg query heads of the group at
+// once (each K/V tile is read once for the whole GQA group).  The slices are
+// then combined through distributed shared memory: after a cluster barrier
+// every CTA reads the (max, sum, unnormalised output) of all slices for its
+// share of the outputs and writes them as bf16.  No global scratch, no
+// atomics, one launch; the cluster barriers are hardware barriers.
+constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxHpg = 8;
 constexpr int kAttnMaxHd = 128;
-constexpr int kAttnMaxSplits = 128;
 
 __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
+    namespace cg = cooperative_groups;
     constexpr int CH = kAttnChunk;
-    constexpr int KP = kAttnMaxHd + 8;  // padded row (bf16)
+    constexpr int KP = kAttnMaxHd + 8;  // padded row (bf16): conflict-free 16-byte reads
     __shared__ __align__(16) uint16_t Ks[CH * KP];
     __shared__ __align__(16) uint16_t Vs[CH * KP];
     __shared__ __align__(16) float Qs[kAttnMaxHpg * kAttnMaxHd];
     __shared__ float Ps[kAttnMaxHpg][CH];
-    __shared__ float Ms[kAttnMaxHpg], Ls[kAttnMaxHpg];
-    __shared__ float Wc[kAttnMaxHpg][kAttnMaxSplits];
-    __shared__ int s_last;
+    __shared__ float Ms[kAttnMaxHpg], Ls[kAttnMaxHpg], Al[kAttnMaxHpg];
+    __shared__ __align__(16) float Os[kAttnMaxHpg * kAttnMaxHd];  // this slice's unnormalised output
 
-    const int s = blockIdx.x, grp = blockIdx.y, m = blockIdx.z;
-    const int hd = a.hd, hpg = a.hpg, tid = threadIdx.x;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int s = (int)cluster.block_rank(), ns = (int)cluster.num_blocks();
+    const int grp = blockIdx.y, m = blockIdx.z;
+    const int hd = a.hd, hpg = a.hpg, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_wait();
     pdl_launch();
     const int pos = a.row_pos[m];
     const int nkeys = min(pos + 1, a.cap);
-    const int nsplit = (nkeys + CH - 1) / CH;
-    if (s >= nsplit) return;
+    const int per = (nkeys + ns - 1) / ns;
+    const int k0 = min(nkeys, s * per), k1 = min(nkeys, k0 + per);
     const int slot = a.row_slot[m];
-    const int k0 = s * CH, kn = min(CH, nkeys - k0);
-    const size_t cache_off = (((size_t)slot * a.n_kv + grp) * a.cap + k0) * hd;
+    const size_t cache_base = (((size_t)slot * a.n_kv + grp) * a.cap) * hd;
     const int q_dim = a.n_kv * hpg * hd;
 
-    // stage q (hpg heads) as f32, and the K/V chunk
     const uint16_t* qrow = a.q + (size_t)m * q_dim + (size_t)grp * hpg * hd;
     for (int i = tid; i < hpg * hd; i += kAttnThreads) Qs[i] = bf16_bits_to_f32(qrow[i]);
+    if (tid < kAttnMaxHpg) {
+        Ms[tid] = -INFINITY;
+        Ls[tid] = 0.f;
+    }
+    // PV ownership: thread -> (head, 4 output dims); hpg * hd / 4 <= 256
+    const int per_head = hd / 4;
+    const int ph = tid / per_head, pd = (tid % per_head) * 4;
+    const bool owns = tid < hpg * per_head;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     const int vec_per_row = hd / 8;
-    for (int i = tid; i < kn * vec_per_row; i += kAttnThreads) {
-        const int j = i / vec_per_row, v = i % vec_per_row;
-        uint4 kv = ldg_nc(a.kcache + cache_off + (size_t)j * hd + v * 8);
-        uint4 vv = ldg_nc(a.vcache + cache_off + (size_t)j * hd + v * 8);
-        *reinterpret_cast<uint4*>(&Ks[j * KP + v * 8]) = kv;
-        *reinterpret_cast<uint4*>(&Vs[j * KP + v * 8]) = vv;
-    }
-    __syncthreads();
 
-    // scores: thread -> key j, heads h = hh, hh+2, ...
-    {
-        const int j = tid % CH, hh = tid / CH;
-        for (int h = hh; h < hpg; h += kAttnThreads / CH) {
-            float sc = -INFINITY;
-            if (j < kn) {
-                float acc = 0.f;
-                const float* qh = Qs + h * hd;
-                for (int d = 0; d < hd; d += 8) {
-                    uint4 kv = *reinterpret_cast<const uint4*>(&Ks[j * KP + d]);
-                    acc += qh[d + 0] * bf16lo(kv.x) + qh[d + 1] * bf16hi(kv.x) +
-                           qh[d + 2] * bf16lo(kv.y) + qh[d + 3] * bf16hi(kv.y) +
-                           qh[d + 4] * bf16lo(kv.z) + qh[d + 5] * bf16hi(kv.z) +
-                           qh[d + 6] * bf16lo(kv.w) + qh[d + 7] * bf16hi(kv.w);
-                }
-                sc = acc;
-            }
-            Ps[h][j] = sc;
+    for (int c0 = k0; c0 < k1; c0 += CH) {
+        const int kn = min(CH, k1 - c0);
+        __syncthreads();  // previous tile fully consumed (and Qs/Ms ready on the first)
+        for (int i = tid; i < kn * vec_per_row; i += kAttnThreads) {
+            const int j = i / vec_per_row, v = i % vec_per_row;
+            const size_t off = cache_base + (size_t)(c0 + j) * hd + v * 8;
+            *reinterpret_cast<uint4*>(&Ks[j * KP + v * 8]) = ldg_nc(a.kcache + off);
+            *reinterpret_cast<uint4*>(&Vs[j * KP + v * 8]) = ldg_nc(a.vcache + off);
         }
-    }
-    __syncthreads();
-    // softmax statistics per head (warp h, h+4, ...)
-    {
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int h = warp; h < hpg; h += kAttnThreads / 32) {
+        __syncthreads();
+        // scores: thread -> key j, heads h = t/CH, t/CH + 4, ...
+        {
+            const int j = tid % CH;
+            for (int h = tid / CH; h < hpg; h += kAttnThreads / CH) {
+                float sc = -INFINITY;
+                if (j < kn) {
+                    float acc = 0.f;
+                    const float* qh = Qs + h * hd;
+                    for (int d = 0; d < hd; d += 8) {
+                        uint4 kv = *reinterpret_cast<const uint4*>(&Ks[j * KP + d]);
+                        acc += qh[d + 0] * bf16lo(kv.x) + qh[d + 1] * bf16hi(kv.x) +
+                               qh[d + 2] * bf16lo(kv.y) + qh[d + 3] * bf16hi(kv.y) +
+                               qh[d + 4] * bf16lo(kv.z) + qh[d + 5] * bf16hi(kv.z) +
+                               qh[d + 6] * bf16lo(kv.w) + qh[d + 7] * bf16hi(kv.w);
+                    }
+                    sc = acc;
+                }
+                Ps[h][j] = sc;
+            }
+        }
+        __syncthreads();
+        // online-softmax statistics: warp h
+        if (warp < hpg) {
+            const int h = warp;
             float mx = -INFINITY;
             for (int j = lane; j < CH; j += 32) mx = fmaxf(mx, Ps[h][j]);
             mx = warp_max(mx);
+            const float m_old = Ms[h], m_new = fmaxf(m_old, mx);
             float sum = 0.f;
             for (int j = lane; j < CH; j += 32) {
-                float p = (j < kn) ? expf(Ps[h][j] - mx) : 0.f;
+                const float p = (j < kn) ? expf(Ps[h][j] - m_new) : 0.f;
                 Ps[h][j] = p;
                 sum += p;
             }
             sum = warp_sum(sum);
             if (lane == 0) {
-                Ms[h] = mx;
-                Ls[h] = sum;
+                const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                Al[h] = alpha;
+                Ls[h] = Ls[h] * alpha + sum;
+                Ms[h] = m_new;
+            }
+        }
+        __syncthreads();
+        if (owns) {
+            const float al = Al[ph];
+            acc0 *= al;
+            acc1 *= al;
+            acc2 *= al;
+            acc3 *= al;
+            for (int j = 0; j < kn; j++) {
+                const float p = Ps[ph][j];
+                uint2 vv = *reinterpret_cast<const uint2*>(&Vs[j * KP + pd]);
+                acc0 += p * bf16lo(vv.x);
+                acc1 += p * bf16hi(vv.x);
+                acc2 += p * bf16lo(vv.y);
+                acc3 += p * bf16hi(vv.y);
             }
         }
     }
-    __syncthreads();
-    // P @ V: each thread four output dims of one head
-    const int per_head = hd / 4;
-    const size_t pbase = (((size_t)m * a.n_kv + grp) * a.nsplit_max + s) * hpg;
-    for (int o = tid; o < hpg * per_head; o += kAttnThreads) {
-        const int h = o / per_head, d = (o % per_head) * 4;
-        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-        for (int j = 0; j < kn; j++) {
-            const float p = Ps[h][j];
-            uint2 vv = *reinterpret_cast<const uint2*>(&Vs[j * KP + d]);
-            acc0 += p * bf16lo(vv.x);
-            acc1 += p * bf16hi(vv.x);
-            acc2 += p * bf16lo(vv.y);
-            acc3 += p * bf16hi(vv.y);
-        }
-        if (nsplit == 1) {
-            const float il = 1.0f / Ls[h];
-            uint16_t* out = a.out + (size_t)m * q_dim + ((size_t)grp * hpg + h) * hd + d;
-            out[0] = f32_to_bf16_bits(acc0 * il);
-            out[1] = f32_to_bf16_bits(acc1 * il);
-            out[2] = f32_to_bf16_bits(acc2 * il);
-            out[3] = f32_to_bf16_bits(acc3 * il);
-        } else {
-            float* po = a.part_o + (pbase + h) * hd + d;
-            *reinterpret_cast<float4*>(po) = make_float4(acc0, acc1, acc2, acc3);
-        }
-    }
-    if (nsplit == 1) return;
-    if (tid < hpg) {
-        a.part_ml[(pbase + tid) * 2 + 0] = Ms[tid];
-        a.part_ml[(pbase + tid) * 2 + 1] = Ls[tid];
-    }
-    __threadfence();
-    __syncthreads();
-    unsigned int* cnt = a.count + (size_t)m * a.n_kv + grp;
-    if (tid == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(nsplit - 1));
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // combine: weights w[h][s] = exp(m_s - M) / sum_s exp(m_s - M) l_s
-    const size_t base0 = (((size_t)m * a.n_kv + grp) * a.nsplit_max) * hpg;
-    for (int h = tid; h < hpg; h += kAttnThreads) {
-        float mx = -INFINITY;
-        for (int t = 0; t < nsplit; t++) mx = fmaxf(mx, __ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2));
-        float den = 0.f;
-        for (int t = 0; t < nsplit; t++) {
-            float e = expf(__ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2) - mx);
-            Wc[h][t] = e;
-            den += e * __ldcg(a.part_ml + (base0 + (size_t)t * hpg + h) * 2 + 1);
-        }
-        const float iden = 1.0f / den;
-        for (int t = 0; t < nsplit; t++) Wc[h][t] *= iden;
-    }
-    __syncthreads();
-    for (int o = tid; o < hpg * hd; o += kAttnThreads) {
+    if (owns) *reinterpret_cast<float4*>(&Os[ph * hd + pd]) = make_float4(acc0, acc1, acc2, acc3);
+    cluster.sync();  // every slice's (Ms, Ls, Os) is complete and visible cluster-wide
+
+    // combine: CTA s writes outputs o = s, s + ns, ... of the hpg * hd
+    for (int o = s + ns * tid; o < hpg * hd; o += ns * kAttnThreads) {
         const int h = o / hd, d = o % hd;
-        float acc = 0.f;
-        for (int t = 0; t < nsplit; t++)
-            acc += Wc[h][t] * __ldcg(a.part_o + (base0 + (size_t)t * hpg + h) * hd + d);
-        a.out[(size_t)m * q_dim + ((size_t)grp * hpg + h) * hd + d] = f32_to_bf16_bits(acc);
+        float mx = -INFINITY;
+        for (int r = 0; r < ns; r++) mx = fmaxf(mx, *cluster.map_shared_rank(&Ms[h], r));
+        float num = 0.f, den = 0.f;
+        for (int r = 0; r < ns; r++) {
+            const float mr = *cluster.map_shared_rank(&Ms[h], r);
+            const float w = (mr == -INFINITY) ? 0.f : expf(mr - mx);
+            num += w * *cluster.map_shared_rank(&Os[h * hd + d], r);
+            den += w * *cluster.map_shared_rank(&Ls[h], r);
+        }
+        a.out[(size_t)m * q_dim + ((size_t)grp * hpg + h) * hd + d] = f32_to_bf16_bits(num / den);
     }
-    if (tid == 0) *cnt = 0u;
+    cluster.sync();  // keep this CTA's shared memory alive until its peers have read it
 }
 
 cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t st) {
-    if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.nsplit_max > kAttnMaxSplits)
+    if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.hpg * (a.hd / 4) > kAttnThreads)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    cfg.gridDim = dim3(a.nsplit_max, a.n_kv, a.M);
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(kAttnCluster, a.n_kv, a.M);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.stream = st;
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAttnCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, k_attn, a);
 }
 

@@ -77,12 +77,9 @@ struct AttnArgs {
     const uint16_t* kcache; // this layer [B][n_kv][cap][hd]
     const uint16_t* vcache;
     uint16_t* out;          // [M][q_dim]
-    float* part_o;          // [M][n_kv][nsplit_max][hpg][hd]
-    float* part_ml;         // [M][n_kv][nsplit_max][hpg][2]
-    unsigned int* count;    // [M][n_kv]
     const int* row_slot;
     const int* row_pos;
-    int M, n_kv, hpg, hd, cap, nsplit_max;
+    int M, n_kv, hpg, hd, cap;
 };
 
 struct EmbedArgs {
@@ -128,6 +125,7 @@ int fp8_quantize_device(const uint16_t* w, int64_t rows, int64_t cols, int fmt, 
                         float backoff, uint8_t* codes, float* scales, uint32_t* bias_dev,
                         cudaStream_t st);
 
-constexpr int kAttnChunk = 64;
+constexpr int kAttnChunk = 64;    // keys per shared-memory tile
+constexpr int kAttnCluster = 8;   // CTAs (key slices) per (row, KV group)
 
 }  // namespace reng

@@ -50,12 +50,9 @@ struct reng_model {
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
     int* err = nullptr;  // device error word of the bounded waits
     uint32_t *ids_ring = nullptr, *prefill_ids = nullptr, *next_id = nullptr;
-    float *part_o = nullptr, *part_ml = nullptr;
-    unsigned int* attn_count = nullptr;
     float* am_val = nullptr;
     int* am_idx = nullptr;
     unsigned int* am_count = nullptr;
-    int nsplit_max = 0;
     int lm_grid = 0;
     // GEMV launch shapes per kind (qkv, o, gate/up, down, LM head), for
     // M <= 2 and M > 2 activation rows
@@ -207,8 +204,7 @@ int validate(const reng_model_desc* d) {
                    "reng_model_create: unknown weight format");
     RENG_CHECK_ARG(std::isfinite(d->eps) && d->eps >= 0.f && std::isfinite(d->attn_scale),
                    "reng_model_create: eps / attn_scale not finite");
-    RENG_CHECK_ARG((int64_t)d->capacity <= (int64_t)kAttnChunk * 128,
-                   "reng_model_create: capacity above " + std::to_string(kAttnChunk * 128));
+    RENG_CHECK_ARG(d->capacity <= (1 << 20), "reng_model_create: capacity above 1048576 positions");
     if (d->batch > kMaxRows)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) +
                                             " above " + std::to_string(kMaxRows) + " is not built yet");
@@ -289,9 +285,6 @@ int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
     at.kcache = m->kcache + (size_t)l * m->layer_kv;
     at.vcache = m->vcache + (size_t)l * m->layer_kv;
     at.out = m->attn;
-    at.part_o = m->part_o;
-    at.part_ml = m->part_ml;
-    at.count = m->attn_count;
     at.row_slot = m->row_slot;
     at.row_pos = m->row_pos;
     at.M = M;
@@ -299,7 +292,6 @@ int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
     at.hpg = m->hpg;
     at.hd = m->hd;
     at.cap = m->cap;
-    at.nsplit_max = m->nsplit_max;
     CU(launch_attn(at, kAttnChunk, true, st));
     return RENG_OK;
 }
@@ -555,11 +547,6 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->ids_ring, (size_t)(m->cap + 1) * m->B));
     TRY(dalloc(m, &m->prefill_ids, MR));
     TRY(dalloc(m, &m->next_id, 1));
-    m->nsplit_max = (m->cap + kAttnChunk - 1) / kAttnChunk;
-    TRY(dalloc(m, &m->part_o, (size_t)MR * m->nkv * m->nsplit_max * m->hpg * m->hd));
-    TRY(dalloc(m, &m->part_ml, (size_t)MR * m->nkv * m->nsplit_max * m->hpg * 2));
-    TRY(dalloc(m, &m->attn_count, (size_t)MR * m->nkv));
-    CU(cudaMemsetAsync(m->attn_count, 0, (size_t)MR * m->nkv * 4, m->st));
     CU(cudaMemsetAsync(m->pos, 0, (size_t)m->B * 4, m->st));
     CU(cudaMemsetAsync(m->step, 0, 4, m->st));
     CU(cudaMemsetAsync(m->x_res, 0, (size_t)MR * H * 2, m->st));
