@@ -195,8 +195,9 @@ def run_ours(args, cfg):
     w = random_weights(cfg, seed=args.seed, device=dev)
     torch.cuda.synchronize()
     cap = args.prompt + args.warmup + 2 * args.steps + 8
+    fp8 = ("e4m3", "pcs") if args.weights == "fp8" else None
     eng = Engine(cfg, w, batch=args.batch, capacity=cap, device=local, tp_rank=rank,
-                 tp_world=ws, nccl_id=nccl_id)
+                 tp_world=ws, nccl_id=nccl_id, fp8=fp8)
     del w
     torch.cuda.empty_cache()
     B = args.batch
@@ -261,11 +262,17 @@ def run_ours(args, cfg):
         value = tokens / (ms / 1e3)
         peak, peak_kind = peaks()
         ctx = args.prompt + args.steps // 2
-        bytes_step = (2 * cfg.active_params() / ws +
-                      (1 - 1.0 / ws) * 2 * cfg.hidden_size * cfg.vocab_size +
-                      B * ctx * cfg.kv_bytes_per_token() / ws)
+        head = cfg.hidden_size * cfg.vocab_size
+        body = cfg.active_params() - head
+        wb = 1 if args.weights == "fp8" else 2  # bytes per projection weight
+        # projections sharded over the ranks, LM head replicated, KV per rank;
+        # FP8 adds one f32 scale per output row
+        rows_per_layer = (cfg.q_dim() + 2 * cfg.n_kv_heads() * cfg.head_dim() + cfg.hidden_size +
+                          2 * cfg.intermediate_size + cfg.hidden_size)
+        scales = 4 * rows_per_layer * cfg.num_hidden_layers if args.weights == "fp8" else 0
+        bytes_step = (wb * body + scales) / ws + 2 * head + B * ctx * cfg.kv_bytes_per_token() / ws
         h, inter = cfg.hidden_size, cfg.intermediate_size // ws
-        gu_bytes = 2 * inter * h * 2 + B * h * 2 + B * inter * 2
+        gu_bytes = 2 * inter * h * wb + (8 * inter if args.weights == "fp8" else 0) + B * h * 2 + B * inter * 2
         gu_ms = kt["gate_up"]
         achieved = gu_bytes / (gu_ms / 1e3) / 1e9
         step_gbs = bytes_step / (ms / 1e3 / args.steps) / 1e9
@@ -273,11 +280,13 @@ def run_ours(args, cfg):
             "metric": "decode tok/s (b%d)" % B, "value": value, "unit": "tok/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.weights == "bf16" else "fp8-e4m3 weights, bf16 activations",
             "data": "synthetic (random-init N(0,0.02) bf16 weights, uniform-random prompt ids)",
-            "config": {"workload": "%s decode b%d, prompt %d, %d greedy steps%s" % (
-                args.model, B, args.prompt, args.steps, ", tensor-parallel %d" % ws if ws > 1 else ""),
-                "model": args.model, "batch": B, "prompt": args.prompt,
+            "config": {"workload": "%s%s decode b%d, prompt %d, %d greedy steps%s" % (
+                args.model, " fp8" if args.weights == "fp8" else "", B, args.prompt, args.steps,
+                ", tensor-parallel %d" % ws if ws > 1 else ""),
+                "model": args.model, "batch": B, "prompt": args.prompt, "weights": args.weights,
                 "parallelism": "tp%d" % ws if ws > 1 else "single",
                 "l2": "inputs larger than L2 (weights %.1f GB streamed per step)" % (bytes_step / 1e9)},
             "clocks": clk,
@@ -347,6 +356,8 @@ def main():
     ap.add_argument("--model", default="llama-3.1-8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
+                    help="fp8: projections quantized E4M3 per channel at load (config 3)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true")

@@ -42,7 +42,9 @@ __device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, const uint16_t* x
     return ldg_nc(a.x + (size_t)g * a.ldx + k);
 }
 
-// RMS-normalise the staged x rows in place: x' = bf16(x * inv[m] * gain[k]).
+// RMS-normalise the staged x rows in place: x' = bf16(x * inv[m] * gain[k])
+// (f16 for the FP8-weight kernels, whose mma runs in f16).
+template <int W8>
 __device__ __forceinline__ void normalise_x(const GemvArgs& a, uint16_t* xs, int xstride, int K,
                                             const float* inv_s) {
     const int nv = K / 8;
@@ -53,11 +55,77 @@ __device__ __forceinline__ void normalise_x(const GemvArgs& a, uint16_t* xs, int
         const float inv = inv_s[m];
         const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain + k));
         const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain + k + 4));
-        v.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
-        v.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
-        v.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
-        v.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+        if (W8) {
+            v.x = pack_f16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+            v.y = pack_f16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+            v.z = pack_f16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+            v.w = pack_f16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+        } else {
+            v.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+            v.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+            v.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+            v.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+        }
         *p = v;
+    }
+}
+
+// Staged bf16 x rows -> f16 in place (FP8-weight kernels without a norm).
+__device__ __forceinline__ void x_to_f16(const GemvArgs& a, uint16_t* xs, int xstride, int K) {
+    const int nv = K / 8;
+    for (int i = threadIdx.x; i < a.M * nv; i += blockDim.x) {
+        const int m = i / nv, k = (i % nv) * 8;
+        uint4* p = reinterpret_cast<uint4*>(xs + m * xstride + k);
+        uint4 v = *p;
+        v.x = bf16x2_to_f16x2(v.x);
+        v.y = bf16x2_to_f16x2(v.y);
+        v.z = bf16x2_to_f16x2(v.z);
+        v.w = bf16x2_to_f16x2(v.w);
+        *p = v;
+    }
+}
+
+// FP8 blocks: lane (g, q) multiplies k = 64c + 16q .. +16; its x fragment is
+// those 16 values of row g as f16 (two uint4).
+__device__ __forceinline__ void x_fragment16(const GemvArgs& a, const uint16_t* xs, int xstride, int K, int c,
+                                             int g, int q, uint4& lo, uint4& hi) {
+    const int k = c * 64 + q * 16;
+    if (g >= a.M || k >= K) {
+        lo = hi = make_uint4(0u, 0u, 0u, 0u);
+        return;
+    }
+    if (xs != nullptr) {
+        lo = *reinterpret_cast<const uint4*>(xs + g * xstride + k);
+        hi = *reinterpret_cast<const uint4*>(xs + g * xstride + k + 8);
+        return;
+    }
+    const uint4 b0 = ldg_nc(a.x + (size_t)g * a.ldx + k), b1 = ldg_nc(a.x + (size_t)g * a.ldx + k + 8);
+    lo = make_uint4(bf16x2_to_f16x2(b0.x), bf16x2_to_f16x2(b0.y), bf16x2_to_f16x2(b0.z), bf16x2_to_f16x2(b0.w));
+    hi = make_uint4(bf16x2_to_f16x2(b1.x), bf16x2_to_f16x2(b1.y), bf16x2_to_f16x2(b1.z), bf16x2_to_f16x2(b1.w));
+}
+
+// One packed block into the accumulators.  bf16: two m16n8k16 steps over
+// 32 k.  FP8: the lane's 16 codes of rows g and g+8 become f16 pairs and run
+// four f16 steps over 64 k; step i takes codes 4i..4i+3 (k pairs (2q, 2q+1)
+// and (2q+8, 2q+9) of the step in the mma's numbering), matched by the same
+// x values.
+template <int W8>
+__device__ __forceinline__ void block_mma(float (&acc)[4], const uint4& wa, const uint4& wb, const GemvArgs& a,
+                                          const uint16_t* xs, int xstride, int K, int c, int g, int q) {
+    if (!W8) {
+        const uint4 xf = x_fragment(a, xs, xstride, K, c, g, q);
+        mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xf.x, xf.y);
+        mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xf.z, xf.w);
+    } else {
+        uint4 xl, xh;
+        x_fragment16(a, xs, xstride, K, c, g, q, xl, xh);
+        const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb[4] = {wb.x, wb.y, wb.z, wb.w};
+        const uint32_t xv[8] = {xl.x, xl.y, xl.z, xl.w, xh.x, xh.y, xh.z, xh.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            mma_f16_16816(acc, e4m3x2_to_f16x2(ra[i] & 0xffffu), e4m3x2_to_f16x2(rb[i] & 0xffffu),
+                          e4m3x2_to_f16x2(ra[i] >> 16), e4m3x2_to_f16x2(rb[i] >> 16), xv[2 * i], xv[2 * i + 1]);
+        }
     }
 }
 
@@ -281,7 +349,7 @@ __host__ __device__ constexpr int gemv_ring_bytes() {
     return PIPE == PIPE_TMA ? kTmaRing : 0;
 }
 
-template <int EPI, int NWARP, int PIPE>
+template <int EPI, int NWARP, int PIPE, int W8>
 __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     extern __shared__ __align__(128) uint8_t smem_dyn[];
     __shared__ float4 red[NWARP > 1 ? NWARP : 1][32];
@@ -394,7 +462,10 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         }
         __syncthreads();
         if (a.ss_in != nullptr) {
-            normalise_x(a, xsm, xstride, K, inv_s);
+            normalise_x<W8>(a, xsm, xstride, K, inv_s);
+            __syncthreads();
+        } else if (W8) {
+            x_to_f16(a, xsm, xstride, K);
             __syncthreads();
         }
         xs = xsm;
@@ -423,9 +494,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
                 if (b0 + b < c1) {
                     const uint4 wa = lds128(st + b * kBlockBytes);
                     const uint4 wb = lds128(st + b * kBlockBytes + 512);
-                    const uint4 xf = x_fragment(a, xs, xstride, K, b0 + b, g, q);
-                    mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xf.x, xf.y);
-                    mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xf.z, xf.w);
+                    block_mma<W8>(acc, wa, wb, a, xs, xstride, K, b0 + b, g, q);
                 }
             // the stage is read: let the async proxy refill it
             __syncwarp();
@@ -444,11 +513,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
             rload(j + 1);
 #pragma unroll
             for (int b = 0; b < kRegDepth; b++)
-                if (b0 + b < c1) {
-                    const uint4 xf = x_fragment(a, xs, xstride, K, b0 + b, g, q);
-                    mma_bf16_16816(acc, wa[b].x, wb[b].x, wa[b].y, wb[b].y, xf.x, xf.y);
-                    mma_bf16_16816(acc, wa[b].z, wb[b].z, wa[b].w, wb[b].w, xf.z, xf.w);
-                }
+                if (b0 + b < c1) block_mma<W8>(acc, wa[b], wb[b], a, xs, xstride, K, b0 + b, g, q);
         }
         if ((j % nct) != nct - 1) continue;
         // ---- a tile is complete: reduce the warps' k-slices on warp 0 ----
@@ -468,7 +533,16 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
                 }
             }
         }
-        if (warp == 0) gemv_epilogue<EPI>(a, tile, acc, g, q, best_v, best_i);
+        if (warp == 0) {
+            if (W8) {  // per-row scale of the FP8 codes
+                const float s0 = a.wscale[tile * kTileRows + g], s1 = a.wscale[tile * kTileRows + g + 8];
+                acc[0] *= s0;
+                acc[1] *= s0;
+                acc[2] *= s1;
+                acc[3] *= s1;
+            }
+            gemv_epilogue<EPI>(a, tile, acc, g, q, best_v, best_i);
+        }
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
     }
     if (PIPE == PIPE_TMA && failed && lane == 0) {
@@ -535,14 +609,21 @@ static size_t gemv_xbytes(const GemvArgs& a) {
 
 template <int EPI, int NW>
 static cudaError_t prepare_one() {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          200 * 1024);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024);
     return e;
 }
 
-template <int EPI, int NW, int PIPE>
+template <int EPI, int NW, int PIPE, int W8>
 static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStream_t st, int* grid_out) {
     const size_t xbytes = gemv_xbytes(a);
     const size_t smem = (size_t)NW * gemv_ring_bytes<PIPE>() + xbytes;
@@ -550,7 +631,7 @@ static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStr
     int per_sm = 0, dev = 0, sms = 148;
     cudaGetDevice(&dev);
     sms = num_sms(dev);
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<EPI, NW, PIPE>, NW * 32, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<EPI, NW, PIPE, W8>, NW * 32, smem);
     if (e != cudaSuccess || per_sm < 1) per_sm = 1;
     int cap = sms * per_sm;
     if (max_grid > 0 && max_grid < cap) cap = max_grid;
@@ -568,7 +649,7 @@ static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStr
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemv<EPI, NW, PIPE>, a, xbytes > 0 ? 1 : 0);
+    return cudaLaunchKernelEx(&cfg, k_gemv<EPI, NW, PIPE, W8>, a, xbytes > 0 ? 1 : 0);
 }
 
 template <int EPI>
@@ -594,10 +675,14 @@ template <int EPI>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int shape, int max_grid, bool pdl, cudaStream_t st,
                                  int* grid_out) {
     switch (shape) {
-        case 4: return launch_one<EPI, 4, PIPE_REG>(a, max_grid, pdl, st, grid_out);
-        case 8: return launch_one<EPI, 8, PIPE_REG>(a, max_grid, pdl, st, grid_out);
-        case 104: return launch_one<EPI, 4, PIPE_TMA>(a, max_grid, pdl, st, grid_out);
-        case 108: return launch_one<EPI, 8, PIPE_TMA>(a, max_grid, pdl, st, grid_out);
+        case 4: return a.w8 ? launch_one<EPI, 4, PIPE_REG, 1>(a, max_grid, pdl, st, grid_out)
+                            : launch_one<EPI, 4, PIPE_REG, 0>(a, max_grid, pdl, st, grid_out);
+        case 8: return a.w8 ? launch_one<EPI, 8, PIPE_REG, 1>(a, max_grid, pdl, st, grid_out)
+                            : launch_one<EPI, 8, PIPE_REG, 0>(a, max_grid, pdl, st, grid_out);
+        case 104: return a.w8 ? launch_one<EPI, 4, PIPE_TMA, 1>(a, max_grid, pdl, st, grid_out)
+                              : launch_one<EPI, 4, PIPE_TMA, 0>(a, max_grid, pdl, st, grid_out);
+        case 108: return a.w8 ? launch_one<EPI, 8, PIPE_TMA, 1>(a, max_grid, pdl, st, grid_out)
+                              : launch_one<EPI, 8, PIPE_TMA, 0>(a, max_grid, pdl, st, grid_out);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -606,8 +691,8 @@ template <int EPI>
 static int blocks_t(int nwarp) {
     int n = 0;
     cudaError_t e = cudaErrorInvalidValue;
-    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4, PIPE_REG>, 128, 0);
-    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8, PIPE_REG>, 256, 0);
+    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4, PIPE_REG, 0>, 128, 0);
+    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8, PIPE_REG, 0>, 256, 0);
     return e == cudaSuccess ? n : 1;
 }
 
@@ -886,6 +971,52 @@ cudaError_t launch_pack(const PackArgs& a, cudaStream_t st) {
     const int64_t total = (int64_t)a.tiles * a.kc * 64;
     int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
     k_pack<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+// FP8 packing: one thread per (block, half, lane) 16-byte piece: row 8h + l/4
+// of the tile, k = 64c + 16(l%4) .. +16.
+__global__ void k_pack8(Pack8Args a) {
+    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(i & 31), h = (int)((i >> 5) & 1);
+        const int64_t blk = i >> 6;
+        const int c = (int)(blk % a.kc);
+        const int tile = (int)(blk / a.kc);
+        const int srow = a.rowmap[tile * kTileRows + h * 8 + (lane >> 2)];
+        const int k0 = c * 64 + (lane & 3) * 16;
+        uint8_t v[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) v[e] = (srow >= 0 && k0 + e < a.K) ? a.src[(int64_t)srow * a.K + k0 + e] : 0;
+        uint4 o;
+        o.x = v[0] | (v[1] << 8) | (v[2] << 16) | ((uint32_t)v[3] << 24);
+        o.y = v[4] | (v[5] << 8) | (v[6] << 16) | ((uint32_t)v[7] << 24);
+        o.z = v[8] | (v[9] << 8) | (v[10] << 16) | ((uint32_t)v[11] << 24);
+        o.w = v[12] | (v[13] << 8) | (v[14] << 16) | ((uint32_t)v[15] << 24);
+        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytes + h * 512 + lane * 16) = o;
+    }
+}
+
+cudaError_t launch_pack8(const Pack8Args& a, cudaStream_t st) {
+    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+    k_pack8<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+// Row scales in packed row order: dst[p] = src[rowmap[p]] (x mul for the
+// rows below mul_rows: the attention scale on the q rows); 0 for padding.
+__global__ void k_gather_scales(const float* src, const int* rowmap, int n, float mul, int mul_rows, float* dst) {
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+        const int r = rowmap[p];
+        dst[p] = r < 0 ? 0.f : (r < mul_rows ? src[r] * mul : src[r]);
+    }
+}
+
+cudaError_t launch_gather_scales(const float* src, const int* rowmap, int n, float mul, int mul_rows, float* dst,
+                                 cudaStream_t st) {
+    k_gather_scales<<<(n + 255) / 256, 256, 0, st>>>(src, rowmap, n, mul, mul_rows, dst);
     return cudaGetLastError();
 }
 

@@ -70,6 +70,10 @@ struct GemvArgs {
     uint32_t* ids_ring;     // [(cap+1)][batch]
     uint32_t* next_id;      // prefill: argmax of the last row
     int* err;               // device error word (RENG_E_TIMEOUT from a bounded wait)
+    // FP8-E4M3 weights: blocks hold 16 rows x 64 k of codes; the mma runs in
+    // f16 (x staged as f16) and the epilogue multiplies by the row's scale
+    int w8;
+    const float* wscale;    // [tiles*16] per packed row
 };
 
 struct AttnArgs {
@@ -99,6 +103,13 @@ struct EmbedArgs {
     int batch;
 };
 
+struct Pack8Args {
+    const uint8_t* src;    // codes, row-major [rows][K]
+    const int* rowmap;     // [tiles*16] source row per packed row, -1 = zero
+    int tiles, K, kc;      // kc = ceil(K / 64)
+    uint8_t* dst;
+};
+
 struct PackArgs {
     const uint16_t* src;   // row-major [rows][ld]
     int64_t ld;
@@ -119,6 +130,9 @@ cudaError_t gemv_prepare();
 cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
 cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);
+cudaError_t launch_pack8(const Pack8Args& a, cudaStream_t st);
+cudaError_t launch_gather_scales(const float* src, const int* rowmap, int n, float mul, int mul_rows,
+                                 float* dst, cudaStream_t st);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, int64_t n, cudaStream_t st);
 
 int fp8_quantize_device(const uint16_t* w, int64_t rows, int64_t cols, int fmt, int scaling,

@@ -26,6 +26,8 @@ int gemv_blocks_per_sm(int epi, int nwarp);
 struct LayerDev {
     uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
     float *g1 = nullptr, *g2 = nullptr, *bqkv = nullptr;
+    // FP8 weights: per packed row scales (null for bf16)
+    float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sd = nullptr;
 };
 
 struct reng_model {
@@ -49,6 +51,7 @@ struct reng_model {
     float* part = nullptr;  // tensor-parallel f32 partials [kMaxRows][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
     int* err = nullptr;  // device error word of the bounded waits
+    int w8 = 0;          // projections held as FP8-E4M3 codes + row scales
     uint32_t *ids_ring = nullptr, *prefill_ids = nullptr, *next_id = nullptr;
     float* am_val = nullptr;
     int* am_idx = nullptr;
@@ -132,6 +135,42 @@ int pack(reng_model* m, uint8_t** out, const uint16_t* staged, const std::vector
     return RENG_OK;
 }
 
+// Quantize a staged bf16 matrix [src_rows][K] on the device (E4M3,
+// per-channel absmax scales, backoff 1.0: reng_fp8::quantize_with's
+// per-channel scheme) and pack the codes; the scales go to packed row order,
+// the rows below scale_rows multiplied by `scale` (the attention scale on the
+// q rows, which the bf16 path folds into wq).
+int pack_fp8(reng_model* m, uint8_t** out, float** out_scales, const uint16_t* staged, int src_rows,
+             const std::vector<int>& rowmap, int K, float scale, int scale_rows, int* tiles_out) {
+    const int tiles = (int)(rowmap.size() / kTileRows);
+    const int kc = (K + 63) / 64;
+    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytes));
+    TRY(dalloc(m, out_scales, (size_t)tiles * kTileRows));
+    uint8_t* codes = nullptr;
+    float* sc = nullptr;
+    int* dmap = nullptr;
+    CU(cudaMallocAsync((void**)&codes, (size_t)src_rows * K, m->st));
+    CU(cudaMallocAsync((void**)&sc, (size_t)src_rows * 4, m->st));
+    CU(cudaMallocAsync((void**)&dmap, rowmap.size() * sizeof(int), m->st));
+    CU(cudaMemcpyAsync(dmap, rowmap.data(), rowmap.size() * sizeof(int), cudaMemcpyHostToDevice, m->st));
+    TRY(fp8_quantize_device(staged, src_rows, K, RENG_FP8_E4M3, RENG_SCALING_PCS, 1.0f, codes, sc, nullptr, m->st));
+    Pack8Args a{};
+    a.src = codes;
+    a.rowmap = dmap;
+    a.tiles = tiles;
+    a.K = K;
+    a.kc = kc;
+    a.dst = *out;
+    CU(launch_pack8(a, m->st));
+    CU(launch_gather_scales(sc, dmap, tiles * kTileRows, scale, scale_rows, *out_scales, m->st));
+    CU(cudaFreeAsync(codes, m->st));
+    CU(cudaFreeAsync(sc, m->st));
+    CU(cudaFreeAsync(dmap, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    if (tiles_out) *tiles_out = tiles;
+    return RENG_OK;
+}
+
 std::vector<int> plain_map(int rows) {
     int tiles = (rows + kTileRows - 1) / kTileRows;
     std::vector<int> v((size_t)tiles * kTileRows, -1);
@@ -208,8 +247,6 @@ int validate(const reng_model_desc* d) {
     if (d->batch > kMaxRows)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) +
                                             " above " + std::to_string(kMaxRows) + " is not built yet");
-    if (d->weights != RENG_WEIGHTS_BF16)
-        return fail(RENG_E_UNSUPPORTED, "reng_model_create: fp8 weights are not wired yet");
     return RENG_OK;
 }
 
@@ -241,6 +278,9 @@ GemvArgs base_args(reng_model* m) {
     return g;
 }
 
+// k-chunks of a K-wide projection: 32 bf16 or 64 FP8 codes per packed block
+int proj_kc(reng_model* m, int K) { return m->w8 ? (K + 63) / 64 : (K + kChunkK - 1) / kChunkK; }
+
 GemvArgs norm_args(reng_model* m, int M, const float* gain) {
     GemvArgs g = base_args(m);
     g.M = M;
@@ -262,6 +302,9 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     const LayerDev& w = m->layers[l];
     GemvArgs g = norm_args(m, M, w.g1);
     g.w = w.wqkv;
+    g.w8 = m->w8;
+    g.wscale = w.sqkv;
+    g.kc = proj_kc(m, m->hidden);
     g.tiles = m->qkv_tiles;
     g.out = m->qbuf;
     g.ldo = m->q_dim;
@@ -305,7 +348,9 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* 
     o.w = which == 0 ? w.wo : w.wd;
     o.tiles = which == 0 ? m->o_tiles : m->d_tiles;
     o.K = which == 0 ? m->q_dim : m->inter;
-    o.kc = (o.K + kChunkK - 1) / kChunkK;
+    o.kc = proj_kc(m, o.K);
+    o.w8 = m->w8;
+    o.wscale = which == 0 ? w.so : w.sd;
     o.x = which == 0 ? m->attn : m->act;
     o.ldx = o.K;
     o.out = m->x_res;
@@ -328,6 +373,9 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
     const LayerDev& w = m->layers[l];
     GemvArgs u = norm_args(m, M, w.g2);
     u.w = w.wgu;
+    u.w8 = m->w8;
+    u.wscale = w.sgu;
+    u.kc = proj_kc(m, m->hidden);
     u.tiles = m->gu_tiles;
     u.out = m->act;
     u.ldo = m->inter;
@@ -419,6 +467,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(gemv_prepare());
     m->rank = d->tp_rank;
     m->world = d->tp_world;
+    m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;
     const int W = m->world, R = m->rank;
     m->hidden = d->hidden;
     m->L = d->n_layers;
@@ -482,17 +531,30 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
         TRY(copy_matrix(stage + (size_t)m->q_dim * H, s.wk + (size_t)R * m->kv_dim * H, m->kv_dim, H, H, mem, m->st));
         TRY(copy_matrix(stage + (size_t)(m->q_dim + m->kv_dim) * H, s.wv + (size_t)R * m->kv_dim * H, m->kv_dim, H, H,
                         mem, m->st));
-        TRY(pack(m, &w.wqkv, stage, qkv_map, H, d->attn_scale, m->q_dim, &m->qkv_tiles));
+        if (m->w8)
+            TRY(pack_fp8(m, &w.wqkv, &w.sqkv, stage, m->q_dim + 2 * m->kv_dim, qkv_map, H, d->attn_scale, m->q_dim,
+                         &m->qkv_tiles));
+        else
+            TRY(pack(m, &w.wqkv, stage, qkv_map, H, d->attn_scale, m->q_dim, &m->qkv_tiles));
         // o_proj column window
         TRY(copy_matrix(stage, s.wo + (size_t)R * m->q_dim, H, m->q_dim, q_full, mem, m->st));
-        TRY(pack(m, &w.wo, stage, plain_map(H), m->q_dim, 0.f, 0, &m->o_tiles));
+        if (m->w8)
+            TRY(pack_fp8(m, &w.wo, &w.so, stage, H, plain_map(H), m->q_dim, 1.f, 0, &m->o_tiles));
+        else
+            TRY(pack(m, &w.wo, stage, plain_map(H), m->q_dim, 0.f, 0, &m->o_tiles));
         // gate, up row blocks
         TRY(copy_matrix(stage, s.wg + (size_t)R * m->inter * H, m->inter, H, H, mem, m->st));
         TRY(copy_matrix(stage + (size_t)m->inter * H, s.wu + (size_t)R * m->inter * H, m->inter, H, H, mem, m->st));
-        TRY(pack(m, &w.wgu, stage, gu_map, H, 0.f, 0, &m->gu_tiles));
+        if (m->w8)
+            TRY(pack_fp8(m, &w.wgu, &w.sgu, stage, 2 * m->inter, gu_map, H, 1.f, 0, &m->gu_tiles));
+        else
+            TRY(pack(m, &w.wgu, stage, gu_map, H, 0.f, 0, &m->gu_tiles));
         // down column window
         TRY(copy_matrix(stage, s.wd + (size_t)R * m->inter, H, m->inter, d->inter, mem, m->st));
-        TRY(pack(m, &w.wd, stage, plain_map(H), m->inter, 0.f, 0, &m->d_tiles));
+        if (m->w8)
+            TRY(pack_fp8(m, &w.wd, &w.sd, stage, H, plain_map(H), m->inter, 1.f, 0, &m->d_tiles));
+        else
+            TRY(pack(m, &w.wd, stage, plain_map(H), m->inter, 0.f, 0, &m->d_tiles));
         TRY(upload_f32(m, &w.g1, s.g1, H, mem));
         TRY(upload_f32(m, &w.g2, s.g2, H, mem));
         if (d->has_qkv_bias) {
@@ -554,7 +616,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
 
     // launch shapes
     const int kch = (H + kChunkK - 1) / kChunkK;
-    const int kcs[5] = {kch, (m->q_dim + kChunkK - 1) / kChunkK, kch, (m->inter + kChunkK - 1) / kChunkK, kch};
+    const int kcs[5] = {proj_kc(m, H), proj_kc(m, m->q_dim), proj_kc(m, H), proj_kc(m, m->inter), kch};
     for (int k = 0; k < 5; k++) pick_shape(m, k, kcs[k], &m->shape[k][0], &m->shape[k][1]);
     m->lm_grid = m->sms * 32;  // argmax partial slots: an upper bound of the persistent grid
     TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * MR));
