@@ -35,8 +35,8 @@ namespace reng {
 // else straight from global memory (rows too long for shared memory; only
 // un-normalised inputs take that path).
 __device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, const uint16_t* xs, int xstride,
-                                            int K, int c, int g, int q) {
-    const int k = c * kChunkK + q * 8;
+                                            int K, int c, int h, int g, int q) {
+    const int k = c * kChunkK + h * 32 + q * 8;
     if (g >= a.M || k >= K) return make_uint4(0u, 0u, 0u, 0u);
     if (xs != nullptr) return *reinterpret_cast<const uint4*>(xs + g * xstride + k);
     return ldg_nc(a.x + (size_t)g * a.ldx + k);
@@ -110,22 +110,43 @@ __device__ __forceinline__ void x_fragment16(const GemvArgs& a, const uint16_t* 
 // and (2q+8, 2q+9) of the step in the mma's numbering), matched by the same
 // x values.
 template <int W8>
-__device__ __forceinline__ void block_mma(float (&acc)[4], const uint4& wa, const uint4& wb, const GemvArgs& a,
+__device__ __forceinline__ void block_mma(float (&acc)[4], const uint4 (&v)[4], const GemvArgs& a,
                                           const uint16_t* xs, int xstride, int K, int c, int g, int q) {
     if (!W8) {
-        const uint4 xf = x_fragment(a, xs, xstride, K, c, g, q);
-        mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xf.x, xf.y);
-        mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xf.z, xf.w);
+        // v: row g (k-half 0, 1), row g+8 (k-half 0, 1)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint4 xf = x_fragment(a, xs, xstride, K, c, h, g, q);
+            mma_bf16_16816(acc, v[h].x, v[2 + h].x, v[h].y, v[2 + h].y, xf.x, xf.y);
+            mma_bf16_16816(acc, v[h].z, v[2 + h].z, v[h].w, v[2 + h].w, xf.z, xf.w);
+        }
     } else {
+        // v[0]: 16 codes of row g, v[1]: of row g+8
         uint4 xl, xh;
         x_fragment16(a, xs, xstride, K, c, g, q, xl, xh);
-        const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb[4] = {wb.x, wb.y, wb.z, wb.w};
+        const uint32_t ra[4] = {v[0].x, v[0].y, v[0].z, v[0].w}, rb[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
         const uint32_t xv[8] = {xl.x, xl.y, xl.z, xl.w, xh.x, xh.y, xh.z, xh.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             mma_f16_16816(acc, e4m3x2_to_f16x2(ra[i] & 0xffffu), e4m3x2_to_f16x2(rb[i] & 0xffffu),
                           e4m3x2_to_f16x2(ra[i] >> 16), e4m3x2_to_f16x2(rb[i] >> 16), xv[2 * i], xv[2 * i + 1]);
         }
+    }
+}
+
+// Byte offsets, inside a block, of lane (g, q)'s 16-byte pieces in the order
+// block_mma takes them.
+template <int W8>
+__device__ __forceinline__ void lane_pieces(int g, int q, int lane, int (&off)[4]) {
+    if (!W8) {
+        off[0] = g * 128 + ((q ^ g) & 7) * 16;                 // row g, k 8q (chunk q)
+        off[1] = g * 128 + (((4 + q) ^ g) & 7) * 16;           // row g, k 32 + 8q (chunk 4 + q)
+        off[2] = 1024 + off[0];                               // row g + 8: same swizzle phase
+        off[3] = 1024 + off[1];
+    } else {
+        off[0] = lane * 16;
+        off[1] = 512 + lane * 16;
+        off[2] = off[3] = 0;
     }
 }
 
@@ -288,9 +309,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
 // Each warp walks a flat sequence of chunks (its k-range of a tile, tile
 // after tile of the CTA) so the stream never restarts at a tile boundary.
 //
-// PIPE_REG: the next chunk (kRegDepth blocks) is loaded into registers while
+// PIPE_REG: the next chunk (kChunkBytes of blocks) is loaded into registers while
 // the current one is multiplied.
-// PIPE_TMA: each warp owns a ring of kTmaStages stages of kTmaBlocks
+// PIPE_TMA: each warp owns a ring of kTmaStages stages of kChunkBytes of
 // contiguous packed blocks in shared memory, filled by one
 // cp.async.bulk (TMA) copy per stage and an mbarrier with the transaction
 // byte count; lane 0 refills a stage as soon as the warp has read it.  The
@@ -299,10 +320,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
 // records RENG_E_TIMEOUT in *a.err, stops issuing copies, drains its own
 // copies (again bounded) and finishes without waiting.
 enum { PIPE_REG = 0, PIPE_TMA = 1 };
-constexpr int kRegDepth = 4;
+constexpr int kChunkBytes = 4096;                             // weight bytes per pipeline chunk
 constexpr int kTmaStages = 4;
-constexpr int kTmaBlocks = 4;
-constexpr int kTmaRing = kTmaStages * kTmaBlocks * kBlockBytes;  // bytes per warp
+constexpr int kTmaRing = kTmaStages * kChunkBytes;           // bytes per warp
 constexpr unsigned long long kWaitNs = 2000000000ull;           // 2 s per wait
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -363,7 +383,11 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     const int g = lane >> 2, q = lane & 3;
     const int kc_per = (a.kc + NWARP - 1) / NWARP;
     const int c0 = min(a.kc, warp * kc_per), c1 = min(a.kc, c0 + kc_per);
-    constexpr int CB = PIPE == PIPE_TMA ? kTmaBlocks : kRegDepth;  // blocks per chunk
+    constexpr int BB = W8 ? kBlockBytesFp8 : kBlockBytesBf16;  // bytes per block
+    constexpr int CB = kChunkBytes / BB;                        // blocks per chunk
+    constexpr int NP = W8 ? 2 : 4;                              // 16-byte pieces per lane per block
+    int poff[4];
+    lane_pieces<W8>(g, q, lane, poff);
     const int nct = max(1, (c1 - c0 + CB - 1) / CB);
     const int ntile = blockIdx.x < a.tiles ? (a.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int nchunks = ntile * nct;
@@ -373,12 +397,12 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         const int tile = blockIdx.x + (j / nct) * gridDim.x;
         const int b0 = c0 + (j % nct) * CB;
         nb = max(0, min(CB, c1 - b0));
-        return a.w + ((size_t)tile * a.kc + b0) * kBlockBytes;
+        return a.w + ((size_t)tile * a.kc + b0) * BB;
     };
 
     // ---- start the weight stream (independent of the previous kernel) ----
-    uint4 ra[PIPE == PIPE_REG ? kRegDepth : 1], rb[PIPE == PIPE_REG ? kRegDepth : 1];
-    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem_dyn) + warp * gemv_ring_bytes<PIPE>();
+    uint4 rv[PIPE == PIPE_REG ? CB : 1][4];  // the chunk in flight (register pipeline)
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem_dyn) + warp * gemv_ring_bytes<PIPE>();  // per warp
     const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]) + warp * kTmaStages * 8;
     bool failed = false;
     int issued = 0;  // lane 0: chunks whose copy was issued
@@ -386,12 +410,12 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     auto rload = [&](int j) {
         if (j >= nchunks) return;
         int nb;
-        const uint8_t* src = chunk_src(j, nb) + lane * 16;
+        const uint8_t* src = chunk_src(j, nb);
 #pragma unroll
-        for (int b = 0; b < (PIPE == PIPE_REG ? kRegDepth : 1); b++)
+        for (int b = 0; b < (PIPE == PIPE_REG ? CB : 1); b++)
             if (b < nb) {
-                ra[b] = ldg_stream(src + b * kBlockBytes);
-                rb[b] = ldg_stream(src + b * kBlockBytes + 512);
+#pragma unroll
+                for (int p = 0; p < NP; p++) rv[b][p] = ldg_stream(src + b * BB + poff[p]);
             }
     };
     auto tma_issue = [&](int j) {  // lane 0 only
@@ -399,9 +423,9 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         int nb;
         const uint8_t* src = chunk_src(j, nb);
         const uint32_t bar = bar0 + (j % kTmaStages) * 8;
-        const uint32_t bytes = (uint32_t)nb * kBlockBytes;
+        const uint32_t bytes = (uint32_t)nb * BB;
         mbar_expect_tx(bar, bytes);
-        if (bytes) tma_load_1d(ring + (j % kTmaStages) * (kTmaBlocks * kBlockBytes), src, bytes, bar);
+        if (bytes) tma_load_1d(ring + (j % kTmaStages) * kChunkBytes, src, bytes, bar);
         issued = j + 1;
     };
     const uint32_t xbar_a = (uint32_t)__cvta_generic_to_shared(&xbar);
@@ -421,9 +445,9 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     } else {
         if (lane == 0 && nchunks > 0 && c1 > c0) {
             // the rest of this warp's first tile range into L2
-            const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * kBlockBytes;
+            const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * BB;
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p),
-                         "r"((uint32_t)(c1 - c0) * kBlockBytes)
+                         "r"((uint32_t)(c1 - c0) * BB)
                          : "memory");
         }
         rload(0);
@@ -488,13 +512,14 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
                     if (lane == 0) atomicExch(a.err, RENG_E_TIMEOUT);
                 }
             }
-            const uint32_t st = ring + (j % kTmaStages) * (kTmaBlocks * kBlockBytes) + lane * 16;
+            const uint32_t st = ring + (j % kTmaStages) * kChunkBytes;
 #pragma unroll
-            for (int b = 0; b < kTmaBlocks; b++)
+            for (int b = 0; b < CB; b++)
                 if (b0 + b < c1) {
-                    const uint4 wa = lds128(st + b * kBlockBytes);
-                    const uint4 wb = lds128(st + b * kBlockBytes + 512);
-                    block_mma<W8>(acc, wa, wb, a, xs, xstride, K, b0 + b, g, q);
+                    uint4 v[4];
+#pragma unroll
+                    for (int p = 0; p < NP; p++) v[p] = lds128(st + b * BB + poff[p]);
+                    block_mma<W8>(acc, v, a, xs, xstride, K, b0 + b, g, q);
                 }
             // the stage is read: let the async proxy refill it
             __syncwarp();
@@ -504,16 +529,15 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
             }
             __syncwarp();
         } else {
-            uint4 wa[kRegDepth], wb[kRegDepth];
+            uint4 cur[CB][4];
 #pragma unroll
-            for (int b = 0; b < kRegDepth; b++) {
-                wa[b] = ra[b];
-                wb[b] = rb[b];
-            }
+            for (int b = 0; b < CB; b++)
+#pragma unroll
+                for (int p = 0; p < NP; p++) cur[b][p] = rv[b][p];
             rload(j + 1);
 #pragma unroll
-            for (int b = 0; b < kRegDepth; b++)
-                if (b0 + b < c1) block_mma<W8>(acc, wa[b], wb[b], a, xs, xstride, K, b0 + b, g, q);
+            for (int b = 0; b < CB; b++)
+                if (b0 + b < c1) block_mma<W8>(acc, cur[b], a, xs, xstride, K, b0 + b, g, q);
         }
         if ((j % nct) != nct - 1) continue;
         // ---- a tile is complete: reduce the warps' k-slices on warp 0 ----
@@ -935,18 +959,18 @@ cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ pack --
-// One thread per (block, half, lane) 16-byte piece of the packed layout.
+// bf16 packing: one thread per 16-byte piece of a block: atom a, row r,
+// stored chunk position p holding logical chunk j = p ^ r (k = 64c + 8j).
 __global__ void k_pack(PackArgs a) {
-    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    const int64_t total = (int64_t)a.tiles * a.kc * 128;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int lane = (int)(i & 31), h = (int)((i >> 5) & 1);
-        const int64_t blk = i >> 6;
+        const int p = (int)(i & 7), r = (int)((i >> 3) & 7), at = (int)((i >> 6) & 1);
+        const int64_t blk = i >> 7;
         const int c = (int)(blk % a.kc);
         const int tile = (int)(blk / a.kc);
-        const int prow = tile * kTileRows + h * 8 + (lane >> 2);
-        const int srow = a.rowmap[prow];
-        const int k0 = c * kChunkK + (lane & 3) * 8;
+        const int srow = a.rowmap[tile * kTileRows + at * 8 + r];
+        const int k0 = c * kChunkK + ((p ^ r) & 7) * 8;
         uint16_t v[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
@@ -963,12 +987,12 @@ __global__ void k_pack(PackArgs a) {
         o.y = v[2] | ((uint32_t)v[3] << 16);
         o.z = v[4] | ((uint32_t)v[5] << 16);
         o.w = v[6] | ((uint32_t)v[7] << 16);
-        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytes + h * 512 + lane * 16) = o;
+        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytesBf16 + at * 1024 + r * 128 + p * 16) = o;
     }
 }
 
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st) {
-    const int64_t total = (int64_t)a.tiles * a.kc * 64;
+    const int64_t total = (int64_t)a.tiles * a.kc * 128;
     int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
     k_pack<<<grid, 256, 0, st>>>(a);
     return cudaGetLastError();
@@ -994,7 +1018,7 @@ __global__ void k_pack8(Pack8Args a) {
         o.y = v[4] | (v[5] << 8) | (v[6] << 16) | ((uint32_t)v[7] << 24);
         o.z = v[8] | (v[9] << 8) | (v[10] << 16) | ((uint32_t)v[11] << 24);
         o.w = v[12] | (v[13] << 8) | (v[14] << 16) | ((uint32_t)v[15] << 24);
-        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytes + h * 512 + lane * 16) = o;
+        *reinterpret_cast<uint4*>(a.dst + blk * kBlockBytesFp8 + h * 512 + lane * 16) = o;
     }
 }
 

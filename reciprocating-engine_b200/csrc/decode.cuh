@@ -4,12 +4,21 @@
 
 namespace reng {
 
-// Packed weight block: 16 rows x 32 k of bf16 = 1024 bytes.  Lane l of a
-// warp holds, in half h (rows 8h..8h+7), the 8 values of row 8h + l/4 at
-// k = 32c + 8*(l%4) .. +8, stored at byte h*512 + l*16 of block (tile, c).
+// Packed weights.  A block covers 16 rows x 64 k of a projection.
+//  * bf16 (2 KB): two 8-row atoms (rows 0-7, rows 8-15), each 8 rows x
+//    128 B with the 16-byte chunk j of row r stored at chunk position j ^ r
+//    (the K-major 128-byte-swizzle atom of the tcgen05 UMMA operand layout;
+//    the XOR also makes the GEMV's 16-byte fragment reads bank-conflict
+//    free).  The GEMV lane (g, q) multiplies row g and g+8 at
+//    k = 32h + 8q .. +8 for h = 0, 1.
+//  * FP8-E4M3 codes (1 KB): half h (512 B) holds rows 8h..8h+7; lane l's
+//    16 bytes (offset h*512 + l*16) are row 8h + l/4, k = 16(l%4) .. +16.
+// Block (tile, c) of a [tiles x kc] matrix starts at (tile * kc + c) * block
+// bytes; a warp's k-range of a tile is contiguous.
 constexpr int kTileRows = 16;
-constexpr int kChunkK = 32;
-constexpr int kBlockBytes = 1024;
+constexpr int kChunkK = 64;                 // k per block
+constexpr int kBlockBytesBf16 = 2048;
+constexpr int kBlockBytesFp8 = 1024;
 constexpr int kMaxRows = 8;  // activation rows per GEMV launch (mma N)
 constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
 

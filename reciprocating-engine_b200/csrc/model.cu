@@ -114,7 +114,7 @@ int pack(reng_model* m, uint8_t** out, const uint16_t* staged, const std::vector
          int K, float scale, int scale_rows, int* tiles_out) {
     const int tiles = (int)(rowmap.size() / kTileRows);
     const int kc = (K + kChunkK - 1) / kChunkK;
-    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytes));
+    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytesBf16));
     int* dmap = nullptr;
     CU(cudaMallocAsync((void**)&dmap, rowmap.size() * sizeof(int), m->st));
     CU(cudaMemcpyAsync(dmap, rowmap.data(), rowmap.size() * sizeof(int), cudaMemcpyHostToDevice, m->st));
@@ -143,8 +143,8 @@ int pack(reng_model* m, uint8_t** out, const uint16_t* staged, const std::vector
 int pack_fp8(reng_model* m, uint8_t** out, float** out_scales, const uint16_t* staged, int src_rows,
              const std::vector<int>& rowmap, int K, float scale, int scale_rows, int* tiles_out) {
     const int tiles = (int)(rowmap.size() / kTileRows);
-    const int kc = (K + 63) / 64;
-    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytes));
+    const int kc = (K + kChunkK - 1) / kChunkK;
+    TRY(dalloc(m, out, (size_t)tiles * kc * kBlockBytesFp8));
     TRY(dalloc(m, out_scales, (size_t)tiles * kTileRows));
     uint8_t* codes = nullptr;
     float* sc = nullptr;
@@ -192,13 +192,15 @@ int upload_f32(reng_model* m, float** out, const float* src, size_t n, int mem) 
 // Launch shape of a GEMV kind (0 qkv, 1 o_proj, 2 gate/up, 3 down, 4 LM
 // head) for few (M <= 2) and many activation rows: warps per CTA (4 or 8)
 // + 100 for the TMA weight ring (else the register pipeline).  Measured on
-// B200 (Llama-8B widths): the TMA ring with 4-warp CTAs streams qkv, gate/up
-// and the LM head fastest at batch 1 and 8-warp CTAs at batch 8; o_proj and
-// down_proj (few tiles, long K) prefer 8-warp register-pipeline CTAs.
+// B200 (Llama-8B widths, whole decode step in its CUDA graph): with every
+// kind on the 4-warp TMA ring the step is 3.36 ms against 3.91 ms when
+// o_proj/down use 8-warp register-pipeline CTAs, although those are as fast
+// alone: their registers keep the next kernel's CTAs from starting early,
+// which costs the programmatic-dependent-launch overlap.
 // RENG_GEMV_SHAPES="qkv,o,gu,down,lm" overrides both (a tuning knob).
 void pick_shape(reng_model* m, int kind, int kc, int* shape_small, int* shape_big) {
-    static const int small[5] = {104, 8, 104, 8, 104};
-    static const int big[5] = {108, 8, 108, 8, 108};
+    static const int small[5] = {104, 104, 104, 104, 104};
+    static const int big[5] = {108, 108, 108, 108, 108};
     int ss = small[kind], sb = big[kind];
     if (kc < 32) {  // short K: 8 warps would leave warps without blocks
         ss = ss >= 100 ? 104 : 4;
@@ -279,7 +281,10 @@ GemvArgs base_args(reng_model* m) {
 }
 
 // k-chunks of a K-wide projection: 32 bf16 or 64 FP8 codes per packed block
-int proj_kc(reng_model* m, int K) { return m->w8 ? (K + 63) / 64 : (K + kChunkK - 1) / kChunkK; }
+int proj_kc(reng_model* m, int K) {
+    (void)m;
+    return (K + kChunkK - 1) / kChunkK;  // 64 k per block in both formats
+}
 
 GemvArgs norm_args(reng_model* m, int M, const float* gain) {
     GemvArgs g = base_args(m);

@@ -91,9 +91,10 @@ def lib():
     """Load libreng_cuda.so once (raises OSError if it is not built)."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB):
-            raise OSError("libreng_cuda.so is not built (%s); run reng.build.build()" % LIB)
-        L = C.CDLL(LIB, mode=C.RTLD_GLOBAL)
+        path = os.environ.get("RENG_CUDA_LIB", LIB)  # another build of the library, for A/B runs
+        if not os.path.exists(path):
+            raise OSError("libreng_cuda.so is not built (%s); run reng.build.build()" % path)
+        L = C.CDLL(path, mode=C.RTLD_GLOBAL)
         for name, (args, res) in SIGNATURES.items():
             f = getattr(L, name)
             f.argtypes = args
