@@ -238,6 +238,22 @@ int reng_model_last_times(const reng_model *m, reng_step_times *t);
 #define RENG_KERNEL_KINDS 6
 int reng_model_time_kernels(reng_model *m, int iters, float *ms_out);
 
+/* ==================================================== packed GEMM ===
+ * y[m][r] = sum_k x[m][k] * w[r][k] (f32 out) through the tcgen05 GEMM the
+ * model runs for steps of more than 8 rows: w (bf16 [rows][K], row-major)
+ * is packed into the engine's swizzled 16 x 64 blocks, x (bf16 [M][K]) is
+ * read by the tensor-memory-accelerator copy, the accumulator lives in
+ * tensor memory.  Host buffers (mem RENG_MEM_HOST) or device buffers
+ * (RENG_MEM_DEVICE).  1 <= M <= 256, K % 8 == 0.  splits = K splits (0:
+ * the model's choice).  iters > 0: the kernel alone is also launched iters
+ * more times and *ms_out gets its mean duration (CUDA events).  The
+ * reference's projections are SynapseAI graph matmuls (reng-synapse
+ * src/model.rs:2960-3040); this entry exists so the kernel can be checked
+ * and timed on its own.
+ */
+int reng_gemm_bf16(const uint16_t *w, int rows, int K, const uint16_t *x, int M, float *y, int splits,
+                   int iters, float *ms_out, int mem);
+
 /* ============================================== tensor parallelism ===
  * Replaces hccl::Rank::join's unique-id exchange (hccl.rs:580-637): rank 0
  * creates the id, the caller ships it to the other ranks (a file, a store),

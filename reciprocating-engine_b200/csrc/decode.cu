@@ -205,8 +205,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
             s1 += __shfl_xor_sync(0xffffffffu, s1, o);
         }
         if (g == 0) {
-            if (m0 < a.M) a.ss_out[tile * kMaxRows + m0] = s0;
-            if (m1 < a.M) a.ss_out[tile * kMaxRows + m1] = s1;
+            if (m0 < a.M) a.ss_out[tile * kRowsCap + m0] = s0;
+            if (m1 < a.M) a.ss_out[tile * kRowsCap + m1] = s1;
         }
     } else if (EPI == EPI_F32) {
         const int r0 = tile * kTileRows + g, r1 = r0 + 8;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         for (int m = warp; m < a.M; m += NWARP) {
             float s = 0.0f;
 #pragma unroll 8
-            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kMaxRows + m];
+            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kRowsCap + m];
             s = warp_sum(s);
             if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
         }
@@ -941,7 +941,7 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
             for (int e = 0; e < 8; e++) ss += t[e] * t[e];
         }
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        if (i < nv && (i & 1) == 0) a.ss_out[(i >> 1) * kMaxRows + m] = ss;
+        if (i < nv && (i & 1) == 0) a.ss_out[(i >> 1) * kRowsCap + m] = ss;
     }
 }
 

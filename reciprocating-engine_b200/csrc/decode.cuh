@@ -19,7 +19,8 @@ constexpr int kTileRows = 16;
 constexpr int kChunkK = 64;                 // k per block
 constexpr int kBlockBytesBf16 = 2048;
 constexpr int kBlockBytesFp8 = 1024;
-constexpr int kMaxRows = 8;  // activation rows per GEMV launch (mma N)
+constexpr int kMaxRows = 8;    // activation rows per GEMV launch (mma N)
+constexpr int kRowsCap = 256;  // rows of a step (work buffers, RMS-partials stride)
 constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
 
 enum Epi : int {
@@ -55,7 +56,7 @@ struct GemvArgs {
                        // EPI_SWIGLU: act [M][ldo]; EPI_LOGITS: logits [M][ldo]
     float* out_f32;    // EPI_F32: [M][ldo]
     int ldo;
-    float* ss_out;     // EPI_RESID: norm partials [tiles][kMaxRows]
+    float* ss_out;     // EPI_RESID: norm partials [tiles][kRowsCap]
     const float* bias; // EPI_QKV: [q_dim + 2 kv_dim] (q part pre-scaled) or null
     // EPI_QKV
     int head_dim;
@@ -99,7 +100,7 @@ struct EmbedArgs {
     const uint16_t* table;  // [vocab][hidden]
     int hidden, vocab;
     uint16_t* x_res;        // [M][hidden]
-    float* ss_out;          // [hidden/16][kMaxRows]
+    float* ss_out;          // [hidden/16][kRowsCap]
     int* row_slot;
     int* row_pos;
     int mode;               // 0 decode: ids from ids_ring[step], rows = slots

@@ -1,0 +1,721 @@
+// tcgen05 / TMEM GEMM for steps with many activation rows (batch > 8 decode
+// and prefill blocks): Y[m, row] = sum_k X[m, k] * W[row, k] with the
+// weights as the MMA's A operand (M = 128 weight rows per CTA) and the
+// activation rows as its N (16..256), so a wide batch is one N dimension and
+// the weights stream from HBM once per step.
+//
+// Operands in shared memory use the K-major 128-byte-swizzle atom of the
+// UMMA descriptors (8 rows x 128 B, 16-byte chunk j of row r at j ^ r):
+//  * A (weights): the packed blocks are already that atom, so a stage is
+//    eight 2 KB bulk copies (one per 16-row tile of the 128-row super-tile);
+//  * B (activations, row-major [rows][K] bf16): a 2-D tensor-map copy with
+//    128-byte swizzle of a {64 k, N rows} box.
+// Both give SBO = 1024 B (one 8-row atom), and the K=16 steps inside a
+// 64-k stage advance the descriptor start address by 32 B.
+//
+// Roles (192 threads): warp 0 lane 0 issues the copies, warp 1 owns the TMEM
+// accumulator (128 lanes x N f32 columns) and lane 0 issues the MMAs and
+// commits each stage back to the producer; warps 2-5 read the accumulator
+// with tcgen05.ld (warp w reads TMEM lanes 32*(w%4) .. +32) and apply the
+// same epilogues as the GEMV kernels.  A weight matrix with few super-tiles
+// is split along K over several CTAs: each writes its partial tile to a
+// workspace and the last one sums the partials in split order
+// (deterministic) and runs the epilogue.  Every mbarrier wait is bounded.
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+
+namespace reng {
+
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kGemmStages = 4;
+constexpr int kStageA = 8 * kBlockBytesBf16;  // 128 rows x 64 k
+constexpr unsigned long long kGemmWaitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+    if (bar_try(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    while (!bar_try(bar, parity))
+        if (gtimer() - t0 > kGemmWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tensor_g2s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, SBO 1024 B.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next 8-row atom
+    d |= (uint64_t)1 << 46;             // descriptor version (sm100)
+    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor: f32 accumulate, bf16 A and B, both K-major, M=128.
+__device__ __forceinline__ uint32_t umma_idesc(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+}  // namespace
+
+// Epilogue of 16 activation columns (m = cb*16 .. +16) of one weight row
+// (packed row p of the matrix, TMEM lane `lr` of the super-tile).
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, int cb, const float (&v)[16],
+                                              float* am_v, int* am_i, int warp_e) {
+    const GemvArgs& a = g.e;
+    const int lane = lr & 31;
+    const int tile = p >> 4, i16 = p & 15;
+    // rows past the matrix (the last 16-row tile, the last 128-row CTA
+    // tile) are computed but never stored
+    const bool valid = tile < g.tiles16 && (EPI == EPI_SWIGLU || EPI == EPI_QKV || EPI == EPI_LOGITS || p < a.ldo);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int m = cb * 16 + j;
+        const bool live = valid && m < a.M;
+        if (EPI == EPI_RESID) {
+            float sq = 0.f;
+            if (live) {
+                uint16_t* o = a.out + (size_t)m * a.ldo + p;
+                const float x = round_bf16(bf16_bits_to_f32(*o) + round_bf16(v[j]));
+                *o = f32_to_bf16_bits(x);
+                sq = x * x;
+            }
+            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+            if (live && i16 == 0) a.ss_out[tile * kRowsCap + m] = sq;
+        } else if (EPI == EPI_F32) {
+            if (live) a.out_f32[(size_t)m * a.ldo + p] = v[j];
+        } else if (EPI == EPI_SWIGLU) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
+            if (live && i16 < 8) {
+                const float gt = v[j], up = partner;
+                a.out[(size_t)m * a.ldo + tile * 8 + i16] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
+            }
+        } else if (EPI == EPI_QKV) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
+            if (!live) continue;
+            const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;
+            const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
+            const int pos = a.row_pos[m];
+            if (pos >= a.cap) continue;
+            if (tile < a.q_tiles + a.k_tiles) {
+                const bool is_q = tile < a.q_tiles;
+                const int t = is_q ? tile : tile - a.q_tiles;
+                const int h = t / ppt, d = (t % ppt) * 8 + (i16 & 7), d2 = d + half;
+                const int brow = is_q ? h * hd : q_dim + h * hd;
+                const bool first = i16 < 8;
+                const float x1 = (first ? v[j] : partner) + (a.bias ? a.bias[brow + d] : 0.f);
+                const float x2 = (first ? partner : v[j]) + (a.bias ? a.bias[brow + d2] : 0.f);
+                const float* cs = a.rope_cos + (size_t)pos * hd;
+                const float* sn = a.rope_sin + (size_t)pos * hd;
+                const int dd = first ? d : d2;
+                const float y = first ? x1 * cs[d] - x2 * sn[d] : x2 * cs[d2] + x1 * sn[d2];
+                if (is_q) {
+                    a.out[(size_t)m * a.ldo + h * hd + dd] = f32_to_bf16_bits(y);
+                } else {
+                    const int slot = a.row_slot[m];
+                    a.kcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + dd] = f32_to_bf16_bits(y);
+                }
+            } else {
+                const int r = (tile - a.q_tiles - a.k_tiles) * kTileRows + i16;
+                const int h = r / hd, d = r % hd;
+                const int slot = a.row_slot[m];
+                const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
+                a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] = f32_to_bf16_bits(v[j] + b);
+            }
+        } else if (EPI == EPI_LOGITS) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            if (live && p < a.vocab) {
+                const uint16_t b = f32_to_bf16_bits(v[j]);
+                a.out[(size_t)m * a.ldo + p] = b;
+                bv = bf16_bits_to_f32(b);
+                bi = p;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                am_take2(bv, bi, ov, oi);
+            }
+            if (lane == 0) {
+                am_v[warp_e * kRowsCap + m] = bv;
+                am_i[warp_e * kRowsCap + m] = bi;
+            }
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmap_x, GemmArgs g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ __align__(8) unsigned long long full[kGemmStages], empty[kGemmStages], accum;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int s_flag;
+    __shared__ float am_v[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
+    __shared__ int am_i[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = blockIdx.x / g.ks, ksi = blockIdx.x % g.ks;
+    const int kper = (g.kc + g.ks - 1) / g.ks;
+    const int kb = min(g.kc, ksi * kper), ke = min(g.kc, kb + kper), nk = ke - kb;
+    const int N = g.N;
+    const uint32_t stage_bytes = kStageA + (uint32_t)N * 128u;
+    // 1024-byte alignment of the stage buffers (the swizzle atoms)
+    const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem_raw) + 1023u) & ~1023u;
+    const uint32_t bar_full = (uint32_t)__cvta_generic_to_shared(&full[0]);
+    const uint32_t bar_empty = (uint32_t)__cvta_generic_to_shared(&empty[0]);
+    const uint32_t bar_acc = (uint32_t)__cvta_generic_to_shared(&accum);
+    uint32_t ncols = 32;
+    while ((int)ncols < N) ncols <<= 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; s++) {
+            bar_init(bar_full + 8 * s, 1);
+            bar_init(bar_empty + 8 * s, 1);
+        }
+        bar_init(bar_acc, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_base_s);
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_s;
+    bool failed = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            auto issue_a = [&](int i) {
+                const int c = kb + i, s = i % kGemmStages;
+                const uint32_t dst = smem0 + (uint32_t)s * stage_bytes;
+                for (int t = 0; t < 8; t++) {
+                    const int tile = 8 * S + t;
+                    if (tile < g.tiles16)
+                        bulk_g2s(dst + t * kBlockBytesBf16, g.w + ((size_t)tile * g.kc + c) * kBlockBytesBf16,
+                                 kBlockBytesBf16, bar_full + 8 * s);
+                }
+            };
+            auto issue_b = [&](int i) {
+                const int c = kb + i, s = i % kGemmStages;
+                tensor_g2s(smem0 + (uint32_t)s * stage_bytes + kStageA, &tmap_x, c * kChunkK, 0, bar_full + 8 * s);
+            };
+            const int nt = min(8, g.tiles16 - 8 * S);
+            const uint32_t tx = (uint32_t)nt * kBlockBytesBf16 + (uint32_t)N * 128u;
+            const int pre = min(kGemmStages, nk);
+            // the weights do not depend on the previous kernel
+            for (int i = 0; i < pre; i++) {
+                bar_expect_tx(bar_full + 8 * (i % kGemmStages), tx);
+                issue_a(i);
+            }
+            pdl_wait();
+            for (int i = 0; i < pre; i++) issue_b(i);
+            issued = pre;
+            for (int i = pre; i < nk; i++) {
+                const int s = i % kGemmStages;
+                if (!bar_wait(bar_empty + 8 * s, (uint32_t)(((i / kGemmStages) - 1) & 1))) {
+                    failed = true;
+                    atomicExch(g.e.err, RENG_E_TIMEOUT);
+                    break;
+                }
+                bar_expect_tx(bar_full + 8 * s, tx);
+                issue_a(i);
+                issue_b(i);
+                issued = i + 1;
+            }
+            // drain: the last copy into each stage has landed before the CTA
+            // may exit (already true unless a wait gave up; bounded)
+            for (int i = max(0, issued - kGemmStages); i < issued; i++)
+                if (!bar_wait(bar_full + 8 * (i % kGemmStages), (uint32_t)((i / kGemmStages) & 1)))
+                    atomicExch(g.e.err, RENG_E_TIMEOUT);
+        } else {
+            pdl_wait();
+        }
+        pdl_launch();
+    } else if (warp == 1) {
+        pdl_wait();
+        pdl_launch();
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc(N);
+            int done = 0;
+            for (int i = 0; i < nk; i++) {
+                const int s = i % kGemmStages;
+                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / kGemmStages) & 1))) {
+                    atomicExch(g.e.err, RENG_E_TIMEOUT);
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a0 = smem0 + (uint32_t)s * stage_bytes, b0 = a0 + kStageA;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    umma(tmem, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(bar_empty + 8 * s);
+                done = i + 1;
+            }
+            // the commit fires when every MMA issued so far has finished
+            // (also after a wait gave up, so none still reads shared memory)
+            if (done > 0) umma_commit(bar_acc);
+            else bar_arrive(bar_acc);
+        }
+    } else {
+        // ---- epilogue warps 2..5 ----
+        pdl_wait();
+        pdl_launch();
+        const int q4 = warp & 3, warp_e = warp - 2;
+        const int lr = 32 * q4 + lane;       // TMEM lane = row of the super-tile
+        const int p = 128 * S + lr;          // packed row of the matrix
+        if (!bar_wait(bar_acc, 0)) {
+            failed = true;
+            if (lane == 0) atomicExch(g.e.err, RENG_E_TIMEOUT);
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t trow = tmem + ((uint32_t)(32 * q4) << 16);
+        // no MMA ran (empty split, or a wait gave up and *err is set): the
+        // accumulator was never written
+        const bool zero = nk == 0 || failed;
+        if (g.ks == 1) {
+            for (int cb = 0; cb < N / 16; cb++) {
+                float v[16];
+                tmem_ld16(trow + cb * 16, v);
+                if (zero)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = 0.f;
+                tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+            }
+        } else {
+            // split K: publish this split's partial, the last split sums them in order
+            float* wsS = g.ws + (size_t)S * g.ks * N * 128;
+            for (int cb = 0; cb < N / 16; cb++) {
+                float v[16];
+                tmem_ld16(trow + cb * 16, v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) wsS[((size_t)ksi * N + cb * 16 + j) * 128 + lr] = zero ? 0.f : v[j];
+            }
+            __threadfence();
+            named_sync_epilogue();
+            if (warp_e == 0 && lane == 0) s_flag = (atomicAdd(g.ws_count + S, 1u) == (unsigned)(g.ks - 1));
+            named_sync_epilogue();
+            if (s_flag) {
+                __threadfence();
+                for (int cb = 0; cb < N / 16; cb++) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        float acc = 0.f;
+                        for (int k = 0; k < g.ks; k++) acc += __ldcg(wsS + ((size_t)k * N + cb * 16 + j) * 128 + lr);
+                        v[j] = acc;
+                    }
+                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                }
+                if (warp_e == 0 && lane == 0) g.ws_count[S] = 0u;
+            }
+        }
+        if (EPI == EPI_LOGITS) {
+            // CTA partials of every row: best over the 4 epilogue warps
+            named_sync_epilogue();
+            const GemvArgs& a = g.e;
+            for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + m], am_i[w * kRowsCap + m]);
+                a.am_val[(size_t)blockIdx.x * kRowsCap + m] = bv;
+                a.am_idx[(size_t)blockIdx.x * kRowsCap + m] = bi;
+            }
+            __threadfence();
+            named_sync_epilogue();
+            if (threadIdx.x == 64) s_flag = (atomicAdd(a.am_count, 1u) == gridDim.x - 1);
+            named_sync_epilogue();
+            if (s_flag) {
+                __threadfence();
+                // a warp per row, lanes over the CTA partials
+                for (int m = warp_e; m < a.M; m += 4) {
+                    float bv = -INFINITY;
+                    int bi = 0x7fffffff;
+                    for (int b = lane; b < (int)gridDim.x; b += 32)
+                        am_take2(bv, bi, __ldcg(a.am_val + (size_t)b * kRowsCap + m),
+                                 __ldcg(a.am_idx + (size_t)b * kRowsCap + m));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                        am_take2(bv, bi, ov, oi);
+                    }
+                    if (lane == 0) am_i[m] = bi == 0x7fffffff ? 0 : bi;  // all NaN: index 0
+                }
+                named_sync_epilogue();
+                if (threadIdx.x == 64) {
+                    if (a.mode == 0) {
+                        const int s = *a.step;
+                        for (int m = 0; m < a.M; m++) {
+                            a.ids_ring[(size_t)(s + 1) * a.batch + m] = (uint32_t)am_i[m];
+                            a.pos[m] += 1;
+                        }
+                        *a.step = s + 1;
+                    } else {
+                        *a.next_id = (uint32_t)am_i[a.M - 1];
+                    }
+                    *a.am_count = 0u;
+                    __threadfence();
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    }
+}
+
+// ------------------------------------------------------------ host side --
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+}  // namespace
+
+// Tensor map of a row-major bf16 activation buffer [rows][K] read in
+// {64 k, n rows} boxes with 128-byte swizzle.
+int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (K % 8 || n % 16 || n < 16 || n > kRowsCap || n > rows || ((uintptr_t)x & 15))
+        return fail(RENG_E_INVAL, "gemm_tensor_map: bad shape");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)n};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)x, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return RENG_OK;
+}
+
+size_t gemm_smem_bytes(int n) { return (size_t)kGemmStages * (kStageA + (size_t)n * 128) + 1024; }
+
+template <int EPI>
+static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(g.super_tiles * g.ks);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, map, g);
+}
+
+template <int EPI>
+static cudaError_t prepare_t() {
+    return cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)gemm_smem_bytes(kRowsCap));
+}
+
+cudaError_t gemm_prepare() {
+    cudaError_t e = prepare_t<EPI_QKV>();
+    if (e == cudaSuccess) e = prepare_t<EPI_RESID>();
+    if (e == cudaSuccess) e = prepare_t<EPI_SWIGLU>();
+    if (e == cudaSuccess) e = prepare_t<EPI_LOGITS>();
+    if (e == cudaSuccess) e = prepare_t<EPI_F32>();
+    return e;
+}
+
+int gemm_blocks_per_sm(int epi, int n) {
+    int nb = 0;
+    const size_t smem = gemm_smem_bytes(n);
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (epi) {
+        case EPI_QKV: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_QKV>, kGemmThreads, smem); break;
+        case EPI_RESID: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_RESID>, kGemmThreads, smem); break;
+        case EPI_SWIGLU: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_SWIGLU>, kGemmThreads, smem); break;
+        case EPI_LOGITS: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_LOGITS>, kGemmThreads, smem); break;
+        default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_F32>, kGemmThreads, smem); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    return nb < 1 ? 1 : nb;
+}
+
+int gemm_pick_splits(int super_tiles, int kc, int resident, int epi) {
+    if (epi == EPI_LOGITS || super_tiles >= resident / 2) return 1;
+    int ks = resident / super_tiles;
+    ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
+    const int kper = (kc + ks - 1) / ks;
+    return (kc + kper - 1) / kper;  // every split gets at least one chunk
+}
+
+cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
+    if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
+        (epi == EPI_LOGITS && g.ks != 1) || (g.ks > 1 && (g.ws == nullptr || g.ws_count == nullptr)))
+        return cudaErrorInvalidValue;
+    switch (epi) {
+        case EPI_QKV: return launch_tc_t<EPI_QKV>(map, g, pdl, st);
+        case EPI_RESID: return launch_tc_t<EPI_RESID>(map, g, pdl, st);
+        case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(map, g, pdl, st);
+        case EPI_LOGITS: return launch_tc_t<EPI_LOGITS>(map, g, pdl, st);
+        case EPI_F32: return launch_tc_t<EPI_F32>(map, g, pdl, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// RMS-normalise M rows into a bf16 buffer (the x operand of the tcgen05
+// GEMMs): xn = bf16(x * 1/sqrt(sum_t ss[t][m] / H + eps) * gain).
+__global__ void __launch_bounds__(256) k_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles,
+                                                      const float* gain, float eps, int H, uint16_t* xn) {
+    const int m = blockIdx.x;
+    __shared__ float inv_s;
+    pdl_wait();
+    pdl_launch();
+    if (threadIdx.x < 32) {
+        float s = 0.f;
+        for (int t = threadIdx.x; t < ss_tiles; t += 32) s += ss[t * kRowsCap + m];
+        s = warp_sum(s);
+        if (threadIdx.x == 0) inv_s = 1.0f / sqrtf(s / (float)H + eps);
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)m * H + k);
+        const float4 g0 = *reinterpret_cast<const float4*>(gain + k);
+        const float4 g1 = *reinterpret_cast<const float4*>(gain + k + 4);
+        uint4 o;
+        o.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+        o.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+        o.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+        o.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+        *reinterpret_cast<uint4*>(xn + (size_t)m * H + k) = o;
+    }
+}
+
+cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps, int H,
+                                uint16_t* xn, int M, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_rmsnorm_rows, x, ss, ss_tiles, gain, eps, H, xn);
+}
+
+
+// ------------------------------------------------------ reng_gemm_bf16 --
+namespace {
+struct DevFree {
+    std::vector<void*> p;
+    ~DevFree() {
+        for (void* q : p) cudaFree(q);
+    }
+    template <typename T>
+    cudaError_t alloc(T** out, size_t bytes) {
+        cudaError_t e = cudaMalloc((void**)out, bytes < 16 ? 16 : bytes);
+        if (e == cudaSuccess) p.push_back(*out);
+        return e;
+    }
+};
+}  // namespace
+
+}  // namespace reng
+
+#define GEMM_CU(x)                                                                        \
+    do {                                                                                  \
+        cudaError_t e__ = (x);                                                            \
+        if (e__ != cudaSuccess)                                                           \
+            return reng::fail(RENG_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e__)); \
+    } while (0)
+
+extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t* x, int M, float* y, int splits,
+                              int iters, float* ms_out, int mem) {
+    using namespace reng;
+    RENG_CHECK_ARG(w && x && y, "reng_gemm_bf16: NULL buffer");
+    RENG_CHECK_ARG(rows >= 1 && K >= 8 && K % 8 == 0, "reng_gemm_bf16: rows >= 1 and K a positive multiple of 8");
+    RENG_CHECK_ARG(M >= 1 && M <= kRowsCap, "reng_gemm_bf16: M must be in [1, 256]");
+    RENG_CHECK_ARG(splits >= 0 && iters >= 0 && (iters == 0 || ms_out), "reng_gemm_bf16: bad splits / iters");
+    RENG_CHECK_ARG(mem == RENG_MEM_HOST || mem == RENG_MEM_DEVICE, "reng_gemm_bf16: bad mem");
+    const cudaMemcpyKind h2d = mem == RENG_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    const cudaMemcpyKind d2h = mem == RENG_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    int dev = 0;
+    GEMM_CU(cudaGetDevice(&dev));
+    GEMM_CU(gemm_prepare());
+    const int tiles = (rows + kTileRows - 1) / kTileRows, kc = (K + kChunkK - 1) / kChunkK;
+    const int N = (M + 15) / 16 * 16;
+    DevFree f;
+    uint16_t *wd = nullptr, *xd = nullptr;
+    uint8_t* packed = nullptr;
+    int* rowmap = nullptr;
+    float *yd = nullptr, *ws = nullptr;
+    unsigned int* cnt = nullptr;
+    int* err = nullptr;
+    GEMM_CU(f.alloc(&wd, (size_t)rows * K * 2));
+    GEMM_CU(f.alloc(&xd, (size_t)kRowsCap * K * 2));
+    GEMM_CU(f.alloc(&packed, (size_t)tiles * kc * kBlockBytesBf16));
+    GEMM_CU(f.alloc(&rowmap, (size_t)tiles * kTileRows * 4));
+    GEMM_CU(f.alloc(&yd, (size_t)M * rows * 4));
+    GEMM_CU(f.alloc(&err, 4));
+    GEMM_CU(cudaMemcpy(wd, w, (size_t)rows * K * 2, h2d));
+    GEMM_CU(cudaMemset(xd, 0, (size_t)kRowsCap * K * 2));
+    GEMM_CU(cudaMemcpy(xd, x, (size_t)M * K * 2, h2d));
+    GEMM_CU(cudaMemset(err, 0, 4));
+    std::vector<int> map((size_t)tiles * kTileRows, -1);
+    for (int r = 0; r < rows; r++) map[r] = r;
+    GEMM_CU(cudaMemcpy(rowmap, map.data(), map.size() * 4, cudaMemcpyHostToDevice));
+    PackArgs pa{};
+    pa.src = wd;
+    pa.ld = K;
+    pa.rowmap = rowmap;
+    pa.tiles = tiles;
+    pa.K = K;
+    pa.kc = kc;
+    pa.dst = packed;
+    GEMM_CU(launch_pack(pa, 0));
+
+    GemmArgs g{};
+    g.e.M = M;
+    g.e.K = K;
+    g.e.kc = kc;
+    g.e.tiles = tiles;
+    g.e.out_f32 = yd;
+    g.e.ldo = rows;
+    g.e.err = err;
+    g.w = packed;
+    g.tiles16 = tiles;
+    g.kc = kc;
+    g.super_tiles = (tiles + 7) / 8;
+    g.N = N;
+    const int resident = num_sms(dev) * gemm_blocks_per_sm(EPI_F32, N);
+    if (splits == 0) {
+        g.ks = gemm_pick_splits(g.super_tiles, kc, resident, EPI_F32);
+    } else {
+        const int s = splits > kc ? kc : splits;
+        const int kper = (kc + s - 1) / s;
+        g.ks = (kc + kper - 1) / kper;
+    }
+    if (g.ks > 1) {
+        GEMM_CU(f.alloc(&ws, (size_t)g.super_tiles * g.ks * N * 128 * 4));
+        GEMM_CU(f.alloc(&cnt, (size_t)g.super_tiles * 4));
+        GEMM_CU(cudaMemset(cnt, 0, (size_t)g.super_tiles * 4));
+    }
+    g.ws = ws;
+    g.ws_count = cnt;
+    CUtensorMap tmap;
+    const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);
+    if (rc) return rc;
+    GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
+    GEMM_CU(cudaDeviceSynchronize());
+    if (iters > 0) {
+        cudaEvent_t e0, e1;
+        GEMM_CU(cudaEventCreate(&e0));
+        GEMM_CU(cudaEventCreate(&e1));
+        GEMM_CU(cudaEventRecord(e0, 0));
+        for (int i = 0; i < iters; i++) GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
+        GEMM_CU(cudaEventRecord(e1, 0));
+        GEMM_CU(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        *ms_out = ms / (float)iters;
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    int herr = 0;
+    GEMM_CU(cudaMemcpy(&herr, err, 4, cudaMemcpyDeviceToHost));
+    if (herr) return fail(herr, "reng_gemm_bf16: the kernel gave up on a bounded wait");
+    GEMM_CU(cudaMemcpy(y, yd, (size_t)M * rows * 4, d2h));
+    return RENG_OK;
+}

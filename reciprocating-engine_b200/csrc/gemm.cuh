@@ -1,0 +1,41 @@
+// Interfaces of the tcgen05 GEMM path (gemm.cu): projections of steps with
+// more activation rows than the GEMV's mma N (batch > 8 decode, prefill).
+#pragma once
+#include <cuda.h>
+
+#include "decode.cuh"
+
+namespace reng {
+
+constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
+
+struct GemmArgs {
+    GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
+    const uint8_t* w;         // packed bf16 blocks [tiles16][kc]
+    int tiles16;              // 16-row tiles of the matrix
+    int kc;                   // 64-k chunks
+    int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
+    int ks;                   // K splits (every split gets >= 1 chunk)
+    int N;                    // MMA N: activation rows rounded up to 16 (16..256)
+    float* ws;                // split-K partials [super_tiles][ks][N][128]
+    unsigned int* ws_count;   // [super_tiles] arrivals, reset by the last split
+};
+
+// Tensor map of a row-major bf16 activation buffer [rows][K] read as
+// {64 k, n rows} boxes with the 128-byte swizzle; k >= K reads zeros.
+int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out);
+size_t gemm_smem_bytes(int n);
+// Raise the dynamic shared-memory limit of every GEMM instantiation to the
+// n = kRowsCap size (call once per device before capture).
+cudaError_t gemm_prepare();
+// Resident CTAs per SM of a GEMM launch with MMA width n.
+int gemm_blocks_per_sm(int epi, int n);
+// K splits for a matrix of `super_tiles` x `kc` so that the launch fills
+// `resident` CTA slots (1 for the LM head: its argmax needs whole rows).
+int gemm_pick_splits(int super_tiles, int kc, int resident, int epi);
+cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st);
+// xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.
+cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps,
+                                int H, uint16_t* xn, int M, bool pdl, cudaStream_t st);
+
+}  // namespace reng

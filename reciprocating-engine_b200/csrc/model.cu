@@ -11,7 +11,7 @@
 #include <string>
 #include <vector>
 
-#include "decode.cuh"
+#include "gemm.cuh"
 
 using namespace reng;
 
@@ -47,8 +47,15 @@ struct reng_model {
     size_t layer_kv = 0;  // elements per layer
     // work buffers
     uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+    uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
+    float* ws = nullptr;             // GEMM split-K partials
+    size_t ws_floats = 0;
+    unsigned int* ws_count = nullptr;
+    int ws_tiles = 0;                // super-tiles ws_count covers
+    int gemm_occ[5][kRowsCap / 16 + 1] = {};  // resident GEMM CTAs per SM by (epilogue, N/16)
+    int launches = 0;                // kernels of this library enqueued so far
     float* ss = nullptr;
-    float* part = nullptr;  // tensor-parallel f32 partials [kMaxRows][hidden]
+    float* part = nullptr;  // tensor-parallel f32 partials [kRowsCap][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
     int* err = nullptr;  // device error word of the bounded waits
     int w8 = 0;          // projections held as FP8-E4M3 codes + row scales
@@ -63,7 +70,7 @@ struct reng_model {
     cudaGraphExec_t graph = nullptr;
     int kernels_per_step = 0;
     std::vector<int> host_pos;
-    uint32_t* pinned = nullptr;  // small pinned staging
+    uint32_t* pinned = nullptr;  // pinned staging: ids [kRowsCap], positions [kRowsCap], error word
     size_t bytes = 0;
     std::vector<void*> allocs;
     reng_step_times times{};
@@ -73,6 +80,11 @@ struct reng_model {
 };
 
 namespace {
+
+// pinned staging words: ids [0, kRowsCap), positions, the device error word
+constexpr int kPinnedPos = kRowsCap;
+constexpr int kPinnedErr = 2 * kRowsCap;
+constexpr int kPinnedWords = 2 * kRowsCap + 16;
 
 template <typename T>
 int dalloc(reng_model* m, T** p, size_t count) {
@@ -246,9 +258,12 @@ int validate(const reng_model_desc* d) {
     RENG_CHECK_ARG(std::isfinite(d->eps) && d->eps >= 0.f && std::isfinite(d->attn_scale),
                    "reng_model_create: eps / attn_scale not finite");
     RENG_CHECK_ARG(d->capacity <= (1 << 20), "reng_model_create: capacity above 1048576 positions");
-    if (d->batch > kMaxRows)
-        return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) +
-                                            " above " + std::to_string(kMaxRows) + " is not built yet");
+    if (d->weights == RENG_WEIGHTS_FP8_E4M3 && d->batch > kMaxRows)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights run batch <= " + std::to_string(kMaxRows) +
+                                            ", not " + std::to_string(d->batch));
+    if (d->batch > kRowsCap)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) + " above " +
+                                            std::to_string(kRowsCap));
     return RENG_OK;
 }
 
@@ -271,6 +286,7 @@ int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
     e.slot = slot;
     e.batch = m->B;
     CU(launch_embed(e, true, st));
+    m->launches++;
     return RENG_OK;
 }
 
@@ -303,6 +319,54 @@ GemvArgs norm_args(reng_model* m, int M, const float* gain) {
     return g;
 }
 
+// Rows of a step above which projections run on the tcgen05 GEMM (bf16
+// weights); at or below it the GEMV kernels (mma N = kMaxRows) stream the
+// weights with the rows in registers.
+bool use_gemm(const reng_model* m, int M) { return !m->w8 && M > kMaxRows; }
+
+int gemm_occupancy(reng_model* m, int epi, int n) {
+    int& v = m->gemm_occ[epi][n / 16];
+    if (v == 0) v = gemm_blocks_per_sm(epi, n);
+    return v;
+}
+
+// One projection: the GEMV for few rows, else (RMSNorm of x into xn when the
+// projection normalises its input) the tcgen05 GEMM over N = M rounded up
+// to 16 columns.  kind indexes the GEMV launch shapes.
+int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cudaStream_t st) {
+    if (!use_gemm(m, g.M)) {
+        CU(launch_gemv(g, epi, m->shape[kind][g.M > 2], max_grid, true, st));
+        m->launches++;
+        return RENG_OK;
+    }
+    const uint16_t* x = g.x;
+    if (g.ss_in != nullptr) {
+        CU(launch_rmsnorm_rows(g.x, g.ss_in, g.ss_tiles, g.gain, g.eps, g.norm_k, m->xn, g.M, true, st));
+        m->launches++;
+        x = m->xn;
+    }
+    const int N = (g.M + 15) / 16 * 16;
+    CUtensorMap map;
+    TRY(gemm_tensor_map(x, kRowsCap, g.K, N, &map));
+    GemmArgs a{};
+    a.e = g;
+    a.w = g.w;
+    a.tiles16 = g.tiles;
+    a.kc = g.kc;
+    a.super_tiles = (g.tiles + 7) / 8;
+    a.N = N;
+    a.ks = gemm_pick_splits(a.super_tiles, g.kc, m->sms * gemm_occupancy(m, epi, N), epi);
+    a.ws = m->ws;
+    a.ws_count = m->ws_count;
+    if (a.ks > 1 && ((size_t)a.super_tiles * a.ks * N * 128 > m->ws_floats || a.super_tiles > m->ws_tiles))
+        return fail(RENG_E_STATE, "GEMM split-K workspace too small");
+    if (epi == EPI_LOGITS && (size_t)a.super_tiles > (size_t)m->lm_grid)
+        return fail(RENG_E_STATE, "LM head argmax partials too small");
+    CU(launch_gemm_tc(map, a, epi, true, st));
+    m->launches++;
+    return RENG_OK;
+}
+
 int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     const LayerDev& w = m->layers[l];
     GemvArgs g = norm_args(m, M, w.g1);
@@ -323,8 +387,7 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     g.kcache = m->kcache + (size_t)l * m->layer_kv;
     g.vcache = m->vcache + (size_t)l * m->layer_kv;
     g.cap = m->cap;
-    CU(launch_gemv(g, EPI_QKV, m->shape[0][M > 2], 0, true, st));
-    return RENG_OK;
+    return linear(m, g, EPI_QKV, 0, 0, st);
 }
 
 int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
@@ -341,12 +404,13 @@ int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
     at.hd = m->hd;
     at.cap = m->cap;
     CU(launch_attn(at, kAttnChunk, true, st));
+    m->launches++;
     return RENG_OK;
 }
 
 // o_proj (which == 0) or down_proj (which == 1) with the residual add; under
 // tensor parallelism the f32 partial, the all-reduce and the residual kernel.
-int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* extra) {
+int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
     const LayerDev& w = m->layers[l];
     GemvArgs o = base_args(m);
     o.M = M;
@@ -362,14 +426,14 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st, int* 
     o.ldo = m->hidden;
     o.ss_out = m->ss;
     o.out_f32 = m->part;
-    const int nw = m->shape[which == 0 ? 1 : 3][M > 2], gr = 0;
+    const int kind = which == 0 ? 1 : 3;
     if (m->world > 1) {
-        CU(launch_gemv(o, EPI_F32, nw, gr, true, st));
+        TRY(linear(m, o, EPI_F32, kind, 0, st));
         CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, st));
         CU(launch_tp_residual(m, m->part, M, false, st));
-        if (extra) *extra += 2;
+        m->launches++;
     } else {
-        CU(launch_gemv(o, EPI_RESID, nw, gr, true, st));
+        TRY(linear(m, o, EPI_RESID, kind, 0, st));
     }
     return RENG_OK;
 }
@@ -384,12 +448,14 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
     u.tiles = m->gu_tiles;
     u.out = m->act;
     u.ldo = m->inter;
-    CU(launch_gemv(u, EPI_SWIGLU, m->shape[2][M > 2], 0, true, st));
-    return RENG_OK;
+    return linear(m, u, EPI_SWIGLU, 2, 0, st);
 }
 
-int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
+// LM head over rows [r0, r0 + M) of the step (logits and argmax rows 0..M-1).
+int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int r0 = 0) {
     GemvArgs h = norm_args(m, M, m->final_gamma);
+    h.x = m->x_res + (size_t)r0 * m->hidden;
+    h.ss_in = m->ss + r0;
     h.w = m->lm;
     h.tiles = m->lm_tiles;
     h.out = m->logits;
@@ -405,37 +471,34 @@ int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
     h.step = m->step;
     h.ids_ring = m->ids_ring;
     h.next_id = m->next_id;
-    CU(launch_gemv(h, EPI_LOGITS, m->shape[4][M > 2], m->lm_grid, true, st));
-    return RENG_OK;
+    return linear(m, h, EPI_LOGITS, 4, m->lm_grid, st);
 }
 
 // The kernels of one step.  mode 0: decode over the B slots (rows = slots,
 // ids from the device ring).  mode 1: prefill of `M` ids of slot `slot`
-// starting at the device position of that slot; `head` runs the LM head.
-int enqueue_step(reng_model* m, int mode, int M, int slot, bool head, cudaStream_t st, int* nk) {
-    int kernels = 0;
+// starting at the device position of that slot.  head: HEAD_NONE, HEAD_LAST
+// (the LM head on the last row only: its logits land in row 0) or HEAD_ALL.
+enum { HEAD_NONE = 0, HEAD_LAST = 1, HEAD_ALL = 2 };
+int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_t st, int* nk) {
+    const int before = m->launches;
     TRY(k_embed_launch(m, mode, M, slot, st));
-    kernels++;
     for (int l = 0; l < m->L; l++) {
         TRY(k_qkv_launch(m, l, M, st));
         TRY(k_attn_launch(m, l, M, st));
-        TRY(k_proj_launch(m, l, M, 0, st, &kernels));
+        TRY(k_proj_launch(m, l, M, 0, st));
         TRY(k_gateup_launch(m, l, M, st));
-        TRY(k_proj_launch(m, l, M, 1, st, &kernels));
-        kernels += 5;
+        TRY(k_proj_launch(m, l, M, 1, st));
     }
-    if (head) {
-        TRY(k_head_launch(m, mode, M, slot, st));
-        kernels++;
-    }
-    if (nk) *nk = kernels;
+    if (head == HEAD_ALL) TRY(k_head_launch(m, mode, M, slot, st));
+    else if (head == HEAD_LAST) TRY(k_head_launch(m, mode, 1, slot, st, M - 1));
+    if (nk) *nk = m->launches - before;
     return RENG_OK;
 }
 
 int build_graph(reng_model* m) {
     cudaGraph_t g = nullptr;
     CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, 0, m->B, 0, true, m->st, &m->kernels_per_step);
+    int rc = enqueue_step(m, 0, m->B, 0, HEAD_ALL, m->st, &m->kernels_per_step);
     cudaError_t e = cudaStreamEndCapture(m->st, &g);
     if (rc) {
         if (g) cudaGraphDestroy(g);
@@ -470,6 +533,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
     m->sms = num_sms(m->dev);
     CU(gemv_prepare());
+    CU(gemm_prepare());
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;
@@ -597,9 +661,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->vcache, m->layer_kv * m->L));
     CU(cudaMemsetAsync(m->kcache, 0, m->layer_kv * m->L * 2, m->st));
     CU(cudaMemsetAsync(m->vcache, 0, m->layer_kv * m->L * 2, m->st));
-    const int MR = kMaxRows;
+    const int MR = kRowsCap;
     TRY(dalloc(m, &m->x_res, (size_t)MR * H));
     TRY(dalloc(m, &m->qbuf, (size_t)MR * m->q_dim));
+    TRY(dalloc(m, &m->xn, (size_t)MR * H));
     TRY(dalloc(m, &m->attn, (size_t)MR * m->q_dim));
     TRY(dalloc(m, &m->act, (size_t)MR * m->inter));
     TRY(dalloc(m, &m->logits, (size_t)MR * m->vocab));
@@ -628,11 +693,37 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
-    CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * 64));
+    if (!m->w8) {
+        // split-K partials: a split launch fills at most the resident CTA slots
+        // (sms x CTAs per SM <= 2 x sms at N <= 64, fewer above)
+        const int max_tiles = std::max({m->qkv_tiles, m->o_tiles, m->gu_tiles, m->d_tiles, m->lm_tiles});
+        m->ws_tiles = (max_tiles + 7) / 8;
+        size_t most = 0;
+        for (int n = 16; n <= kRowsCap; n += 16)
+            for (int epi = 0; epi < 5; epi++)
+                most = std::max(most, (size_t)m->sms * gemm_occupancy(m, epi, n) * n * 128);
+        m->ws_floats = most;
+        TRY(dalloc(m, &m->ws, m->ws_floats));
+        TRY(dalloc(m, &m->ws_count, (size_t)m->ws_tiles));
+        CU(cudaMemsetAsync(m->ws_count, 0, (size_t)m->ws_tiles * 4, m->st));
+    }
+    CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
     m->host_pos.assign(m->B, 0);
     CU(cudaStreamSynchronize(m->st));
     TRY(build_graph(m));
     return RENG_OK;
+}
+
+// Prompt rows per prefill block: kRowsCap on the GEMM path (bf16), the GEMV
+// width for FP8 weights; RENG_PREFILL_ROWS lowers it (a tuning knob).
+int prefill_rows(const reng_model* m) {
+    int r = m->w8 ? kMaxRows : kRowsCap;
+    const char* v = getenv("RENG_PREFILL_ROWS");
+    if (v) {
+        const int x = atoi(v);
+        if (x >= 1 && x < r) r = x;
+    }
+    return r;
 }
 
 int check_model(const reng_model* m) {
@@ -641,9 +732,9 @@ int check_model(const reng_model* m) {
 }
 
 int sync_pos(reng_model* m) {
-    for (int b = 0; b < m->B; b++) reinterpret_cast<int*>(m->pinned)[b % 64] = m->host_pos[b];
-    // B <= kMaxRows <= 64
-    CU(cudaMemcpyAsync(m->pos, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
+    int* hp = reinterpret_cast<int*>(m->pinned) + kPinnedPos;
+    for (int b = 0; b < m->B; b++) hp[b] = m->host_pos[b];
+    CU(cudaMemcpyAsync(m->pos, hp, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
     CU(cudaStreamSynchronize(m->st));
     return RENG_OK;
 }
@@ -651,7 +742,7 @@ int sync_pos(reng_model* m) {
 // The device error word of the bounded waits: RENG_E_TIMEOUT if a kernel
 // gave up on a wait (its results are then invalid).  Synchronises.
 int check_device_error(reng_model* m) {
-    int* h = reinterpret_cast<int*>(m->pinned) + 63;
+    int* h = reinterpret_cast<int*>(m->pinned) + kPinnedErr;
     CU(cudaMemcpyAsync(h, m->err, 4, cudaMemcpyDeviceToHost, m->st));
     CU(cudaStreamSynchronize(m->st));
     if (*h != 0) {
@@ -712,13 +803,15 @@ extern "C" int reng_model_prefill(reng_model* m, int slot, const uint32_t* ids, 
                                                         " out of range");
     CU(cudaSetDevice(m->dev));
     std::vector<uint16_t> hl;
-    for (int b0 = 0; b0 < n; b0 += kMaxRows) {
-        const int M = std::min(kMaxRows, n - b0);
+    const int block = prefill_rows(m);
+    for (int b0 = 0; b0 < n; b0 += block) {
+        const int M = std::min(block, n - b0);
         const bool last = b0 + M == n;
         memcpy(m->pinned, ids + b0, (size_t)M * 4);
         CU(cudaMemcpyAsync(m->prefill_ids, m->pinned, (size_t)M * 4, cudaMemcpyHostToDevice, m->st));
         // positions of this block: pos[slot] on the device is the block base
-        TRY(enqueue_step(m, 1, M, slot, last || all_logits != nullptr, m->st, nullptr));
+        const int head = all_logits ? HEAD_ALL : (last ? HEAD_LAST : HEAD_NONE);
+        TRY(enqueue_step(m, 1, M, slot, head, m->st, nullptr));
         m->host_pos[slot] += M;
         TRY(sync_pos(m));  // also orders the pinned buffer reuse
         if (all_logits) {
@@ -729,7 +822,8 @@ extern "C" int reng_model_prefill(reng_model* m, int slot, const uint32_t* ids, 
         if (last) {
             if (last_logits) {
                 hl.resize((size_t)m->vocab);
-                CU(cudaMemcpy(hl.data(), m->logits + (size_t)(M - 1) * m->vocab, (size_t)m->vocab * 2,
+                const size_t row = head == HEAD_ALL ? (size_t)(M - 1) : 0;
+                CU(cudaMemcpy(hl.data(), m->logits + row * m->vocab, (size_t)m->vocab * 2,
                               cudaMemcpyDeviceToHost));
                 bf16_to_f32_host(hl.data(), last_logits, m->vocab);
             }
@@ -869,9 +963,9 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
                 switch (kind) {
                     case 0: TRY(k_qkv_launch(m, l, M, m->st)); break;
                     case 1: TRY(k_attn_launch(m, l, M, m->st)); break;
-                    case 2: TRY(k_proj_launch(m, l, M, 0, m->st, nullptr)); break;
+                    case 2: TRY(k_proj_launch(m, l, M, 0, m->st)); break;
                     case 3: TRY(k_gateup_launch(m, l, M, m->st)); break;
-                    case 4: TRY(k_proj_launch(m, l, M, 1, m->st, nullptr)); break;
+                    case 4: TRY(k_proj_launch(m, l, M, 1, m->st)); break;
                     default: TRY(k_head_launch(m, 1, M, 0, m->st)); break;
                 }
             }

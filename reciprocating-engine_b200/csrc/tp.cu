@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) k_tp_residual(uint16_t* x_res, const floa
             *xp = o;
         }
         s += __shfl_xor_sync(0xffffffffu, s, 1);
-        if (i < nv && (i & 1) == 0) ss[(i >> 1) * kMaxRows + m] = s;
+        if (i < nv && (i & 1) == 0) ss[(i >> 1) * kRowsCap + m] = s;
     }
 }
 
