@@ -194,7 +194,7 @@ def run_ours(args, cfg):
 
     w = random_weights(cfg, seed=args.seed, device=dev)
     torch.cuda.synchronize()
-    cap = args.prompt + args.warmup + 2 * args.steps + 8
+    cap = max(args.prompt + args.warmup + 2 * args.steps + 8, args.prefill)
     fp8 = ("e4m3", "pcs") if args.weights == "fp8" else None
     eng = Engine(cfg, w, batch=args.batch, capacity=cap, device=local, tp_rank=rank,
                  tp_world=ws, nccl_id=nccl_id, fp8=fp8)
@@ -256,6 +256,25 @@ def run_ours(args, cfg):
     eng.decode(seeds, args.steps // 2)
     kt = eng.time_kernels(iters=max(32, cfg.num_hidden_layers))
     kpl = eng.last_times().kernels_per_step
+    # ---- prefill of a long prompt through the C ABI (host ids in, next id out) ----
+    pf = None
+    if args.prefill > 0:
+        long_prompt = prompt_ids(args.prefill, cfg.vocab_size, seed=args.seed + 1)
+        runs = []
+        for i in range(3):
+            eng.reset(0)
+            if ws > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            eng.prefill(0, long_prompt)
+            runs.append(time.perf_counter() - t0)
+        tp_ = torch.tensor([statistics.median(runs[1:])], dtype=torch.float64, device=dev)
+        if ws > 1:
+            dist.all_reduce(tp_, op=dist.ReduceOp.MAX)
+        pf_s = float(tp_.item())
+        pf = {"tokens": args.prefill, "tok_s": args.prefill / pf_s, "ms": pf_s * 1e3,
+              "timing": "wall clock around reng_model_prefill (median of 2 after 1 warm-up), max over ranks"}
 
     if rank == 0:
         tokens = args.steps * B
@@ -293,7 +312,9 @@ def run_ours(args, cfg):
             "e2e": {"value": tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B / args.steps,
                     "d2h_bytes_per_step": 4 * B, "ids_equal_device_run": same},
             "gpu_launches": kpl * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "gemv<SWIGLU> gate/up (layer-cycled)",
+            "roofline": {"bound": "hbm", "kernel": ("gemv<SWIGLU> gate/up" if B <= 8 or args.weights == "fp8"
+                                                    else "rmsnorm rows + tcgen05 gemm<SWIGLU> gate/up")
+                         + " (layer-cycled)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": None, "bytes_per_launch": gu_bytes},
@@ -302,6 +323,8 @@ def run_ours(args, cfg):
                               "frac_of_8tbs_spec": step_gbs / 8000.0},
             "kernel_ms": kt,
         }
+        if pf is not None:
+            line["prefill"] = pf
         if not args.no_cpu and ws == 1:
             v, cores, sample = cpu_sample(cfg, tokens=args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
@@ -359,6 +382,8 @@ def main():
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
                     help="fp8: projections quantized E4M3 per channel at load (config 3)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--prefill", type=int, default=1024,
+                    help="also time a prefill of this many prompt tokens (0: skip)")
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fp8", dest="fp8", action="store_false",

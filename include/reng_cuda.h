@@ -238,6 +238,21 @@ int reng_model_last_times(const reng_model *m, reng_step_times *t);
 #define RENG_KERNEL_KINDS 6
 int reng_model_time_kernels(reng_model *m, int iters, float *ms_out);
 
+/* Phase timeline of one decode step of the persistent step kernel (the
+ * models it runs: one CUDA-graph node per step).  Runs one step from the
+ * slots' current state (the ids of the last decode call's first step) and
+ * writes, per phase p < *n_phases (at most max_phases), out[5p] = when the
+ * barrier before phase p released (CTA 0's view), out[5p+1] / out[5p+2] =
+ * the earliest / latest CTA arrival at the barrier after it, out[5p+3] /
+ * out[5p+4] = for a projection phase, when CTA 0 had its x rows staged and
+ * when its last warp left the weight loop (0 otherwise), in ns from the
+ * kernel's start.  Phases: embedding, then per layer q/k/v, attention,
+ * o_proj, gate/up, down_proj, then the LM head.  RENG_E_STATE when the model
+ * runs per-projection kernels.  Advances every slot by one position.  The
+ * reference profiles through SynapseAI traces (tools/profile/README.md).
+ */
+int reng_model_trace_step(reng_model *m, uint64_t *out, int max_phases, int *n_phases);
+
 /* ==================================================== packed GEMM ===
  * y[m][r] = sum_k x[m][k] * w[r][k] (f32 out) through the tcgen05 GEMM the
  * model runs for steps of more than 8 rows: w (bf16 [rows][K], row-major)

@@ -24,345 +24,14 @@
 
 #include <cooperative_groups.h>
 
-#include "decode.cuh"
+#include "gemv_core.cuh"
 
 namespace reng {
 
 // ------------------------------------------------------------------ GEMV --
 
-// The x fragment of lane (g, q) for k-chunk c: row g, k = 32c + 8q .. +8,
-// as 4 u32 of packed bf16.  From the CTA's shared copy when it was staged,
-// else straight from global memory (rows too long for shared memory; only
-// un-normalised inputs take that path).
-__device__ __forceinline__ uint4 x_fragment(const GemvArgs& a, const uint16_t* xs, int xstride,
-                                            int K, int c, int h, int g, int q) {
-    const int k = c * kChunkK + h * 32 + q * 8;
-    if (g >= a.M || k >= K) return make_uint4(0u, 0u, 0u, 0u);
-    if (xs != nullptr) return *reinterpret_cast<const uint4*>(xs + g * xstride + k);
-    return ldg_nc(a.x + (size_t)g * a.ldx + k);
-}
-
-// RMS-normalise the staged x rows in place: x' = bf16(x * inv[m] * gain[k])
-// (f16 for the FP8-weight kernels, whose mma runs in f16).
-template <int W8>
-__device__ __forceinline__ void normalise_x(const GemvArgs& a, uint16_t* xs, int xstride, int K,
-                                            const float* inv_s) {
-    const int nv = K / 8;
-    for (int i = threadIdx.x; i < a.M * nv; i += blockDim.x) {
-        const int m = i / nv, k = (i % nv) * 8;
-        uint4* p = reinterpret_cast<uint4*>(xs + m * xstride + k);
-        uint4 v = *p;
-        const float inv = inv_s[m];
-        const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain + k));
-        const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain + k + 4));
-        if (W8) {
-            v.x = pack_f16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
-            v.y = pack_f16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
-            v.z = pack_f16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
-            v.w = pack_f16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
-        } else {
-            v.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
-            v.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
-            v.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
-            v.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
-        }
-        *p = v;
-    }
-}
-
-// Staged bf16 x rows -> f16 in place (FP8-weight kernels without a norm).
-__device__ __forceinline__ void x_to_f16(const GemvArgs& a, uint16_t* xs, int xstride, int K) {
-    const int nv = K / 8;
-    for (int i = threadIdx.x; i < a.M * nv; i += blockDim.x) {
-        const int m = i / nv, k = (i % nv) * 8;
-        uint4* p = reinterpret_cast<uint4*>(xs + m * xstride + k);
-        uint4 v = *p;
-        v.x = bf16x2_to_f16x2(v.x);
-        v.y = bf16x2_to_f16x2(v.y);
-        v.z = bf16x2_to_f16x2(v.z);
-        v.w = bf16x2_to_f16x2(v.w);
-        *p = v;
-    }
-}
-
-// FP8 blocks: lane (g, q) multiplies k = 64c + 16q .. +16; its x fragment is
-// those 16 values of row g as f16 (two uint4).
-__device__ __forceinline__ void x_fragment16(const GemvArgs& a, const uint16_t* xs, int xstride, int K, int c,
-                                             int g, int q, uint4& lo, uint4& hi) {
-    const int k = c * 64 + q * 16;
-    if (g >= a.M || k >= K) {
-        lo = hi = make_uint4(0u, 0u, 0u, 0u);
-        return;
-    }
-    if (xs != nullptr) {
-        lo = *reinterpret_cast<const uint4*>(xs + g * xstride + k);
-        hi = *reinterpret_cast<const uint4*>(xs + g * xstride + k + 8);
-        return;
-    }
-    const uint4 b0 = ldg_nc(a.x + (size_t)g * a.ldx + k), b1 = ldg_nc(a.x + (size_t)g * a.ldx + k + 8);
-    lo = make_uint4(bf16x2_to_f16x2(b0.x), bf16x2_to_f16x2(b0.y), bf16x2_to_f16x2(b0.z), bf16x2_to_f16x2(b0.w));
-    hi = make_uint4(bf16x2_to_f16x2(b1.x), bf16x2_to_f16x2(b1.y), bf16x2_to_f16x2(b1.z), bf16x2_to_f16x2(b1.w));
-}
-
-// One packed block into the accumulators.  bf16: two m16n8k16 steps over
-// 32 k.  FP8: the lane's 16 codes of rows g and g+8 become f16 pairs and run
-// four f16 steps over 64 k; step i takes codes 4i..4i+3 (k pairs (2q, 2q+1)
-// and (2q+8, 2q+9) of the step in the mma's numbering), matched by the same
-// x values.
-template <int W8>
-__device__ __forceinline__ void block_mma(float (&acc)[4], const uint4 (&v)[4], const GemvArgs& a,
-                                          const uint16_t* xs, int xstride, int K, int c, int g, int q) {
-    if (!W8) {
-        // v: row g (k-half 0, 1), row g+8 (k-half 0, 1)
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 xf = x_fragment(a, xs, xstride, K, c, h, g, q);
-            mma_bf16_16816(acc, v[h].x, v[2 + h].x, v[h].y, v[2 + h].y, xf.x, xf.y);
-            mma_bf16_16816(acc, v[h].z, v[2 + h].z, v[h].w, v[2 + h].w, xf.z, xf.w);
-        }
-    } else {
-        // v[0]: 16 codes of row g, v[1]: of row g+8
-        uint4 xl, xh;
-        x_fragment16(a, xs, xstride, K, c, g, q, xl, xh);
-        const uint32_t ra[4] = {v[0].x, v[0].y, v[0].z, v[0].w}, rb[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
-        const uint32_t xv[8] = {xl.x, xl.y, xl.z, xl.w, xh.x, xh.y, xh.z, xh.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            mma_f16_16816(acc, e4m3x2_to_f16x2(ra[i] & 0xffffu), e4m3x2_to_f16x2(rb[i] & 0xffffu),
-                          e4m3x2_to_f16x2(ra[i] >> 16), e4m3x2_to_f16x2(rb[i] >> 16), xv[2 * i], xv[2 * i + 1]);
-        }
-    }
-}
-
-// Byte offsets, inside a block, of lane (g, q)'s 16-byte pieces in the order
-// block_mma takes them.
-template <int W8>
-__device__ __forceinline__ void lane_pieces(int g, int q, int lane, int (&off)[4]) {
-    if (!W8) {
-        off[0] = g * 128 + ((q ^ g) & 7) * 16;                 // row g, k 8q (chunk q)
-        off[1] = g * 128 + (((4 + q) ^ g) & 7) * 16;           // row g, k 32 + 8q (chunk 4 + q)
-        off[2] = 1024 + off[0];                               // row g + 8: same swizzle phase
-        off[3] = 1024 + off[1];
-    } else {
-        off[0] = lane * 16;
-        off[1] = 512 + lane * 16;
-        off[2] = off[3] = 0;
-    }
-}
-
-// Lexicographic argmax step: larger value, then lower index.
-__device__ __forceinline__ void am_take(float& bv, int& bi, float v, int i) {
-    if (v > bv || (v == bv && i < bi)) {
-        bv = v;
-        bi = i;
-    }
-}
-
-__device__ __forceinline__ void am_reduce_g(float& bv, int& bi) {
-    // across the 8 lanes that share q (xor over the g bits 2,3,4 of the lane id)
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        am_take(bv, bi, ov, oi);
-    }
-}
-
-// Row stride (elements) of the shared x copy: 32 elements of padding put
-// consecutive rows 64 bytes apart, so the fragment loads of a warp hit 32
-// distinct banks.
-__host__ __device__ __forceinline__ int gemv_xstride(int K) { return K + 32; }
-
-// The epilogue of one 16-row tile on warp 0: acc holds rows {g, g+8} x
-// activation rows {2q, 2q+1}.
-template <int EPI>
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const float (&acc)[4], int g,
-                                              int q, float (&best_v)[2], int (&best_i)[2]) {
-    // ---- epilogue (warp 0): acc = rows {g, g+8} x cols {2q, 2q+1} ----
-    const int m0 = 2 * q, m1 = 2 * q + 1;
-    if (EPI == EPI_RESID) {
-        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-        float s0 = 0.f, s1 = 0.f;
-        if (m0 < a.M) {
-            uint16_t* o = a.out + (size_t)m0 * a.ldo;
-            float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[0]));
-            float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[2]));
-            o[r0] = f32_to_bf16_bits(x0);
-            o[r1] = f32_to_bf16_bits(x1);
-            s0 = x0 * x0 + x1 * x1;
-        }
-        if (m1 < a.M) {
-            uint16_t* o = a.out + (size_t)m1 * a.ldo;
-            float x0 = round_bf16(bf16_bits_to_f32(o[r0]) + round_bf16(acc[1]));
-            float x1 = round_bf16(bf16_bits_to_f32(o[r1]) + round_bf16(acc[3]));
-            o[r0] = f32_to_bf16_bits(x0);
-            o[r1] = f32_to_bf16_bits(x1);
-            s1 = x0 * x0 + x1 * x1;
-        }
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        }
-        if (g == 0) {
-            if (m0 < a.M) a.ss_out[tile * kRowsCap + m0] = s0;
-            if (m1 < a.M) a.ss_out[tile * kRowsCap + m1] = s1;
-        }
-    } else if (EPI == EPI_F32) {
-        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-        if (m0 < a.M) {
-            a.out_f32[(size_t)m0 * a.ldo + r0] = acc[0];
-            a.out_f32[(size_t)m0 * a.ldo + r1] = acc[2];
-        }
-        if (m1 < a.M) {
-            a.out_f32[(size_t)m1 * a.ldo + r0] = acc[1];
-            a.out_f32[(size_t)m1 * a.ldo + r1] = acc[3];
-        }
-    } else if (EPI == EPI_SWIGLU) {
-        const int j = tile * 8 + g;
-        if (m0 < a.M) {
-            float gt = acc[0], up = acc[2];
-            a.out[(size_t)m0 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
-        }
-        if (m1 < a.M) {
-            float gt = acc[1], up = acc[3];
-            a.out[(size_t)m1 * a.ldo + j] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
-        }
-    } else if (EPI == EPI_QKV) {
-        const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;  // pair tiles per head
-        const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
-        if (tile < a.q_tiles + a.k_tiles) {
-            const bool is_q = tile < a.q_tiles;
-            const int t = is_q ? tile : tile - a.q_tiles;
-            const int h = t / ppt, d = (t % ppt) * 8 + g, d2 = d + half;
-            const int brow = is_q ? h * hd : q_dim + h * hd;
-            float b1 = a.bias ? a.bias[brow + d] : 0.f, b2 = a.bias ? a.bias[brow + d2] : 0.f;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int m = e ? m1 : m0;
-                if (m >= a.M) continue;
-                const int pos = a.row_pos[m];
-                if (pos >= a.cap) continue;
-                float x1 = (e ? acc[1] : acc[0]) + b1;
-                float x2 = (e ? acc[3] : acc[2]) + b2;
-                const float* cs = a.rope_cos + (size_t)pos * hd;
-                const float* sn = a.rope_sin + (size_t)pos * hd;
-                float y1 = x1 * cs[d] - x2 * sn[d];
-                float y2 = x2 * cs[d2] + x1 * sn[d2];
-                if (is_q) {
-                    uint16_t* o = a.out + (size_t)m * a.ldo + h * hd;
-                    o[d] = f32_to_bf16_bits(y1);
-                    o[d2] = f32_to_bf16_bits(y2);
-                } else {
-                    const int slot = a.row_slot[m];
-                    uint16_t* kc = a.kcache + (((size_t)slot * a.n_kv + h) * a.cap + pos) * hd;
-                    kc[d] = f32_to_bf16_bits(y1);
-                    kc[d2] = f32_to_bf16_bits(y2);
-                }
-            }
-        } else {
-            const int vt = tile - a.q_tiles - a.k_tiles;
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                const int r = vt * kTileRows + g + rr * 8;
-                const int h = r / hd, d = r % hd;
-                const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const int m = e ? m1 : m0;
-                    if (m >= a.M) continue;
-                    const int pos = a.row_pos[m];
-                    if (pos >= a.cap) continue;
-                    const int slot = a.row_slot[m];
-                    float val = acc[rr * 2 + e] + b;
-                    a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] =
-                        f32_to_bf16_bits(val);
-                }
-            }
-        }
-    } else if (EPI == EPI_LOGITS) {
-        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const int m = e ? m1 : m0;
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            if (m < a.M) {
-                if (r0 < a.vocab) {
-                    uint16_t b = f32_to_bf16_bits(acc[e]);
-                    a.out[(size_t)m * a.ldo + r0] = b;
-                    am_take(bv, bi, bf16_bits_to_f32(b), r0);
-                }
-                if (r1 < a.vocab) {
-                    uint16_t b = f32_to_bf16_bits(acc[2 + e]);
-                    a.out[(size_t)m * a.ldo + r1] = b;
-                    am_take(bv, bi, bf16_bits_to_f32(b), r1);
-                }
-            }
-            am_reduce_g(bv, bi);
-            am_take(best_v[e], best_i[e], bv, bi);
-        }
-    }
-}
-
-// ---- weight pipelines ----------------------------------------------------
-// Each warp walks a flat sequence of chunks (its k-range of a tile, tile
-// after tile of the CTA) so the stream never restarts at a tile boundary.
-//
-// PIPE_REG: the next chunk (kChunkBytes of blocks) is loaded into registers while
-// the current one is multiplied.
-// PIPE_TMA: each warp owns a ring of kTmaStages stages of kChunkBytes of
-// contiguous packed blocks in shared memory, filled by one
-// cp.async.bulk (TMA) copy per stage and an mbarrier with the transaction
-// byte count; lane 0 refills a stage as soon as the warp has read it.  The
-// bytes in flight are bounded by shared memory, not registers.  Every
-// mbarrier wait is bounded by a %globaltimer deadline: on expiry the kernel
-// records RENG_E_TIMEOUT in *a.err, stops issuing copies, drains its own
-// copies (again bounded) and finishes without waiting.
-enum { PIPE_REG = 0, PIPE_TMA = 1 };
-constexpr int kChunkBytes = 4096;                             // weight bytes per pipeline chunk
-constexpr int kTmaStages = 4;
-constexpr int kTmaRing = kTmaStages * kChunkBytes;           // bytes per warp
-constexpr unsigned long long kWaitNs = 2000000000ull;           // 2 s per wait
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait: false if the deadline passed first.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity))
-        if (globaltimer() - t0 > kWaitNs) return false;
-    return true;
-}
-__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ uint4 lds128(uint32_t saddr) {
-    uint4 r;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(saddr));
-    return r;
-}
+// The device pieces shared with the persistent step kernel (x fragments,
+// block MMAs, tile epilogues, the TMA ring primitives) are in gemv_core.cuh.
 
 template <int PIPE>
 __host__ __device__ constexpr int gemv_ring_bytes() {
@@ -746,8 +415,9 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int shape, int max_grid, boo
 }
 
 // ------------------------------------------------------------- attention --
-// Decode attention over the KV cache.  One thread-block cluster of
-// kAttnCluster CTAs per (row, KV group): CTA s takes the s-th contiguous
+// Decode attention over the KV cache.  One thread-block cluster of up to
+// kAttnCluster CTAs per (row, KV group) (fewer when the rows x groups
+// already fill the GPU, chosen at launch): CTA s takes the s-th contiguous
 // slice of the row's keys 0..pos and runs an f32 online softmax over it in
 // kAttnChunk-key shared-memory tiles, for all hpg query heads of the group at
 // once (each K/V tile is read once for the whole GQA group).  The slices are
@@ -889,13 +559,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
 cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t st) {
     if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.hpg * (a.hd / 4) > kAttnThreads)
         return cudaErrorInvalidValue;
+    // key slices per (row, KV group): 8 (a cluster) when the rows x groups
+    // are few, fewer once they alone fill the GPU several times over
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long units = (long long)a.M * a.n_kv, want = 4LL * num_sms(dev);
+    int ns = kAttnCluster;
+    while (ns > 1 && units * ns / 2 >= want) ns /= 2;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
-    cfg.gridDim = dim3(kAttnCluster, a.n_kv, a.M);
+    cfg.gridDim = dim3(ns, a.n_kv, a.M);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kAttnCluster;
+    attr[0].val.clusterDim.x = ns;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -23,6 +23,11 @@ constexpr int kMaxRows = 8;    // activation rows per GEMV launch (mma N)
 constexpr int kRowsCap = 256;  // rows of a step (work buffers, RMS-partials stride)
 constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
 
+// Row stride (elements) of the shared x copy: 32 elements of padding put
+// consecutive rows 64 bytes apart, so the fragment loads of a warp hit 32
+// distinct banks.
+__host__ __device__ __forceinline__ int gemv_xstride(int K) { return K + 32; }
+
 enum Epi : int {
     EPI_QKV = 0,     // bias + RoPE, q to a buffer, k/v into the KV cache
     EPI_RESID = 1,   // x_res += bf16(acc) (bf16), norm partials of x_res

@@ -18,9 +18,13 @@
 // commits each stage back to the producer; warps 2-5 read the accumulator
 // with tcgen05.ld (warp w reads TMEM lanes 32*(w%4) .. +32) and apply the
 // same epilogues as the GEMV kernels.  A weight matrix with few super-tiles
-// is split along K over several CTAs: each writes its partial tile to a
-// workspace and the last one sums the partials in split order
-// (deterministic) and runs the epilogue.  Every mbarrier wait is bounded.
+// is split along K over up to 8 CTAs launched as one thread-block cluster:
+// each keeps its partial tile in its own shared memory, and after a cluster
+// barrier CTA r adds column blocks r, r + ks, ... of every split over
+// distributed shared memory in rank order (deterministic) and runs their
+// epilogue.  Every mbarrier wait is bounded.
+#include <cooperative_groups.h>
+
 #include <mutex>
 #include <string>
 #include <vector>
@@ -358,31 +362,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                 tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
             }
         } else {
-            // split K: publish this split's partial, the last split sums them in order
-            float* wsS = g.ws + (size_t)S * g.ks * N * 128;
+            // split K: this split's partial into the (finished) stage buffers,
+            // row lr at lr * (N + 4) floats (conflict-free 16-byte stores)
+            float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
             for (int cb = 0; cb < N / 16; cb++) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
+                float4* dst = reinterpret_cast<float4*>(part + (size_t)lr * (N + 4) + cb * 16);
 #pragma unroll
-                for (int j = 0; j < 16; j++) wsS[((size_t)ksi * N + cb * 16 + j) * 128 + lr] = zero ? 0.f : v[j];
-            }
-            __threadfence();
-            named_sync_epilogue();
-            if (warp_e == 0 && lane == 0) s_flag = (atomicAdd(g.ws_count + S, 1u) == (unsigned)(g.ks - 1));
-            named_sync_epilogue();
-            if (s_flag) {
-                __threadfence();
-                for (int cb = 0; cb < N / 16; cb++) {
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        float acc = 0.f;
-                        for (int k = 0; k < g.ks; k++) acc += __ldcg(wsS + ((size_t)k * N + cb * 16 + j) * 128 + lr);
-                        v[j] = acc;
-                    }
-                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
-                }
-                if (warp_e == 0 && lane == 0) g.ws_count[S] = 0u;
+                for (int j = 0; j < 4; j++)
+                    dst[j] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                  : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
         }
         if (EPI == EPI_LOGITS) {
@@ -435,6 +425,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             }
         }
     }
+    if (g.ks > 1) {
+        // the K splits of this super-tile are one cluster: once every
+        // split's partial is in its shared memory, CTA r adds column blocks
+        // r, r + ks, ... over the cluster in rank order (deterministic) and
+        // runs their epilogue
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (warp >= 2) {
+            const int lr = 32 * (warp & 3) + lane, p = 128 * S + lr, warp_e = warp - 2;
+            float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
+            for (int cb = ksi; cb < N / 16; cb += g.ks) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = 0.f;
+                for (int k = 0; k < g.ks; k++) {
+                    const float4* src =
+                        reinterpret_cast<const float4*>(cluster.map_shared_rank(part, k) + (size_t)lr * (N + 4) + cb * 16);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float4 x = src[j];
+                        v[4 * j] += x.x;
+                        v[4 * j + 1] += x.y;
+                        v[4 * j + 2] += x.z;
+                        v[4 * j + 3] += x.w;
+                    }
+                }
+                tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+            }
+        }
+        cluster.sync();  // peers are done reading this CTA's partial
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
@@ -485,15 +507,26 @@ size_t gemm_smem_bytes(int n) { return (size_t)kGemmStages * (kStageA + (size_t)
 template <int EPI>
 static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool pdl, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(g.super_tiles * g.ks);
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = gemm_smem_bytes(g.N);
     cfg.stream = st;
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 0;
+    if (g.ks > 1) {  // the K splits of a super-tile form one cluster
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = g.ks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, map, g);
 }
 
@@ -534,13 +567,14 @@ int gemm_pick_splits(int super_tiles, int kc, int resident, int epi) {
     if (epi == EPI_LOGITS || super_tiles >= resident / 2) return 1;
     int ks = resident / super_tiles;
     ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
+    if (ks > kGemmMaxSplits) ks = kGemmMaxSplits;
     const int kper = (kc + ks - 1) / ks;
     return (kc + kper - 1) / kper;  // every split gets at least one chunk
 }
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
     if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
-        (epi == EPI_LOGITS && g.ks != 1) || (g.ks > 1 && (g.ws == nullptr || g.ws_count == nullptr)))
+        g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1))
         return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_QKV: return launch_tc_t<EPI_QKV>(map, g, pdl, st);
@@ -640,8 +674,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     uint16_t *wd = nullptr, *xd = nullptr;
     uint8_t* packed = nullptr;
     int* rowmap = nullptr;
-    float *yd = nullptr, *ws = nullptr;
-    unsigned int* cnt = nullptr;
+    float* yd = nullptr;
     int* err = nullptr;
     GEMM_CU(f.alloc(&wd, (size_t)rows * K * 2));
     GEMM_CU(f.alloc(&xd, (size_t)kRowsCap * K * 2));
@@ -683,17 +716,11 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     if (splits == 0) {
         g.ks = gemm_pick_splits(g.super_tiles, kc, resident, EPI_F32);
     } else {
-        const int s = splits > kc ? kc : splits;
+        int s = splits > kc ? kc : splits;
+        if (s > kGemmMaxSplits) s = kGemmMaxSplits;
         const int kper = (kc + s - 1) / s;
         g.ks = (kc + kper - 1) / kper;
     }
-    if (g.ks > 1) {
-        GEMM_CU(f.alloc(&ws, (size_t)g.super_tiles * g.ks * N * 128 * 4));
-        GEMM_CU(f.alloc(&cnt, (size_t)g.super_tiles * 4));
-        GEMM_CU(cudaMemset(cnt, 0, (size_t)g.super_tiles * 4));
-    }
-    g.ws = ws;
-    g.ws_count = cnt;
     CUtensorMap tmap;
     const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);
     if (rc) return rc;

@@ -8,6 +8,7 @@
 namespace reng {
 
 constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
+constexpr int kGemmMaxSplits = 8;     // K splits of a super-tile (a portable cluster)
 
 struct GemmArgs {
     GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
@@ -15,10 +16,8 @@ struct GemmArgs {
     int tiles16;              // 16-row tiles of the matrix
     int kc;                   // 64-k chunks
     int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
-    int ks;                   // K splits (every split gets >= 1 chunk)
+    int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
-    float* ws;                // split-K partials [super_tiles][ks][N][128]
-    unsigned int* ws_count;   // [super_tiles] arrivals, reset by the last split
 };
 
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as

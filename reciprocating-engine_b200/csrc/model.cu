@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "step.cuh"
 
 using namespace reng;
 
@@ -48,12 +49,13 @@ struct reng_model {
     // work buffers
     uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
     uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
-    float* ws = nullptr;             // GEMM split-K partials
-    size_t ws_floats = 0;
-    unsigned int* ws_count = nullptr;
-    int ws_tiles = 0;                // super-tiles ws_count covers
     int gemm_occ[5][kRowsCap / 16 + 1] = {};  // resident GEMM CTAs per SM by (epilogue, N/16)
     int launches = 0;                // kernels of this library enqueued so far
+    // the persistent decode step (one cooperative launch per step) when the
+    // shape allows it, else the per-projection kernels
+    bool step_on = false;
+    int step_grid = 0;
+    StepCtl step_ctl{};
     float* ss = nullptr;
     float* part = nullptr;  // tensor-parallel f32 partials [kRowsCap][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
@@ -268,7 +270,7 @@ int validate(const reng_model_desc* d) {
 }
 
 // Launch helpers, one per kernel of the step (all on stream `st`).
-int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
+EmbedArgs embed_args(reng_model* m, int mode, int M, int slot) {
     EmbedArgs e{};
     e.table = m->embed;
     e.hidden = m->hidden;
@@ -285,7 +287,11 @@ int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
     e.prefill_ids = m->prefill_ids;
     e.slot = slot;
     e.batch = m->B;
-    CU(launch_embed(e, true, st));
+    return e;
+}
+
+int k_embed_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st) {
+    CU(launch_embed(embed_args(m, mode, M, slot), true, st));
     m->launches++;
     return RENG_OK;
 }
@@ -296,10 +302,10 @@ GemvArgs base_args(reng_model* m) {
     return g;
 }
 
-// k-chunks of a K-wide projection: 32 bf16 or 64 FP8 codes per packed block
+// k-chunks of a K-wide projection (64 k per packed block in both formats)
 int proj_kc(reng_model* m, int K) {
     (void)m;
-    return (K + kChunkK - 1) / kChunkK;  // 64 k per block in both formats
+    return (K + kChunkK - 1) / kChunkK;
 }
 
 GemvArgs norm_args(reng_model* m, int M, const float* gain) {
@@ -356,10 +362,6 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
     a.ks = gemm_pick_splits(a.super_tiles, g.kc, m->sms * gemm_occupancy(m, epi, N), epi);
-    a.ws = m->ws;
-    a.ws_count = m->ws_count;
-    if (a.ks > 1 && ((size_t)a.super_tiles * a.ks * N * 128 > m->ws_floats || a.super_tiles > m->ws_tiles))
-        return fail(RENG_E_STATE, "GEMM split-K workspace too small");
     if (epi == EPI_LOGITS && (size_t)a.super_tiles > (size_t)m->lm_grid)
         return fail(RENG_E_STATE, "LM head argmax partials too small");
     CU(launch_gemm_tc(map, a, epi, true, st));
@@ -367,7 +369,7 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     return RENG_OK;
 }
 
-int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
+GemvArgs qkv_args(reng_model* m, int l, int M) {
     const LayerDev& w = m->layers[l];
     GemvArgs g = norm_args(m, M, w.g1);
     g.w = w.wqkv;
@@ -387,10 +389,14 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     g.kcache = m->kcache + (size_t)l * m->layer_kv;
     g.vcache = m->vcache + (size_t)l * m->layer_kv;
     g.cap = m->cap;
-    return linear(m, g, EPI_QKV, 0, 0, st);
+    return g;
 }
 
-int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
+int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    return linear(m, qkv_args(m, l, M), EPI_QKV, 0, 0, st);
+}
+
+AttnArgs attn_args(reng_model* m, int l, int M) {
     AttnArgs at{};
     at.q = m->qbuf;
     at.kcache = m->kcache + (size_t)l * m->layer_kv;
@@ -403,14 +409,18 @@ int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
     at.hpg = m->hpg;
     at.hd = m->hd;
     at.cap = m->cap;
-    CU(launch_attn(at, kAttnChunk, true, st));
+    return at;
+}
+
+int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    CU(launch_attn(attn_args(m, l, M), kAttnChunk, true, st));
     m->launches++;
     return RENG_OK;
 }
 
 // o_proj (which == 0) or down_proj (which == 1) with the residual add; under
 // tensor parallelism the f32 partial, the all-reduce and the residual kernel.
-int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
+GemvArgs proj_args(reng_model* m, int l, int M, int which) {
     const LayerDev& w = m->layers[l];
     GemvArgs o = base_args(m);
     o.M = M;
@@ -426,6 +436,11 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
     o.ldo = m->hidden;
     o.ss_out = m->ss;
     o.out_f32 = m->part;
+    return o;
+}
+
+int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
+    const GemvArgs o = proj_args(m, l, M, which);
     const int kind = which == 0 ? 1 : 3;
     if (m->world > 1) {
         TRY(linear(m, o, EPI_F32, kind, 0, st));
@@ -438,7 +453,7 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
     return RENG_OK;
 }
 
-int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
+GemvArgs gateup_args(reng_model* m, int l, int M) {
     const LayerDev& w = m->layers[l];
     GemvArgs u = norm_args(m, M, w.g2);
     u.w = w.wgu;
@@ -448,11 +463,15 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
     u.tiles = m->gu_tiles;
     u.out = m->act;
     u.ldo = m->inter;
-    return linear(m, u, EPI_SWIGLU, 2, 0, st);
+    return u;
+}
+
+int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
+    return linear(m, gateup_args(m, l, M), EPI_SWIGLU, 2, 0, st);
 }
 
 // LM head over rows [r0, r0 + M) of the step (logits and argmax rows 0..M-1).
-int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int r0 = 0) {
+GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0) {
     GemvArgs h = norm_args(m, M, m->final_gamma);
     h.x = m->x_res + (size_t)r0 * m->hidden;
     h.ss_in = m->ss + r0;
@@ -471,7 +490,11 @@ int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int
     h.step = m->step;
     h.ids_ring = m->ids_ring;
     h.next_id = m->next_id;
-    return linear(m, h, EPI_LOGITS, 4, m->lm_grid, st);
+    return h;
+}
+
+int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int r0 = 0) {
+    return linear(m, head_args(m, mode, M, slot, r0), EPI_LOGITS, 4, m->lm_grid, st);
 }
 
 // The kernels of one step.  mode 0: decode over the B slots (rows = slots,
@@ -495,8 +518,134 @@ int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_
     return RENG_OK;
 }
 
+// The phase table and scratch of the persistent step kernel (decode rows =
+// the B slots), when RENG_STEP_KERNEL=1 asks for it.  Measured on B200
+// (Llama-8B b1) it is behind the per-projection kernels (3.86 against 3.40
+// ms per step: each phase pays a grid barrier, the x staging and the tile
+// reductions, about as much as a launch), so it is not the default.  Leaves
+// step_on false when the shape is outside what it runs (tensor parallel,
+// batch > 8, head_dim above 128, shared memory).
+int build_step(reng_model* m) {
+    m->step_on = false;
+    const char* env = getenv("RENG_STEP_KERNEL");
+    if (!env || atoi(env) != 1) return RENG_OK;
+    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep) return RENG_OK;
+    const int M = m->B;
+    std::vector<StepPhase> ph;
+    StepPhase pe{};
+    pe.kind = PH_EMBED;
+    pe.em = embed_args(m, 0, M, 0);
+    ph.push_back(pe);
+    auto gemv = [&](const GemvArgs& g, int epi) {
+        StepPhase p{};
+        p.kind = PH_GEMV;
+        p.epi = epi;
+        p.g = g;
+        p.blocks = (long long)g.tiles * g.kc;
+        ph.push_back(p);
+    };
+    for (int l = 0; l < m->L; l++) {
+        gemv(qkv_args(m, l, M), EPI_QKV);
+        StepPhase pa{};
+        pa.kind = PH_ATTN;
+        pa.at = attn_args(m, l, M);
+        ph.push_back(pa);
+        gemv(proj_args(m, l, M, 0), EPI_RESID);
+        gemv(gateup_args(m, l, M), EPI_SWIGLU);
+        gemv(proj_args(m, l, M, 1), EPI_RESID);
+    }
+    gemv(head_args(m, 0, M, 0, 0), EPI_LOGITS);
+    // shared memory: the rings + the x rows of a phase (or the attention q)
+    int xbytes = (int)step_attn_smem_bytes();
+    for (const StepPhase& p : ph)
+        if (p.kind == PH_GEMV)  // x rows + a zero patch + the warps' tile reduction
+            xbytes = std::max(xbytes, (M * step_xstride(p.g.K) * 2 + 128 + 15) / 16 * 16 + step_red_bytes(M));
+    int stages = 4, per_sm = 0;
+    for (; stages >= 2; stages--) {
+        per_sm = step_blocks_per_sm(m->w8, stages, xbytes, (int)ph.size());
+        if (per_sm >= 1) break;
+    }
+    if (per_sm < 1) return RENG_OK;
+    const int grid = m->sms;  // one CTA per SM, all resident (cooperative launch)
+    size_t part_f4 = 0;
+    int max_tiles = 0;
+    for (StepPhase& p : ph) {
+        if (p.kind != PH_GEMV) continue;
+        const long long T = p.blocks, kc = p.g.kc, Gp = std::min<long long>(T, grid);  // CTAs of the phase
+        int slots = 1;
+        for (long long t = 0; t < p.g.tiles; t++) {
+            const long long first = ((t * kc + 1) * Gp - 1) / T, last = ((t + 1) * kc * Gp - 1) / T;
+            slots = std::max(slots, (int)(last - first + 1));
+        }
+        p.slots = slots;
+        part_f4 = std::max(part_f4, (size_t)p.g.tiles * slots * 32);
+        max_tiles = std::max(max_tiles, p.g.tiles);
+    }
+    // attention units (key ranges) per (row, KV group): about one per CTA
+    const int A = std::max(1, std::min(16, grid / (M * m->nkv)));
+    StepCtl& c = m->step_ctl;
+    StepPhase* dph = nullptr;
+    TRY(dalloc(m, &dph, ph.size()));
+    CU(cudaMemcpyAsync(dph, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice, m->st));
+    c.ph = dph;
+    std::vector<StepSeq> seq(ph.size());
+    for (size_t i = 0; i < ph.size(); i++) {
+        StepSeq q{};
+        if (ph[i].kind == PH_GEMV) {
+            q.w = ph[i].g.w;
+            q.blocks = (int)ph[i].blocks;
+            q.kc = (short)ph[i].g.kc;
+            q.bb = (short)(ph[i].g.w8 ? kBlockBytesFp8 : kBlockBytesBf16);
+        }
+        seq[i] = q;
+    }
+    StepSeq* dseq = nullptr;
+    TRY(dalloc(m, &dseq, seq.size()));
+    CU(cudaMemcpyAsync(dseq, seq.data(), seq.size() * sizeof(StepSeq), cudaMemcpyHostToDevice, m->st));
+    c.seq = dseq;
+    c.nph = (int)ph.size();
+    c.stages = stages;
+    c.xbytes = xbytes;
+    c.attn_units = A;
+    TRY(dalloc(m, &c.part, part_f4));
+    TRY(dalloc(m, &c.tile_cnt, (size_t)max_tiles));
+    TRY(dalloc(m, &c.apart, (size_t)M * m->nkv * A * step_attn_part_len(m->hpg, m->hd)));
+    TRY(dalloc(m, &c.acnt, (size_t)M * m->nkv));
+    TRY(dalloc(m, &c.bar, 1));
+    TRY(dalloc(m, &c.abort, 1));
+    CU(cudaMemsetAsync(c.tile_cnt, 0, (size_t)max_tiles * 4, m->st));
+    CU(cudaMemsetAsync(c.acnt, 0, (size_t)M * m->nkv * 4, m->st));
+    CU(cudaMemsetAsync(c.bar, 0, 8, m->st));
+    CU(cudaMemsetAsync(c.abort, 0, 4, m->st));
+    c.err = m->err;
+    c.am_val = m->am_val;  // G x kMaxRows fits the LM head's partial buffers
+    c.am_idx = m->am_idx;
+    c.am_count = m->am_count;
+    CU(cudaStreamSynchronize(m->st));
+    m->step_grid = grid;
+    m->step_on = true;
+    return RENG_OK;
+}
+
 int build_graph(reng_model* m) {
     cudaGraph_t g = nullptr;
+    if (m->step_on) {
+        // one cooperative launch per step; if it cannot be captured the
+        // per-projection kernels take over
+        cudaError_t e = cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal);
+        cudaError_t el = e == cudaSuccess ? launch_step(m->step_ctl, m->w8, m->step_grid, m->st) : e;
+        cudaError_t ee = e == cudaSuccess ? cudaStreamEndCapture(m->st, &g) : e;
+        if (el == cudaSuccess && ee == cudaSuccess && g != nullptr &&
+            cudaGraphInstantiate(&m->graph, g, 0) == cudaSuccess) {
+            cudaGraphDestroy(g);
+            m->kernels_per_step = 1;
+            return RENG_OK;
+        }
+        if (g) cudaGraphDestroy(g);
+        g = nullptr;
+        cudaGetLastError();
+        m->step_on = false;
+    }
     CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
     int rc = enqueue_step(m, 0, m->B, 0, HEAD_ALL, m->st, &m->kernels_per_step);
     cudaError_t e = cudaStreamEndCapture(m->st, &g);
@@ -693,23 +842,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
-    if (!m->w8) {
-        // split-K partials: a split launch fills at most the resident CTA slots
-        // (sms x CTAs per SM <= 2 x sms at N <= 64, fewer above)
-        const int max_tiles = std::max({m->qkv_tiles, m->o_tiles, m->gu_tiles, m->d_tiles, m->lm_tiles});
-        m->ws_tiles = (max_tiles + 7) / 8;
-        size_t most = 0;
-        for (int n = 16; n <= kRowsCap; n += 16)
-            for (int epi = 0; epi < 5; epi++)
-                most = std::max(most, (size_t)m->sms * gemm_occupancy(m, epi, n) * n * 128);
-        m->ws_floats = most;
-        TRY(dalloc(m, &m->ws, m->ws_floats));
-        TRY(dalloc(m, &m->ws_count, (size_t)m->ws_tiles));
-        CU(cudaMemsetAsync(m->ws_count, 0, (size_t)m->ws_tiles * 4, m->st));
-    }
     CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
     m->host_pos.assign(m->B, 0);
     CU(cudaStreamSynchronize(m->st));
+    TRY(build_step(m));
     TRY(build_graph(m));
     return RENG_OK;
 }
@@ -748,6 +884,11 @@ int check_device_error(reng_model* m) {
     if (*h != 0) {
         const int code = *h;
         CU(cudaMemsetAsync(m->err, 0, 4, m->st));
+        if (m->step_on) {  // a step that gave up may leave the barrier mid-count
+            CU(cudaMemsetAsync(m->step_ctl.abort, 0, 4, m->st));
+            CU(cudaMemsetAsync(m->step_ctl.bar, 0, 8, m->st));
+            CU(cudaStreamSynchronize(m->st));
+        }
         return fail(code, "a kernel of the step gave up on a bounded wait; the results are invalid");
     }
     return RENG_OK;
@@ -983,6 +1124,41 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
     // with other activations: the cached prefix is no longer valid
     for (int b = 0; b < m->B; b++) m->host_pos[b] = 0;
     return sync_pos(m);
+}
+
+extern "C" int reng_model_trace_step(reng_model* m, uint64_t* out, int max_phases, int* n_phases) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(out != nullptr && n_phases != nullptr && max_phases >= 1, "reng_model_trace_step: bad arguments");
+    if (!m->step_on) return fail(RENG_E_STATE, "reng_model_trace_step: this model runs per-projection kernels");
+    for (int b = 0; b < m->B; b++)
+        RENG_CHECK_ARG((int64_t)m->host_pos[b] + 1 <= m->cap, "reng_model_trace_step: capacity overflow");
+    CU(cudaSetDevice(m->dev));
+    const int nph = m->step_ctl.nph;
+    std::vector<unsigned long long> h((size_t)kTraceStride * nph, 0ull);
+    for (int p = 0; p < nph; p++) h[kTraceStride * p + 1] = ~0ull;
+    unsigned long long* d = nullptr;
+    CU(cudaMalloc((void**)&d, h.size() * 8));
+    struct Free {
+        void* p;
+        ~Free() { cudaFree(p); }
+    } fr{d};
+    CU(cudaMemcpyAsync(d, h.data(), h.size() * 8, cudaMemcpyHostToDevice, m->st));
+    CU(cudaMemsetAsync(m->step, 0, 4, m->st));
+    StepCtl c = m->step_ctl;
+    c.trace = d;
+    CU(launch_step(c, m->w8, m->step_grid, m->st));
+    CU(cudaMemcpyAsync(h.data(), d, h.size() * 8, cudaMemcpyDeviceToHost, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    for (int b = 0; b < m->B; b++) m->host_pos[b] += 1;
+    const unsigned long long t0 = h[0];
+    const int n = std::min(nph, max_phases);
+    for (int p = 0; p < n; p++)
+        for (int k = 0; k < kTraceStride; k++) {
+            const unsigned long long v = h[kTraceStride * p + k];
+            out[kTraceStride * p + k] = (v == 0 || v == ~0ull || v < t0) ? 0 : v - t0;
+        }
+    *n_phases = n;
+    return check_device_error(m);
 }
 
 // ------------------------------------------------------------------- TP --

@@ -82,6 +82,7 @@ SIGNATURES = {
     "reng_model_last_times": ([_P, _P], C.c_int),
     "reng_model_time_kernels": ([_P, C.c_int, _P], C.c_int),
     "reng_tp_unique_id": ([_P], C.c_int),
+    "reng_model_trace_step": ([_P, _P, C.c_int, _P], C.c_int),
     "reng_gemm_bf16": ([_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, C.c_int, _P, C.c_int], C.c_int),
 }
 
