@@ -245,13 +245,11 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     }
 
     if (EPI == EPI_LOGITS) {
+        // this CTA's best per row into the rows' running maxima (lanes g == 0
+        // of warp 0 hold rows 2q, 2q + 1); the last CTA reads them out
         if (warp == 0 && g == 0) {
-            if (2 * q < kMaxRows) {
-                a.am_val[blockIdx.x * kMaxRows + 2 * q] = best_v[0];
-                a.am_idx[blockIdx.x * kMaxRows + 2 * q] = best_i[0];
-                a.am_val[blockIdx.x * kMaxRows + 2 * q + 1] = best_v[1];
-                a.am_idx[blockIdx.x * kMaxRows + 2 * q + 1] = best_i[1];
-            }
+            if (2 * q < a.M) atomicMax(a.am_key + 2 * q, am_pack(best_v[0], best_i[0]));
+            if (2 * q + 1 < a.M) atomicMax(a.am_key + 2 * q + 1, am_pack(best_v[1], best_i[1]));
         }
         __threadfence();
         __syncthreads();
@@ -259,21 +257,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         __syncthreads();
         if (!s_last) return;
         __threadfence();
-        // the last CTA: reduce the per-CTA partials of every row (warp m)
-        for (int m = warp; m < a.M; m += NWARP) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int b = lane; b < (int)gridDim.x; b += 32)
-                am_take(bv, bi, __ldcg(a.am_val + b * kMaxRows + m), __ldcg(a.am_idx + b * kMaxRows + m));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                am_take(bv, bi, ov, oi);
-            }
-            if (bi == 0x7fffffff) bi = 0;  // all NaN: the reference's initial index
-            s_ids[m] = bi;
-        }
+        if (threadIdx.x < a.M) s_ids[threadIdx.x] = am_unpack(atomicExch(a.am_key + threadIdx.x, 0ull));
         __syncthreads();
         if (threadIdx.x == 0) {
             if (a.mode == 0) {

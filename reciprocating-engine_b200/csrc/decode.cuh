@@ -74,8 +74,9 @@ struct GemvArgs {
     int cap;
     // EPI_LOGITS
     int vocab;
-    float* am_val;          // [gridDim][kMaxRows]
+    float* am_val;          // (persistent step kernel) per-warp partials [warps][kMaxRows]
     int* am_idx;
+    unsigned long long* am_key;  // [kRowsCap] running maximum of am_pack keys per row, 0 between launches
     unsigned int* am_count;
     int mode;               // 0 decode, 1 prefill
     int slot;               // prefill slot
@@ -134,6 +135,21 @@ struct PackArgs {
     int scale_rows;
     uint8_t* dst;
 };
+
+// Argmax over CTAs as one 64-bit atomicMax per row: the high word orders the
+// f32 values (NaN lowest: it never wins, as in the reference's comparison),
+// the low word is ~index, so among equal values the first index wins.  The
+// maximum is the same whatever order the CTAs arrive in.
+__device__ __forceinline__ unsigned long long am_pack(float v, int i) {
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t ord = (v != v) ? 0u : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+}
+// The index of a row's maximum key (0 for a row of NaN only, or no key).
+__device__ __forceinline__ int am_unpack(unsigned long long key) {
+    const uint32_t i = 0xffffffffu - (uint32_t)(key & 0xffffffffu);
+    return (key == 0ull || i >= 0x7fffffffu) ? 0 : (int)i;
+}
 
 // Launchers (return cudaError of the launch).  `pdl` sets programmatic
 // stream serialization so the kernel may start before its predecessor ends.

@@ -138,16 +138,23 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
     // rows past the matrix (the last 16-row tile, the last 128-row CTA
     // tile) are computed but never stored
     const bool valid = tile < g.tiles16 && (EPI == EPI_SWIGLU || EPI == EPI_QKV || EPI == EPI_LOGITS || p < a.ldo);
+    // every global load of the 16 columns is issued before the arithmetic
+    // that needs it (one round trip per group, not one per column)
+    if (EPI == EPI_RESID) {
+        uint16_t xo[16];
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-        const int m = cb * 16 + j;
-        const bool live = valid && m < a.M;
-        if (EPI == EPI_RESID) {
+        for (int j = 0; j < 16; j++) {
+            const int m = cb * 16 + j;
+            xo[j] = (valid && m < a.M) ? __ldcg(a.out + (size_t)m * a.ldo + p) : (uint16_t)0;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int m = cb * 16 + j;
+            const bool live = valid && m < a.M;
             float sq = 0.f;
             if (live) {
-                uint16_t* o = a.out + (size_t)m * a.ldo + p;
-                const float x = round_bf16(bf16_bits_to_f32(*o) + round_bf16(v[j]));
-                *o = f32_to_bf16_bits(x);
+                const float x = round_bf16(bf16_bits_to_f32(xo[j]) + round_bf16(v[j]));
+                a.out[(size_t)m * a.ldo + p] = f32_to_bf16_bits(x);
                 sq = x * x;
             }
             sq += __shfl_xor_sync(0xffffffffu, sq, 1);
@@ -155,7 +162,74 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
             sq += __shfl_xor_sync(0xffffffffu, sq, 4);
             sq += __shfl_xor_sync(0xffffffffu, sq, 8);
             if (live && i16 == 0) a.ss_out[tile * kRowsCap + m] = sq;
-        } else if (EPI == EPI_F32) {
+        }
+        return;
+    }
+    if (EPI == EPI_QKV) {
+        const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;
+        const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
+        const bool rope = tile < a.q_tiles + a.k_tiles, is_q = tile < a.q_tiles, first = i16 < 8;
+        int h, d, d2, brow = 0, r = 0;
+        if (rope) {
+            const int t = is_q ? tile : tile - a.q_tiles;
+            h = t / ppt;
+            d = (t % ppt) * 8 + (i16 & 7);
+            d2 = d + half;
+            brow = is_q ? h * hd : q_dim + h * hd;
+        } else {
+            r = (tile - a.q_tiles - a.k_tiles) * kTileRows + i16;
+            h = r / hd;
+            d = d2 = r % hd;
+        }
+        const int dd = first ? d : d2;
+        float b1 = 0.f, b2 = 0.f;
+        if (a.bias && valid) {
+            if (rope) {
+                b1 = a.bias[brow + d];
+                b2 = a.bias[brow + d2];
+            } else {
+                b1 = a.bias[q_dim + kv_dim + r];
+            }
+        }
+        int pos[16], slot[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int m = cb * 16 + j;
+            const bool live = valid && m < a.M;
+            pos[j] = live ? a.row_pos[m] : a.cap;
+            slot[j] = live ? a.row_slot[m] : 0;
+        }
+        float cs[16], sn[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const bool ok = rope && pos[j] < a.cap;
+            cs[j] = ok ? a.rope_cos[(size_t)pos[j] * hd + dd] : 0.f;
+            sn[j] = ok ? a.rope_sin[(size_t)pos[j] * hd + dd] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int m = cb * 16 + j;
+            const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
+            if (pos[j] >= a.cap) continue;  // also the rows past M and past the matrix
+            if (rope) {
+                const float x1 = (first ? v[j] : partner) + b1;
+                const float x2 = (first ? partner : v[j]) + b2;
+                const float y = first ? x1 * cs[j] - x2 * sn[j] : x2 * cs[j] + x1 * sn[j];
+                if (is_q)
+                    a.out[(size_t)m * a.ldo + h * hd + dd] = f32_to_bf16_bits(y);
+                else
+                    a.kcache[(((size_t)slot[j] * a.n_kv + h) * a.cap + pos[j]) * hd + dd] = f32_to_bf16_bits(y);
+            } else {
+                a.vcache[(((size_t)slot[j] * a.n_kv + h) * a.cap + pos[j]) * hd + d] = f32_to_bf16_bits(v[j] + b1);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int m = cb * 16 + j;
+        const bool live = valid && m < a.M;
+        if (EPI == EPI_F32) {
             if (live) a.out_f32[(size_t)m * a.ldo + p] = v[j];
         } else if (EPI == EPI_SWIGLU) {
             const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
@@ -163,46 +237,17 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
                 const float gt = v[j], up = partner;
                 a.out[(size_t)m * a.ldo + tile * 8 + i16] = f32_to_bf16_bits(gt / (1.0f + expf(-gt)) * up);
             }
-        } else if (EPI == EPI_QKV) {
-            const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
-            if (!live) continue;
-            const int hd = a.head_dim, half = hd >> 1, ppt = hd >> 4;
-            const int q_dim = (a.q_tiles / ppt) * hd, kv_dim = a.n_kv * hd;
-            const int pos = a.row_pos[m];
-            if (pos >= a.cap) continue;
-            if (tile < a.q_tiles + a.k_tiles) {
-                const bool is_q = tile < a.q_tiles;
-                const int t = is_q ? tile : tile - a.q_tiles;
-                const int h = t / ppt, d = (t % ppt) * 8 + (i16 & 7), d2 = d + half;
-                const int brow = is_q ? h * hd : q_dim + h * hd;
-                const bool first = i16 < 8;
-                const float x1 = (first ? v[j] : partner) + (a.bias ? a.bias[brow + d] : 0.f);
-                const float x2 = (first ? partner : v[j]) + (a.bias ? a.bias[brow + d2] : 0.f);
-                const float* cs = a.rope_cos + (size_t)pos * hd;
-                const float* sn = a.rope_sin + (size_t)pos * hd;
-                const int dd = first ? d : d2;
-                const float y = first ? x1 * cs[d] - x2 * sn[d] : x2 * cs[d2] + x1 * sn[d2];
-                if (is_q) {
-                    a.out[(size_t)m * a.ldo + h * hd + dd] = f32_to_bf16_bits(y);
-                } else {
-                    const int slot = a.row_slot[m];
-                    a.kcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + dd] = f32_to_bf16_bits(y);
-                }
-            } else {
-                const int r = (tile - a.q_tiles - a.k_tiles) * kTileRows + i16;
-                const int h = r / hd, d = r % hd;
-                const int slot = a.row_slot[m];
-                const float b = a.bias ? a.bias[q_dim + kv_dim + r] : 0.f;
-                a.vcache[(((size_t)slot * a.n_kv + h) * a.cap + pos) * hd + d] = f32_to_bf16_bits(v[j] + b);
-            }
         } else if (EPI == EPI_LOGITS) {
             float bv = -INFINITY;
             int bi = 0x7fffffff;
             if (live && p < a.vocab) {
                 const uint16_t b = f32_to_bf16_bits(v[j]);
                 a.out[(size_t)m * a.ldo + p] = b;
-                bv = bf16_bits_to_f32(b);
-                bi = p;
+                const float f = bf16_bits_to_f32(b);
+                if (f > -INFINITY) {  // the reference takes a value only if it beats -inf (NaN never)
+                    bv = f;
+                    bi = p;
+                }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -231,6 +276,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
     const int S = blockIdx.x / g.ks, ksi = blockIdx.x % g.ks;
     const int kper = (g.kc + g.ks - 1) / g.ks;
     const int kb = min(g.kc, ksi * kper), ke = min(g.kc, kb + kper), nk = ke - kb;
+    // each super-tile walks its k range from a different starting chunk, so
+    // the CTAs in flight read different activation chunks (all CTAs read the
+    // same x; in lock-step they would all hit the same L2 lines)
+    const int rot = nk > 0 ? (int)(((unsigned)S * 2654435761u) % (unsigned)nk) : 0;
     const int N = g.N;
     const uint32_t stage_bytes = kStageA + (uint32_t)N * 128u;
     // 1024-byte alignment of the stage buffers (the swizzle atoms)
@@ -266,7 +315,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
         if (lane == 0) {
             int issued = 0;
             auto issue_a = [&](int i) {
-                const int c = kb + i, s = i % kGemmStages;
+                const int c = kb + (i + rot) % nk, s = i % kGemmStages;
                 const uint32_t dst = smem0 + (uint32_t)s * stage_bytes;
                 for (int t = 0; t < 8; t++) {
                     const int tile = 8 * S + t;
@@ -276,7 +325,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                 }
             };
             auto issue_b = [&](int i) {
-                const int c = kb + i, s = i % kGemmStages;
+                const int c = kb + (i + rot) % nk, s = i % kGemmStages;
                 tensor_g2s(smem0 + (uint32_t)s * stage_bytes + kStageA, &tmap_x, c * kChunkK, 0, bar_full + 8 * s);
             };
             const int nt = min(8, g.tiles16 - 8 * S);
@@ -379,12 +428,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             // CTA partials of every row: best over the 4 epilogue warps
             named_sync_epilogue();
             const GemvArgs& a = g.e;
+            // this CTA's best per row into the rows' running maxima
             for (int m = threadIdx.x - 64; m < a.M; m += 128) {
                 float bv = -INFINITY;
                 int bi = 0x7fffffff;
                 for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + m], am_i[w * kRowsCap + m]);
-                a.am_val[(size_t)blockIdx.x * kRowsCap + m] = bv;
-                a.am_idx[(size_t)blockIdx.x * kRowsCap + m] = bi;
+                atomicMax(a.am_key + m, am_pack(bv, bi));
             }
             __threadfence();
             named_sync_epilogue();
@@ -392,21 +441,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             named_sync_epilogue();
             if (s_flag) {
                 __threadfence();
-                // a warp per row, lanes over the CTA partials
-                for (int m = warp_e; m < a.M; m += 4) {
-                    float bv = -INFINITY;
-                    int bi = 0x7fffffff;
-                    for (int b = lane; b < (int)gridDim.x; b += 32)
-                        am_take2(bv, bi, __ldcg(a.am_val + (size_t)b * kRowsCap + m),
-                                 __ldcg(a.am_idx + (size_t)b * kRowsCap + m));
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                        am_take2(bv, bi, ov, oi);
-                    }
-                    if (lane == 0) am_i[m] = bi == 0x7fffffff ? 0 : bi;  // all NaN: index 0
-                }
+                for (int m = threadIdx.x - 64; m < a.M; m += 128)
+                    am_i[m] = am_unpack(atomicExch(a.am_key + m, 0ull));
                 named_sync_epilogue();
                 if (threadIdx.x == 64) {
                     if (a.mode == 0) {

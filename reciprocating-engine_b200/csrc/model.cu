@@ -65,6 +65,7 @@ struct reng_model {
     float* am_val = nullptr;
     int* am_idx = nullptr;
     unsigned int* am_count = nullptr;
+    unsigned long long* am_key = nullptr;  // [kRowsCap] LM-head argmax keys
     int lm_grid = 0;
     // GEMV launch shapes per kind (qkv, o, gate/up, down, LM head), for
     // M <= 2 and M > 2 activation rows
@@ -483,6 +484,7 @@ GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0) {
     h.am_val = m->am_val;
     h.am_idx = m->am_idx;
     h.am_count = m->am_count;
+    h.am_key = m->am_key;
     h.mode = mode;
     h.slot = slot;
     h.batch = m->B;
@@ -683,6 +685,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     m->sms = num_sms(m->dev);
     CU(gemv_prepare());
     CU(gemm_prepare());
+    // GEMM occupancy per (epilogue, N), queried now: the decode graph is
+    // built under stream capture, where the occupancy calculator may not run
+    for (int epi = 0; epi < 5; epi++)
+        for (int n = 16; n <= kRowsCap; n += 16) m->gemm_occ[epi][n / 16] = gemm_blocks_per_sm(epi, n);
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;
@@ -842,6 +848,8 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
+    TRY(dalloc(m, &m->am_key, (size_t)kRowsCap));
+    CU(cudaMemsetAsync(m->am_key, 0, (size_t)kRowsCap * 8, m->st));
     CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
     m->host_pos.assign(m->B, 0);
     CU(cudaStreamSynchronize(m->st));
