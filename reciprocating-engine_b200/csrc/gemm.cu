@@ -36,7 +36,9 @@ namespace reng {
 namespace {
 
 constexpr int kGemmThreads = 192;
-constexpr int kGemmStages = 4;
+constexpr int kGemmMaxStages = 8;  // pipeline stages (runtime: GemmArgs::stages)
+constexpr int kGemmStageBudget = 200 * 1024;                  // stage bytes of a one-per-SM launch
+constexpr int kGemmMaxDynSmem = kGemmStageBudget + 2048;      // + the 1024-byte alignment slack
 constexpr int kStageA = 8 * kBlockBytesBf16;  // 128 rows x 64 k
 constexpr unsigned long long kGemmWaitNs = 2000000000ull;
 
@@ -266,7 +268,7 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmap_x, GemmArgs g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ __align__(8) unsigned long long full[kGemmStages], empty[kGemmStages], accum;
+    __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], accum;
     __shared__ uint32_t tmem_base_s;
     __shared__ int s_flag;
     __shared__ float am_v[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
     // the CTAs in flight read different activation chunks (all CTAs read the
     // same x; in lock-step they would all hit the same L2 lines)
     const int rot = nk > 0 ? (int)(((unsigned)S * 2654435761u) % (unsigned)nk) : 0;
-    const int N = g.N;
+    const int N = g.N, SG = g.stages;
     const uint32_t stage_bytes = kStageA + (uint32_t)N * 128u;
     // 1024-byte alignment of the stage buffers (the swizzle atoms)
     const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem_raw) + 1023u) & ~1023u;
@@ -291,7 +293,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
     while ((int)ncols < N) ncols <<= 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kGemmStages; s++) {
+        for (int s = 0; s < SG; s++) {
             bar_init(bar_full + 8 * s, 1);
             bar_init(bar_empty + 8 * s, 1);
         }
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
         if (lane == 0) {
             int issued = 0;
             auto issue_a = [&](int i) {
-                const int c = kb + (i + rot) % nk, s = i % kGemmStages;
+                const int c = kb + (i + rot) % nk, s = i % SG;
                 const uint32_t dst = smem0 + (uint32_t)s * stage_bytes;
                 for (int t = 0; t < 8; t++) {
                     const int tile = 8 * S + t;
@@ -325,23 +327,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                 }
             };
             auto issue_b = [&](int i) {
-                const int c = kb + (i + rot) % nk, s = i % kGemmStages;
+                const int c = kb + (i + rot) % nk, s = i % SG;
                 tensor_g2s(smem0 + (uint32_t)s * stage_bytes + kStageA, &tmap_x, c * kChunkK, 0, bar_full + 8 * s);
             };
             const int nt = min(8, g.tiles16 - 8 * S);
             const uint32_t tx = (uint32_t)nt * kBlockBytesBf16 + (uint32_t)N * 128u;
-            const int pre = min(kGemmStages, nk);
+            const int pre = min(SG, nk);
             // the weights do not depend on the previous kernel
             for (int i = 0; i < pre; i++) {
-                bar_expect_tx(bar_full + 8 * (i % kGemmStages), tx);
+                bar_expect_tx(bar_full + 8 * (i % SG), tx);
                 issue_a(i);
             }
             pdl_wait();
             for (int i = 0; i < pre; i++) issue_b(i);
             issued = pre;
             for (int i = pre; i < nk; i++) {
-                const int s = i % kGemmStages;
-                if (!bar_wait(bar_empty + 8 * s, (uint32_t)(((i / kGemmStages) - 1) & 1))) {
+                const int s = i % SG;
+                if (!bar_wait(bar_empty + 8 * s, (uint32_t)(((i / SG) - 1) & 1))) {
                     failed = true;
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
                     break;
@@ -353,8 +355,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             }
             // drain: the last copy into each stage has landed before the CTA
             // may exit (already true unless a wait gave up; bounded)
-            for (int i = max(0, issued - kGemmStages); i < issued; i++)
-                if (!bar_wait(bar_full + 8 * (i % kGemmStages), (uint32_t)((i / kGemmStages) & 1)))
+            for (int i = max(0, issued - SG); i < issued; i++)
+                if (!bar_wait(bar_full + 8 * (i % SG), (uint32_t)((i / SG) & 1)))
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
         } else {
             pdl_wait();
@@ -367,8 +369,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             const uint32_t idesc = umma_idesc(N);
             int done = 0;
             for (int i = 0; i < nk; i++) {
-                const int s = i % kGemmStages;
-                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / kGemmStages) & 1))) {
+                const int s = i % SG;
+                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
                     break;
                 }
@@ -538,7 +540,15 @@ int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out)
     return RENG_OK;
 }
 
-size_t gemm_smem_bytes(int n) { return (size_t)kGemmStages * (kStageA + (size_t)n * 128) + 1024; }
+size_t gemm_smem_bytes(int n, int stages) { return (size_t)stages * (kStageA + (size_t)n * 128) + 1024; }
+
+int gemm_pick_stages(int n, bool /*one_per_sm*/) {
+    // Four stages.  Measured on B200 (Llama-8B widths, 64 rows): one CTA per
+    // SM with 8 stages (twice the weight bytes in flight) was slower than 4
+    // (q/k/v 55 against 33 us), so the deeper pipeline is not used.
+    int s = (int)((unsigned)kGemmStageBudget / (kStageA + (unsigned)n * 128u));
+    return s < 4 ? (s < 2 ? 2 : s) : 4;
+}
 
 template <int EPI>
 static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool pdl, cudaStream_t st) {
@@ -546,7 +556,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool p
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(g.super_tiles * g.ks);
     cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages);
     cfg.stream = st;
     int na = 0;
     if (g.ks > 1) {  // the K splits of a super-tile form one cluster
@@ -566,10 +576,17 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool p
     return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, map, g);
 }
 
+// The largest dynamic shared memory any launch uses, and the whole of the
+// SM's unified L1/shared storage as shared memory, so that two ~100 KB CTAs
+// (N <= 64) fit on one SM (the default carveout sizes the SM for one block).
 template <int EPI>
 static cudaError_t prepare_t() {
-    return cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)gemm_smem_bytes(kRowsCap));
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kGemmMaxDynSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    return e;
 }
 
 cudaError_t gemm_prepare() {
@@ -581,36 +598,29 @@ cudaError_t gemm_prepare() {
     return e;
 }
 
-int gemm_blocks_per_sm(int epi, int n) {
-    int nb = 0;
-    const size_t smem = gemm_smem_bytes(n);
-    cudaError_t e = cudaErrorInvalidValue;
-    switch (epi) {
-        case EPI_QKV: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_QKV>, kGemmThreads, smem); break;
-        case EPI_RESID: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_RESID>, kGemmThreads, smem); break;
-        case EPI_SWIGLU: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_SWIGLU>, kGemmThreads, smem); break;
-        case EPI_LOGITS: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_LOGITS>, kGemmThreads, smem); break;
-        default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_gemm_tc<EPI_F32>, kGemmThreads, smem); break;
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, int* ks_out, int* stages_out) {
+    // Enough super-tiles to occupy the SMs (or the LM head, whose argmax
+    // needs whole rows per CTA): one CTA per super-tile, two per SM at N <= 64.
+    // Else split K over a cluster of up to 8 CTAs; clusters of these kernels
+    // are scheduled one CTA per SM, so the splits fill the SMs once and each
+    // CTA gets a deep pipeline.
+    int ks = 1;
+    if (epi != EPI_LOGITS && super_tiles < sms) {
+        ks = sms / super_tiles;
+        ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
+        if (ks > kGemmMaxSplits) ks = kGemmMaxSplits;
+        const int kper = (kc + ks - 1) / ks;
+        ks = (kc + kper - 1) / kper;  // every split gets at least one chunk
     }
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        return 1;
-    }
-    return nb < 1 ? 1 : nb;
-}
-
-int gemm_pick_splits(int super_tiles, int kc, int resident, int epi) {
-    if (epi == EPI_LOGITS || super_tiles >= resident / 2) return 1;
-    int ks = resident / super_tiles;
-    ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
-    if (ks > kGemmMaxSplits) ks = kGemmMaxSplits;
-    const int kper = (kc + ks - 1) / ks;
-    return (kc + kper - 1) / kper;  // every split gets at least one chunk
+    *ks_out = ks;
+    *stages_out = gemm_pick_stages(n, ks > 1 || n > 64);
 }
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
     if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
-        g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1))
+        g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1) || g.stages < 2 || g.stages > kGemmMaxStages ||
+        gemm_smem_bytes(g.N, g.stages) > (size_t)kGemmMaxDynSmem ||
+        (g.ks > 1 && (size_t)g.stages * (kStageA + (size_t)g.N * 128) < (size_t)128 * (g.N + 4) * 4))
         return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_QKV: return launch_tc_t<EPI_QKV>(map, g, pdl, st);
@@ -748,14 +758,13 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
-    const int resident = num_sms(dev) * gemm_blocks_per_sm(EPI_F32, N);
-    if (splits == 0) {
-        g.ks = gemm_pick_splits(g.super_tiles, kc, resident, EPI_F32);
-    } else {
+    gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), &g.ks, &g.stages);
+    if (splits > 0) {
         int s = splits > kc ? kc : splits;
         if (s > kGemmMaxSplits) s = kGemmMaxSplits;
         const int kper = (kc + s - 1) / s;
         g.ks = (kc + kper - 1) / kper;
+        g.stages = gemm_pick_stages(N, g.ks > 1 || N > 64);
     }
     CUtensorMap tmap;
     const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);

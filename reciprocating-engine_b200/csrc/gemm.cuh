@@ -18,20 +18,21 @@ struct GemmArgs {
     int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
     int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
+    int stages;               // pipeline stages (2..8)
 };
 
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as
 // {64 k, n rows} boxes with the 128-byte swizzle; k >= K reads zeros.
 int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out);
-size_t gemm_smem_bytes(int n);
-// Raise the dynamic shared-memory limit of every GEMM instantiation to the
-// n = kRowsCap size (call once per device before capture).
+size_t gemm_smem_bytes(int n, int stages);
+// Pipeline stages for MMA width n: 4 with two CTAs per SM, else as many as
+// fit in about 200 KB.
+int gemm_pick_stages(int n, bool one_per_sm);
+// Raise the dynamic shared-memory limit of every GEMM instantiation (call
+// once per device before capture).
 cudaError_t gemm_prepare();
-// Resident CTAs per SM of a GEMM launch with MMA width n.
-int gemm_blocks_per_sm(int epi, int n);
-// K splits for a matrix of `super_tiles` x `kc` so that the launch fills
-// `resident` CTA slots (1 for the LM head: its argmax needs whole rows).
-int gemm_pick_splits(int super_tiles, int kc, int resident, int epi);
+// K splits and pipeline stages of a launch over super_tiles x kc blocks.
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, int* ks, int* stages);
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps,

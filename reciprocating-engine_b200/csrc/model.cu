@@ -49,7 +49,6 @@ struct reng_model {
     // work buffers
     uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
     uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
-    int gemm_occ[5][kRowsCap / 16 + 1] = {};  // resident GEMM CTAs per SM by (epilogue, N/16)
     int launches = 0;                // kernels of this library enqueued so far
     // the persistent decode step (one cooperative launch per step) when the
     // shape allows it, else the per-projection kernels
@@ -331,12 +330,6 @@ GemvArgs norm_args(reng_model* m, int M, const float* gain) {
 // weights with the rows in registers.
 bool use_gemm(const reng_model* m, int M) { return !m->w8 && M > kMaxRows; }
 
-int gemm_occupancy(reng_model* m, int epi, int n) {
-    int& v = m->gemm_occ[epi][n / 16];
-    if (v == 0) v = gemm_blocks_per_sm(epi, n);
-    return v;
-}
-
 // One projection: the GEMV for few rows, else (RMSNorm of x into xn when the
 // projection normalises its input) the tcgen05 GEMM over N = M rounded up
 // to 16 columns.  kind indexes the GEMV launch shapes.
@@ -362,7 +355,7 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.kc = g.kc;
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
-    a.ks = gemm_pick_splits(a.super_tiles, g.kc, m->sms * gemm_occupancy(m, epi, N), epi);
+    gemm_plan(a.super_tiles, g.kc, N, epi, m->sms, &a.ks, &a.stages);
     if (epi == EPI_LOGITS && (size_t)a.super_tiles > (size_t)m->lm_grid)
         return fail(RENG_E_STATE, "LM head argmax partials too small");
     CU(launch_gemm_tc(map, a, epi, true, st));
@@ -685,10 +678,6 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     m->sms = num_sms(m->dev);
     CU(gemv_prepare());
     CU(gemm_prepare());
-    // GEMM occupancy per (epilogue, N), queried now: the decode graph is
-    // built under stream capture, where the occupancy calculator may not run
-    for (int epi = 0; epi < 5; epi++)
-        for (int n = 16; n <= kRowsCap; n += 16) m->gemm_occ[epi][n / 16] = gemm_blocks_per_sm(epi, n);
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;
