@@ -32,6 +32,13 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 HBM_FALLBACK_GBS = 6650.0
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the roofline
+# kernel, from one ncu capture of that kernel on B200 (same shapes), keyed
+# by (model, batch, weights); absent: null in the JSON line
+MEASURED_TRAFFIC = {
+    ("llama-3.1-8b", 1, "bf16"): 238.8e6,  # gate/up GEMV: 234.97 MB read + 3.85 MB written
+}
+
 
 def peaks():
     try:
@@ -317,7 +324,8 @@ def run_ours(args, cfg):
                          + " (layer-cycled)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None, "bytes_per_launch": gu_bytes},
+                         "traffic": MEASURED_TRAFFIC.get((args.model, B, args.weights)),
+                         "bytes_per_launch": gu_bytes},
             "step_roofline": {"bytes_per_step": bytes_step, "achieved_gbs": step_gbs,
                               "frac_of_measured": step_gbs / peak,
                               "frac_of_8tbs_spec": step_gbs / 8000.0},
