@@ -328,13 +328,20 @@ GemvArgs norm_args(reng_model* m, int M, const float* gain) {
 // Rows of a step above which projections run on the tcgen05 GEMM (bf16
 // weights); at or below it the GEMV kernels (mma N = kMaxRows) stream the
 // weights with the rows in registers.
-bool use_gemm(const reng_model* m, int M) { return !m->w8 && M > kMaxRows; }
+// From 4 rows on, down_proj (kind 3) and the LM head (kind 4) also run on the
+// GEMM: their GEMV would stage 4-8 rows of a wide x (inter = 14336) or
+// share shared memory with it, leaving the weight ring short (measured at
+// batch 8: down 52 -> 47 us).
+bool use_gemm(const reng_model* m, int M, int kind) {
+    if (m->w8) return false;
+    return M > kMaxRows || (M >= 4 && (kind == 3 || kind == 4));
+}
 
 // One projection: the GEMV for few rows, else (RMSNorm of x into xn when the
 // projection normalises its input) the tcgen05 GEMM over N = M rounded up
 // to 16 columns.  kind indexes the GEMV launch shapes.
 int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cudaStream_t st) {
-    if (!use_gemm(m, g.M)) {
+    if (!use_gemm(m, g.M, kind)) {
         CU(launch_gemv(g, epi, m->shape[kind][g.M > 2], max_grid, true, st));
         m->launches++;
         return RENG_OK;
