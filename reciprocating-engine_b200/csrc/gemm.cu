@@ -542,12 +542,19 @@ int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out)
 
 size_t gemm_smem_bytes(int n, int stages) { return (size_t)stages * (kStageA + (size_t)n * 128) + 1024; }
 
-int gemm_pick_stages(int n, bool /*one_per_sm*/) {
-    // Four stages.  Measured on B200 (Llama-8B widths, 64 rows): one CTA per
-    // SM with 8 stages (twice the weight bytes in flight) was slower than 4
-    // (q/k/v 55 against 33 us), so the deeper pipeline is not used.
-    int s = (int)((unsigned)kGemmStageBudget / (kStageA + (unsigned)n * 128u));
-    return s < 4 ? (s < 2 ? 2 : s) : 4;
+int gemm_pick_stages(int n, bool one_per_sm, int epi) {
+    // Two CTAs per SM (no cluster): as many stages as fit in half the SM's
+    // 228 KB beside the kernel's static shared memory, the 1 KB alignment
+    // slack and the 1 KB per-CTA reservation (6 at N = 16, 5 at N = 32, 4 at
+    // N = 64; one fewer for the LM head's argmax scratch).  One CTA per SM:
+    // 4 stages; measured on B200 (Llama-8B widths, 64 rows), 8 stages at one
+    // CTA per SM were slower than 4 (q/k/v 55 against 33 us).
+    const unsigned stage = kStageA + (unsigned)n * 128u;
+    const unsigned fixed = 2048u + (epi == EPI_LOGITS ? 9216u : 1024u);
+    int s = one_per_sm ? 4 : (int)((114u * 1024u - fixed) / stage);
+    const int fit = (int)((unsigned)kGemmStageBudget / stage);
+    if (s > fit) s = fit;
+    return s < 2 ? 2 : (s > kGemmMaxStages ? kGemmMaxStages : s);
 }
 
 template <int EPI>
@@ -613,7 +620,7 @@ void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, int* ks_out, in
         ks = (kc + kper - 1) / kper;  // every split gets at least one chunk
     }
     *ks_out = ks;
-    *stages_out = gemm_pick_stages(n, ks > 1 || n > 64);
+    *stages_out = gemm_pick_stages(n, ks > 1 || n > 64, epi);
 }
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
@@ -764,7 +771,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
         if (s > kGemmMaxSplits) s = kGemmMaxSplits;
         const int kper = (kc + s - 1) / s;
         g.ks = (kc + kper - 1) / kper;
-        g.stages = gemm_pick_stages(N, g.ks > 1 || N > 64);
+        g.stages = gemm_pick_stages(N, g.ks > 1 || N > 64, EPI_F32);
     }
     CUtensorMap tmap;
     const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);

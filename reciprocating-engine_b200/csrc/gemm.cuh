@@ -27,7 +27,7 @@ int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out)
 size_t gemm_smem_bytes(int n, int stages);
 // Pipeline stages for MMA width n: 4 with two CTAs per SM, else as many as
 // fit in about 200 KB.
-int gemm_pick_stages(int n, bool one_per_sm);
+int gemm_pick_stages(int n, bool one_per_sm, int epi);
 // Raise the dynamic shared-memory limit of every GEMM instantiation (call
 // once per device before capture).
 cudaError_t gemm_prepare();
