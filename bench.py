@@ -314,6 +314,8 @@ def run_ours(args, cfg):
                 ", tensor-parallel %d" % ws if ws > 1 else ""),
                 "model": args.model, "batch": B, "prompt": args.prompt, "weights": args.weights,
                 "parallelism": "tp%d" % ws if ws > 1 else "single",
+                "tp_exchange": {0: "none", 1: "ncclAllReduce", 2: "fused peer all-reduce (NVLink stores)"}[
+                    eng.tp_exchange()],
                 "l2": "inputs larger than L2 (weights %.1f GB streamed per step)" % (bytes_step / 1e9)},
             "clocks": clk,
             "e2e": {"value": tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B / args.steps,

@@ -277,6 +277,13 @@ int reng_gemm_bf16(const uint16_t *w, int rows, int K, const uint16_t *x, int M,
  */
 int reng_tp_unique_id(uint8_t out[128]);
 
+/* How a tensor-parallel model exchanges its partials: 0 none (world 1),
+ * 1 ncclAllReduce + a residual kernel, 2 the one-shot peer all-reduce over
+ * NVLink fused with the residual (decode steps of up to 8 rows; prefill
+ * blocks still use NCCL).  RENG_TP_P2P=0 in every rank's environment keeps
+ * NCCL.  The reference exchanges through hcclAllReduce (hccl.rs:646-651). */
+int reng_model_tp_exchange(reng_model *m, int *kind);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,10 +38,21 @@ __host__ __device__ constexpr int gemv_ring_bytes() {
     return PIPE == PIPE_TMA ? kTmaRing : 0;
 }
 
+// Ring stages issued before the wait on the previous kernel; the others go
+// out after the x copy.  Measured on B200 (Llama-8B b1 step): 2 of 4 is
+// 3.28 ms against 3.35 with all 4 ahead (x then queues behind 192 KB of
+// weights per SM) and 3.38 with none.
+constexpr int kPreStages = 2;
+
 template <int EPI, int NWARP, int PIPE, int W8>
 __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     extern __shared__ __align__(128) uint8_t smem_dyn[];
-    __shared__ float4 red[NWARP > 1 ? NWARP : 1][32];
+    // the warps' tile reduction; before the first tile it holds the RMS
+    // partials of the rows (bulk-copied with x): 4-warp CTAs up to 2 KB,
+    // 8-warp CTAs up to kMaxRows x 256 partials
+    constexpr int kRedF4 = NWARP * 32, kSsF4 = NWARP == 4 ? kRedF4 : kMaxRows * 256 / 4;
+    __shared__ __align__(16) float4 red_buf[kRedF4 > kSsF4 ? kRedF4 : kSsF4];
+    float4(*red)[32] = reinterpret_cast<float4(*)[32]>(red_buf);
     __shared__ float inv_s[kMaxRows];
     __shared__ int s_ids[kMaxRows];
     __shared__ int s_last;
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
             for (int s2 = 0; s2 < kTmaStages; s2++) mbar_init(bar0 + s2 * 8, 1);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            for (int j = 0; j < kTmaStages; j++) tma_issue(j);
+            for (int j = 0; j < kPreStages; j++) tma_issue(j);
         }
         __syncwarp();
     } else {
@@ -121,6 +132,11 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         }
         rload(0);
     }
+    // the RMSNorm gains of this thread's k-groups (constants: before the wait)
+    constexpr int GV = NWARP == 4 ? 5 : 3;  // k-groups per thread: K <= 5120 (4 warps), 6144 (8)
+    float4 gp[GV][2];
+    const bool gain_pre = a.ss_in != nullptr && use_smem && K / 8 <= GV * NWARP * 32;
+    if (gain_pre) gain_preload<GV>(a, K, gp);
 
     pdl_wait();
     pdl_launch();
@@ -129,20 +145,42 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     // shared memory, while the warps reduce the RMS partials
     const int xstride = gemv_xstride(K);
     uint16_t* xsm = reinterpret_cast<uint16_t*>(smem_dyn + NWARP * gemv_ring_bytes<PIPE>());
+    // the RMS partials ride with x when they fit the reduction buffer (plain
+    // loads here queue behind the weight stream already in flight: 2-3 us)
+    const bool ss_tma = a.ss_in != nullptr && use_smem && (a.ss_tiles & 3) == 0 &&
+                        a.M * a.ss_tiles * 4 <= (int)sizeof(red_buf);
     if (use_smem) {
         __syncthreads();  // barrier init visible to every thread before any wait
         if (threadIdx.x == 0) {
-            mbar_expect_tx(xbar_a, (uint32_t)(a.M * K * 2));
+            const uint32_t ssb = (uint32_t)(a.ss_tiles * 4);
+            mbar_expect_tx(xbar_a, (uint32_t)(a.M * K * 2) + (ss_tma ? a.M * ssb : 0u));
             for (int m = 0; m < a.M; m++)
                 tma_load_1d((uint32_t)__cvta_generic_to_shared(xsm + m * xstride), a.x + (size_t)m * a.ldx,
                             (uint32_t)(K * 2), xbar_a);
+            if (ss_tma)
+                for (int m = 0; m < a.M; m++)
+                    tma_load_1d((uint32_t)__cvta_generic_to_shared(red_buf) + m * ssb, a.ss_in + (size_t)m * kSsStride,
+                                ssb, xbar_a);
         }
     }
-    if (a.ss_in != nullptr) {
+    // the rest of the ring behind x (the copies issued so far stand in front
+    // of x in the SM's queue)
+    if (PIPE == PIPE_TMA) {
+        __syncwarp();
+        if (lane == 0)
+            for (int j = kPreStages; j < kTmaStages; j++) tma_issue(j);
+        __syncwarp();
+    }
+    if (a.ss_in != nullptr && !ss_tma) {
         for (int m = warp; m < a.M; m += NWARP) {
             float s = 0.0f;
-#pragma unroll 8
-            for (int t = lane; t < a.ss_tiles; t += 32) s += a.ss_in[t * kRowsCap + m];
+            const float4* sp = reinterpret_cast<const float4*>(a.ss_in + (size_t)m * kSsStride);
+#pragma unroll 4
+            for (int t = lane; t < a.ss_tiles / 4; t += 32) {
+                const float4 v = sp[t];
+                s += (v.x + v.y) + (v.z + v.w);
+            }
+            for (int t = (a.ss_tiles & ~3) + lane; t < a.ss_tiles; t += 32) s += a.ss_in[(size_t)m * kSsStride + t];
             s = warp_sum(s);
             if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
         }
@@ -153,9 +191,22 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
             failed = true;
             if (threadIdx.x == 0) atomicExch(a.err, RENG_E_TIMEOUT);
         }
+        if (ss_tma) {
+            for (int m = warp; m < a.M; m += NWARP) {
+                const float4* sp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(red_buf) + m * a.ss_tiles);
+                float s = 0.0f;
+                for (int t = lane; t < a.ss_tiles / 4; t += 32) {
+                    const float4 v = sp[t];
+                    s += (v.x + v.y) + (v.z + v.w);
+                }
+                s = warp_sum(s);
+                if (lane == 0) inv_s[m] = 1.0f / sqrtf(s / (float)a.norm_k + a.eps);
+            }
+        }
         __syncthreads();
         if (a.ss_in != nullptr) {
-            normalise_x<W8>(a, xsm, xstride, K, inv_s);
+            if (gain_pre) normalise_x_pre<W8, GV>(a, xsm, xstride, K, inv_s, gp);
+            else normalise_x<W8>(a, xsm, xstride, K, inv_s);
             __syncthreads();
         } else if (W8) {
             x_to_f16(a, xsm, xstride, K);
@@ -312,9 +363,18 @@ static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStr
     if (e != cudaSuccess || per_sm < 1) per_sm = 1;
     int cap = sms * per_sm;
     if (max_grid > 0 && max_grid < cap) cap = max_grid;
-    // balanced persistent grid: every CTA gets the same number of tiles
-    const int per = (a.tiles + cap - 1) / cap;
-    const int grid = (a.tiles + per - 1) / per;
+    // persistent grid of every resident slot (tiles interleaved over the
+    // CTAs), so each SM holds the same number of CTAs: the weight stream of
+    // an SM is capped (about 50 GB/s measured on B200, two or three CTAs
+    // alike), so equal tiles per SM, not per CTA, is the balance that counts
+    // (gate/up at Llama-8B b1: 359 CTAs of 5 tiles left 63 SMs with 15
+    // tiles against 10 on the rest, a 10 us tail).  The LM head keeps equal
+    // tiles per CTA: measured 150 against 161 us with every slot filled.
+    int grid = std::min(a.tiles, cap);
+    if (EPI == EPI_LOGITS) {
+        const int per = (a.tiles + cap - 1) / cap;
+        grid = (a.tiles + per - 1) / per;
+    }
     if (grid_out) *grid_out = grid;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -602,7 +662,7 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
             for (int e = 0; e < 8; e++) ss += t[e] * t[e];
         }
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        if (i < nv && (i & 1) == 0) a.ss_out[(i >> 1) * kRowsCap + m] = ss;
+        if (i < nv && (i & 1) == 0) a.ss_out[(size_t)m * kSsStride + (i >> 1)] = ss;
     }
 }
 

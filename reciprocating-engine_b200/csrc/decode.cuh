@@ -22,6 +22,10 @@ constexpr int kBlockBytesFp8 = 1024;
 constexpr int kMaxRows = 8;    // activation rows per GEMV launch (mma N)
 constexpr int kRowsCap = 256;  // rows of a step (work buffers, RMS-partials stride)
 constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
+// RMS partials ss[m][tile] (sum of squares of 16 residual values), row
+// stride kSsStride: a row's partials are contiguous, so the kernels that
+// normalise read a few cache lines per row (hidden <= 16 * kSsStride)
+constexpr int kSsStride = 512;
 
 // Row stride (elements) of the shared x copy: 32 elements of padding put
 // consecutive rows 64 bytes apart, so the fragment loads of a warp hit 32
@@ -46,7 +50,7 @@ struct GemvArgs {
     // activations x [M][ldx] bf16
     const uint16_t* x;
     int ldx;
-    // fused RMSNorm of x: inv[m] = 1/sqrt(sum_t ss_in[t][m] / norm_k + eps),
+    // fused RMSNorm of x: inv[m] = 1/sqrt(sum_t ss_in[m][t] / norm_k + eps),
     // x' = bf16(x * inv * gain).  ss_in == nullptr: x used as is.
     const float* ss_in;
     int ss_tiles;

@@ -163,7 +163,7 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
             sq += __shfl_xor_sync(0xffffffffu, sq, 2);
             sq += __shfl_xor_sync(0xffffffffu, sq, 4);
             sq += __shfl_xor_sync(0xffffffffu, sq, 8);
-            if (live && i16 == 0) a.ss_out[tile * kRowsCap + m] = sq;
+            if (live && i16 == 0) a.ss_out[(size_t)m * kSsStride + tile] = sq;
         }
         return;
     }
@@ -640,7 +640,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, b
 }
 
 // RMS-normalise M rows into a bf16 buffer (the x operand of the tcgen05
-// GEMMs): xn = bf16(x * 1/sqrt(sum_t ss[t][m] / H + eps) * gain).
+// GEMMs): xn = bf16(x * 1/sqrt(sum_t ss[m][t] / H + eps) * gain).
 __global__ void __launch_bounds__(256) k_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles,
                                                       const float* gain, float eps, int H, uint16_t* xn) {
     const int m = blockIdx.x;
@@ -649,7 +649,12 @@ __global__ void __launch_bounds__(256) k_rmsnorm_rows(const uint16_t* x, const f
     pdl_launch();
     if (threadIdx.x < 32) {
         float s = 0.f;
-        for (int t = threadIdx.x; t < ss_tiles; t += 32) s += ss[t * kRowsCap + m];
+        const float4* sp = reinterpret_cast<const float4*>(ss + (size_t)m * kSsStride);
+        for (int t = threadIdx.x; t < ss_tiles / 4; t += 32) {
+            const float4 v = sp[t];
+            s += (v.x + v.y) + (v.z + v.w);
+        }
+        for (int t = (ss_tiles & ~3) + threadIdx.x; t < ss_tiles; t += 32) s += ss[(size_t)m * kSsStride + t];
         s = warp_sum(s);
         if (threadIdx.x == 0) inv_s = 1.0f / sqrtf(s / (float)H + eps);
     }

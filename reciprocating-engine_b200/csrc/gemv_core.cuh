@@ -48,6 +48,52 @@ __device__ __forceinline__ void normalise_x(const GemvArgs& a, uint16_t* xs, int
     }
 }
 
+// The same with the gains already in registers: thread t owns the 8-wide
+// k-groups t + j * blockDim.x (j < GV), loaded before the kernel waited on
+// its predecessor (the gains are constants), so the normalisation after
+// the wait costs no global round trip.
+template <int GV>
+__device__ __forceinline__ void gain_preload(const GemvArgs& a, int K, float4 (&gp)[GV][2]) {
+    const int nv = K / 8;
+#pragma unroll
+    for (int j = 0; j < GV; j++) {
+        const int kv = threadIdx.x + j * blockDim.x;
+        if (kv < nv) {
+            gp[j][0] = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * kv);
+            gp[j][1] = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * kv + 1);
+        }
+    }
+}
+
+template <int W8, int GV>
+__device__ __forceinline__ void normalise_x_pre(const GemvArgs& a, uint16_t* xs, int xstride, int K,
+                                                const float* inv_s, const float4 (&gp)[GV][2]) {
+    const int nv = K / 8;
+#pragma unroll
+    for (int j = 0; j < GV; j++) {
+        const int kv = threadIdx.x + j * blockDim.x;
+        if (kv >= nv) continue;
+        const float4 g0 = gp[j][0], g1 = gp[j][1];
+        for (int m = 0; m < a.M; m++) {
+            uint4* p = reinterpret_cast<uint4*>(xs + m * xstride + kv * 8);
+            uint4 v = *p;
+            const float inv = inv_s[m];
+            if (W8) {
+                v.x = pack_f16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+                v.y = pack_f16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+                v.z = pack_f16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+                v.w = pack_f16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+            } else {
+                v.x = pack_bf16x2(bf16lo(v.x) * inv * g0.x, bf16hi(v.x) * inv * g0.y);
+                v.y = pack_bf16x2(bf16lo(v.y) * inv * g0.z, bf16hi(v.y) * inv * g0.w);
+                v.z = pack_bf16x2(bf16lo(v.z) * inv * g1.x, bf16hi(v.z) * inv * g1.y);
+                v.w = pack_bf16x2(bf16lo(v.w) * inv * g1.z, bf16hi(v.w) * inv * g1.w);
+            }
+            *p = v;
+        }
+    }
+}
+
 // Staged bf16 x rows -> f16 in place (FP8-weight kernels without a norm).
 __device__ __forceinline__ void x_to_f16(const GemvArgs& a, uint16_t* xs, int xstride, int K) {
     const int nv = K / 8;
@@ -182,8 +228,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
             s1 += __shfl_xor_sync(0xffffffffu, s1, o);
         }
         if (g == 0) {
-            if (m0 < a.M) a.ss_out[tile * kRowsCap + m0] = s0;
-            if (m1 < a.M) a.ss_out[tile * kRowsCap + m1] = s1;
+            if (m0 < a.M) a.ss_out[(size_t)m0 * kSsStride + tile] = s0;
+            if (m1 < a.M) a.ss_out[(size_t)m1 * kSsStride + tile] = s1;
         }
     } else if (EPI == EPI_F32) {
         const int r0 = tile * kTileRows + g, r1 = r0 + 8;

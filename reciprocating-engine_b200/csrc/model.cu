@@ -21,6 +21,9 @@ int tp_init(reng_model* m, const uint8_t* id);
 void tp_destroy(reng_model* m);
 cudaError_t tp_allreduce(reng_model* m, float* buf, size_t count, cudaStream_t st);
 cudaError_t launch_tp_residual(reng_model* m, const float* part, int M, bool pdl, cudaStream_t st);
+cudaError_t launch_tp_ar_residual(reng_model* m, const float* part, int M, cudaStream_t st);
+bool tp_p2p(reng_model* m, int M);
+int tp_exchange_kind(reng_model* m);
 int gemv_blocks_per_sm(int epi, int nwarp);
 }  // namespace reng
 
@@ -251,6 +254,8 @@ int validate(const reng_model_desc* d) {
                        std::to_string(d->n_kv_heads) + " / intermediate " + std::to_string(d->inter) +
                        " are not divisible by " + std::to_string(d->tp_world));
     RENG_CHECK_ARG(d->hidden % 16 == 0, "reng_model_create: hidden must be a multiple of 16");
+    if (d->hidden > 16 * kSsStride)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: hidden above " + std::to_string(16 * kSsStride));
     RENG_CHECK_ARG(d->head_dim % 16 == 0 && d->head_dim <= 128,
                    "reng_model_create: head_dim must be a multiple of 16 and <= 128");
     RENG_CHECK_ARG(d->n_heads / d->n_kv_heads <= 8, "reng_model_create: more than 8 query heads per KV head");
@@ -445,8 +450,12 @@ int k_proj_launch(reng_model* m, int l, int M, int which, cudaStream_t st) {
     const int kind = which == 0 ? 1 : 3;
     if (m->world > 1) {
         TRY(linear(m, o, EPI_F32, kind, 0, st));
-        CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, st));
-        CU(launch_tp_residual(m, m->part, M, false, st));
+        if (tp_p2p(m, M)) {  // decode: one-shot peer all-reduce fused with the residual
+            CU(launch_tp_ar_residual(m, m->part, M, st));
+        } else {
+            CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, st));
+            CU(launch_tp_residual(m, m->part, M, false, st));
+        }
         m->launches++;
     } else {
         TRY(linear(m, o, EPI_RESID, kind, 0, st));
@@ -475,7 +484,7 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
 GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0) {
     GemvArgs h = norm_args(m, M, m->final_gamma);
     h.x = m->x_res + (size_t)r0 * m->hidden;
-    h.ss_in = m->ss + r0;
+    h.ss_in = m->ss + (size_t)r0 * kSsStride;
     h.w = m->lm;
     h.tiles = m->lm_tiles;
     h.out = m->logits;
@@ -819,7 +828,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->attn, (size_t)MR * m->q_dim));
     TRY(dalloc(m, &m->act, (size_t)MR * m->inter));
     TRY(dalloc(m, &m->logits, (size_t)MR * m->vocab));
-    TRY(dalloc(m, &m->ss, (size_t)(H / kTileRows) * MR));
+    TRY(dalloc(m, &m->ss, (size_t)kSsStride * MR));
     TRY(dalloc(m, &m->part, (size_t)MR * H));
     TRY(dalloc(m, &m->row_slot, MR));
     TRY(dalloc(m, &m->row_pos, MR));
@@ -833,7 +842,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(cudaMemsetAsync(m->pos, 0, (size_t)m->B * 4, m->st));
     CU(cudaMemsetAsync(m->step, 0, 4, m->st));
     CU(cudaMemsetAsync(m->x_res, 0, (size_t)MR * H * 2, m->st));
-    CU(cudaMemsetAsync(m->ss, 0, (size_t)(H / kTileRows) * MR * 4, m->st));
+    CU(cudaMemsetAsync(m->ss, 0, (size_t)kSsStride * MR * 4, m->st));
 
     // launch shapes
     const int kch = (H + kChunkK - 1) / kChunkK;
@@ -1073,6 +1082,13 @@ extern "C" int reng_model_position(const reng_model* m, int slot, int* pos) {
     return RENG_OK;
 }
 
+extern "C" int reng_model_tp_exchange(reng_model* m, int* kind) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(kind != nullptr, "reng_model_tp_exchange: NULL");
+    *kind = tp_exchange_kind(m);
+    return RENG_OK;
+}
+
 extern "C" int reng_model_device_bytes(const reng_model* m, uint64_t* bytes) {
     TRY(check_model(m));
     RENG_CHECK_ARG(bytes != nullptr, "reng_model_device_bytes: NULL");
@@ -1177,4 +1193,5 @@ int tp_device_of(reng_model* m) { return m->dev; }
 uint16_t* tp_x_res(reng_model* m) { return m->x_res; }
 float* tp_ss(reng_model* m) { return m->ss; }
 int tp_hidden(reng_model* m) { return m->hidden; }
+int* tp_err(reng_model* m) { return m->err; }
 }  // namespace reng

@@ -313,7 +313,7 @@ __device__ void embed_phase(const EmbedArgs& e) {
             for (int k = 0; k < 8; k++) ss += f[k] * f[k];
         }
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);  // nv is even: lanes 2j, 2j+1 hold one 16-wide tile
-        if (live && (i & 1) == 0) e.ss_out[(i >> 1) * kRowsCap + m] = ss;
+        if (live && (i & 1) == 0) e.ss_out[(size_t)m * kSsStride + (i >> 1)] = ss;
     }
 }
 
@@ -570,10 +570,10 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) k_step(StepCtl c) {
 #pragma unroll
                     for (int r = 0; r < 2; r++) {
                         const int t = threadIdx.x + r * kStepWarps * 32;
-                        v[m][r] = (m < M && t < a.ss_tiles) ? __ldcg(a.ss_in + t * kRowsCap + m) : 0.f;
+                        v[m][r] = (m < M && t < a.ss_tiles) ? __ldcg(a.ss_in + (size_t)m * kSsStride + t) : 0.f;
                     }
                 for (int t = threadIdx.x + 2 * kStepWarps * 32; t < a.ss_tiles; t += kStepWarps * 32)
-                    for (int m = 0; m < M; m++) v[m][0] += __ldcg(a.ss_in + t * kRowsCap + m);
+                    for (int m = 0; m < M; m++) v[m][0] += __ldcg(a.ss_in + (size_t)m * kSsStride + t);
 #pragma unroll
                 for (int m = 0; m < kMaxRows; m++) {
                     const float sm = warp_sum(v[m][0] + v[m][1]);

@@ -3,6 +3,21 @@
 // TpModel, crates/reng-synapse/src/tp.rs:1-42 and :709-793, with its HCCL
 // all-reduce, hccl.rs:477-506 / :646-651).
 //
+// Two exchanges:
+//  * decode steps (rows <= kMaxRows): a one-shot all-reduce over NVLink
+//    peer memory fused with the residual add.  Every rank owns a receive
+//    area mapped into every other rank's address space (CUDA IPC handles,
+//    exchanged once through the NCCL communicator).  CTA c of the kernel
+//    takes hidden slice c: it stores its f32 partial slice into every peer's
+//    area (plain peer stores over NVLink; no multicast), raises its flag on
+//    every peer with a system-scope release, waits (bounded) for the peers'
+//    flags of the same slice, sums the W partials in rank order (the same
+//    order on every rank, so every rank gets the same bits), casts to bf16,
+//    adds the residual in bf16 and writes the slice's norm partials.  One
+//    launch instead of an NCCL all-reduce and a residual kernel.
+//  * prefill blocks (and worlds where the peer mappings cannot be made):
+//    ncclAllReduce in place, then the residual kernel.
+//
 // NCCL is resolved at run time with dlopen: a process that already holds a
 // libnccl (torch's) reuses it, so the two never mix.  Only the types come
 // from nccl.h.
@@ -11,8 +26,9 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
-#include "decode.cuh"
+#include "gemv_core.cuh"
 
 struct reng_model;
 
@@ -25,6 +41,7 @@ int tp_device_of(reng_model* m);
 uint16_t* tp_x_res(reng_model* m);
 float* tp_ss(reng_model* m);
 int tp_hidden(reng_model* m);
+int* tp_err(reng_model* m);
 
 namespace {
 struct NcclApi {
@@ -32,6 +49,7 @@ struct NcclApi {
     ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     std::string err;
@@ -52,12 +70,197 @@ NcclApi* api() {
         a.GetUniqueId = (decltype(a.GetUniqueId))dlsym(h, "ncclGetUniqueId");
         a.CommInitRank = (decltype(a.CommInitRank))dlsym(h, "ncclCommInitRank");
         a.AllReduce = (decltype(a.AllReduce))dlsym(h, "ncclAllReduce");
+        a.AllGather = (decltype(a.AllGather))dlsym(h, "ncclAllGather");
         a.CommDestroy = (decltype(a.CommDestroy))dlsym(h, "ncclCommDestroy");
         a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
-        a.ok = a.GetUniqueId && a.CommInitRank && a.AllReduce && a.CommDestroy && a.GetErrorString;
+        a.ok = a.GetUniqueId && a.CommInitRank && a.AllReduce && a.AllGather && a.CommDestroy && a.GetErrorString;
         if (!a.ok) a.err = "libnccl.so.2 lacks a symbol";
     });
     return &a;
+}
+
+constexpr int kArSlice = 256;    // hidden elements per CTA of the peer all-reduce
+constexpr int kArThreads = 64;   // a float4 of the slice per thread
+constexpr int kArMaxWorld = 8;
+
+// The peer all-reduce arguments.  Receive area of a rank: [2 parities]
+// [W source ranks][kMaxRows][hidden] f32; flags of a rank: [W sources][C
+// slices] u32 holding the epoch the source last delivered.
+struct ArArgs {
+    float* recv[kArMaxWorld];      // every rank's receive area (peer mappings; own at [rank])
+    unsigned* flags[kArMaxWorld];  // every rank's flags
+    const float* part;             // this rank's partial [M][hidden]
+    unsigned* epoch;               // [C] exchanges done per slice (this rank only)
+    uint16_t* x_res;               // [M][hidden]
+    float* ss;                     // norm partials [M][kSsStride]
+    int* err;
+    int rank, world, hidden, M;
+};
+
+struct TpState {
+    ncclComm_t comm = nullptr;
+    bool p2p = false;              // the peer all-reduce is set up
+    void* region = nullptr;        // this rank's flags + receive area (exported)
+    unsigned* epoch = nullptr;
+    std::vector<void*> mapped;     // peers' regions opened in this process
+    ArArgs ar{};
+};
+
+size_t ar_flag_bytes(int world, int hidden) {
+    const int C = (hidden + kArSlice - 1) / kArSlice;
+    return ((size_t)world * C * 4 + 255) / 256 * 256;
+}
+size_t ar_recv_floats(int world, int hidden) { return (size_t)2 * world * kMaxRows * hidden; }
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kArThreads) k_tp_ar_residual(ArArgs a) {
+    const int c = blockIdx.x, C = gridDim.x, t = threadIdx.x;
+    const int i0 = c * kArSlice + 4 * t;  // this thread's 4 elements (hidden % 16 == 0)
+    const bool live = i0 < a.hidden;
+    pdl_wait();
+    pdl_launch();
+    const unsigned e = a.epoch[c] + 1;
+    const size_t par = (size_t)(e & 1) * a.world * kMaxRows * a.hidden;
+    // 1. push this rank's partial slice into every peer's area
+    float4 mine[kMaxRows];
+#pragma unroll
+    for (int m = 0; m < kMaxRows; m++)
+        if (m < a.M && live) mine[m] = __ldcg(reinterpret_cast<const float4*>(a.part + (size_t)m * a.hidden + i0));
+    if (live)
+        for (int r = 0; r < a.world; r++) {
+            if (r == a.rank) continue;
+            float* dst = a.recv[r] + par + (size_t)a.rank * kMaxRows * a.hidden + i0;
+#pragma unroll
+            for (int m = 0; m < kMaxRows; m++)
+                if (m < a.M) *reinterpret_cast<float4*>(dst + (size_t)m * a.hidden) = mine[m];
+        }
+    __syncthreads();
+    // 2. slice c delivered: flag it on every peer; 3. wait for the peers' slice c
+    if (t < a.world && t != a.rank) {
+        __threadfence_system();
+        st_release_sys(a.flags[t] + a.rank * C + c, e);
+        const unsigned* f = a.flags[a.rank] + t * C + c;
+        if (ld_acquire_sys(f) < e) {
+            const unsigned long long t0 = globaltimer();
+            while (ld_acquire_sys(f) < e)
+                if (globaltimer() - t0 > kWaitNs) {
+                    atomicExch(a.err, RENG_E_TIMEOUT);
+                    break;
+                }
+        }
+    }
+    __syncthreads();
+    // 4. sum in rank order, bf16 residual add, norm partials of 16-wide tiles
+    const float* own = a.recv[a.rank] + par;
+#pragma unroll
+    for (int m = 0; m < kMaxRows; m++) {
+        if (m >= a.M) break;
+        float sq = 0.f;
+        if (live) {
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < a.world; r++) {
+                const float4 v = r == a.rank ? mine[m]
+                                             : __ldcg(reinterpret_cast<const float4*>(
+                                                   own + ((size_t)r * kMaxRows + m) * a.hidden + i0));
+                if (r == 0) {
+                    s = v;
+                } else {
+                    s.x += v.x;
+                    s.y += v.y;
+                    s.z += v.z;
+                    s.w += v.w;
+                }
+            }
+            uint2* xp = reinterpret_cast<uint2*>(a.x_res + (size_t)m * a.hidden + i0);
+            const uint2 x = *xp;
+            const float r0 = round_bf16(bf16lo(x.x) + round_bf16(s.x)), r1 = round_bf16(bf16hi(x.x) + round_bf16(s.y));
+            const float r2 = round_bf16(bf16lo(x.y) + round_bf16(s.z)), r3 = round_bf16(bf16hi(x.y) + round_bf16(s.w));
+            *xp = make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
+            sq = r0 * r0 + r1 * r1 + r2 * r2 + r3 * r3;
+        }
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        if (live && (t & 3) == 0) a.ss[(size_t)m * kSsStride + i0 / 16] = sq;
+    }
+    __syncthreads();
+    if (t == 0) a.epoch[c] = e;
+}
+
+// Sets up the peer all-reduce: allocate and export this rank's region,
+// all-gather the IPC handles over NCCL, open the peers', and agree (an
+// NCCL min over the ranks' outcomes) so every rank takes the same path.
+// Returns false (after undoing what it did) when any rank could not.
+bool ar_setup(reng_model* m, TpState* s, NcclApi* a) {
+    const int W = tp_world_of(m), R = tp_rank_of(m), H = tp_hidden(m);
+    const char* env = getenv("RENG_TP_P2P");
+    if (env && atoi(env) == 0) return false;  // every rank reads the same environment
+    int ok = W <= kArMaxWorld && H % 16 == 0 ? 1 : 0;
+    const size_t fb = ar_flag_bytes(W, H), bytes = fb + ar_recv_floats(W, H) * 4;
+    const int C = (H + kArSlice - 1) / kArSlice;
+    cudaIpcMemHandle_t mine{};
+    if (ok && cudaMalloc(&s->region, bytes) != cudaSuccess) ok = 0;
+    if (ok && cudaMemset(s->region, 0, bytes) != cudaSuccess) ok = 0;
+    if (ok && cudaMalloc((void**)&s->epoch, (size_t)C * 4) != cudaSuccess) ok = 0;
+    if (ok && cudaMemset(s->epoch, 0, (size_t)C * 4) != cudaSuccess) ok = 0;
+    if (ok && cudaIpcGetMemHandle(&mine, s->region) != cudaSuccess) ok = 0;
+    cudaGetLastError();
+    // exchange: [W] handles, then the agreement word
+    uint8_t* dev = nullptr;
+    std::vector<cudaIpcMemHandle_t> all(W);
+    int agree = 0;
+    if (cudaMalloc((void**)&dev, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t) + 16) != cudaSuccess) return false;
+    uint8_t* send = dev + (size_t)W * sizeof(cudaIpcMemHandle_t);
+    int* okd = reinterpret_cast<int*>(send + sizeof(cudaIpcMemHandle_t));
+    bool done = cudaMemcpy(send, &mine, sizeof(mine), cudaMemcpyHostToDevice) == cudaSuccess &&
+                a->AllGather(send, dev, sizeof(mine), ncclChar, s->comm, 0) == ncclSuccess &&
+                cudaMemcpy(all.data(), dev, (size_t)W * sizeof(mine), cudaMemcpyDeviceToHost) == cudaSuccess;
+    s->ar = ArArgs{};
+    if (done && ok) {
+        for (int r = 0; r < W; r++) {
+            if (r == R) {
+                s->ar.recv[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(s->region) + fb);
+                s->ar.flags[r] = static_cast<unsigned*>(s->region);
+                continue;
+            }
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            s->mapped.push_back(p);
+            s->ar.recv[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(p) + fb);
+            s->ar.flags[r] = static_cast<unsigned*>(p);
+        }
+    }
+    done = done && cudaMemcpy(okd, &ok, 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+           a->AllReduce(okd, okd, 1, ncclInt32, ncclMin, s->comm, 0) == ncclSuccess &&
+           cudaMemcpy(&agree, okd, 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(dev);
+    if (done && agree == 1) {
+        s->p2p = true;
+        s->ar.epoch = s->epoch;
+        s->ar.rank = R;
+        s->ar.world = W;
+        s->ar.hidden = H;
+        return true;
+    }
+    for (void* p : s->mapped) cudaIpcCloseMemHandle(p);
+    s->mapped.clear();
+    if (s->region) cudaFree(s->region);
+    if (s->epoch) cudaFree(s->epoch);
+    s->region = nullptr;
+    s->epoch = nullptr;
+    cudaGetLastError();
+    return false;
 }
 }  // namespace
 
@@ -67,29 +270,77 @@ int tp_init(reng_model* m, const uint8_t* id) {
     ncclUniqueId uid;
     static_assert(sizeof(uid) == 128, "ncclUniqueId is 128 bytes");
     memcpy(&uid, id, sizeof(uid));
-    ncclComm_t comm = nullptr;
     cudaSetDevice(tp_device_of(m));
-    ncclResult_t r = a->CommInitRank(&comm, tp_world_of(m), uid, tp_rank_of(m));
-    if (r != ncclSuccess) return fail(RENG_E_NCCL, std::string("ncclCommInitRank: ") + a->GetErrorString(r));
-    tp_set_handle(m, comm);
+    TpState* s = new TpState();
+    ncclResult_t r = a->CommInitRank(&s->comm, tp_world_of(m), uid, tp_rank_of(m));
+    if (r != ncclSuccess) {
+        delete s;
+        return fail(RENG_E_NCCL, std::string("ncclCommInitRank: ") + a->GetErrorString(r));
+    }
+    tp_set_handle(m, s);
+    ar_setup(m, s, a);
     return RENG_OK;
 }
 
 void tp_destroy(reng_model* m) {
-    void* h = tp_handle(m);
-    if (h && api()->ok) api()->CommDestroy((ncclComm_t)h);
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    if (!s) return;
+    // every exchange this rank took part in has completed (the caller
+    // synchronised its stream): a peer's last stores into this region came
+    // before the flags this rank waited for, and this rank's stores into
+    // the peers' regions before the flags they wait for
+    for (void* p : s->mapped) cudaIpcCloseMemHandle(p);
+    if (s->region) cudaFree(s->region);
+    if (s->epoch) cudaFree(s->epoch);
+    if (s->comm && api()->ok) api()->CommDestroy(s->comm);
+    delete s;
     tp_set_handle(m, nullptr);
+}
+
+// 0 no exchange (world 1), 1 NCCL, 2 the peer all-reduce for decode steps.
+int tp_exchange_kind(reng_model* m) {
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    if (!s) return 0;
+    return s->p2p ? 2 : 1;
+}
+
+bool tp_p2p(reng_model* m, int M) {
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    return s && s->p2p && M <= kMaxRows;
 }
 
 cudaError_t tp_allreduce(reng_model* m, float* buf, size_t count, cudaStream_t st) {
     NcclApi* a = api();
-    if (!a->ok || !tp_handle(m)) return cudaErrorNotReady;
-    ncclResult_t r = a->AllReduce(buf, buf, count, ncclFloat32, ncclSum, (ncclComm_t)tp_handle(m), st);
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    if (!a->ok || !s) return cudaErrorNotReady;
+    ncclResult_t r = a->AllReduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st);
     if (r != ncclSuccess) {
         set_error(std::string("ncclAllReduce: ") + a->GetErrorString(r));
         return cudaErrorUnknown;
     }
     return cudaSuccess;
+}
+
+// The peer all-reduce + residual of M <= kMaxRows rows of partials.
+cudaError_t launch_tp_ar_residual(reng_model* m, const float* part, int M, cudaStream_t st) {
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    if (!s || !s->p2p || M < 1 || M > kMaxRows) return cudaErrorInvalidValue;
+    ArArgs a = s->ar;
+    a.part = part;
+    a.x_res = tp_x_res(m);
+    a.ss = tp_ss(m);
+    a.err = tp_err(m);
+    a.M = M;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3((unsigned)((a.hidden + kArSlice - 1) / kArSlice));
+    cfg.blockDim = dim3(kArThreads);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_tp_ar_residual, a);
 }
 
 // x_res = bf16(x_res + bf16(partial)) (tp.rs:17-21: f32 partials reduced in
@@ -122,7 +373,7 @@ __global__ void __launch_bounds__(256) k_tp_residual(uint16_t* x_res, const floa
             *xp = o;
         }
         s += __shfl_xor_sync(0xffffffffu, s, 1);
-        if (i < nv && (i & 1) == 0) ss[(i >> 1) * kRowsCap + m] = s;
+        if (i < nv && (i & 1) == 0) ss[(size_t)m * kSsStride + (i >> 1)] = s;
     }
 }
 

@@ -215,6 +215,12 @@ class Engine:
         _lib.call("reng_model_last_times", self.h, C.byref(t))
         return t
 
+    def tp_exchange(self):
+        """0 none (world 1), 1 NCCL all-reduce, 2 the fused peer all-reduce."""
+        k = C.c_int(0)
+        _lib.call("reng_model_tp_exchange", self.h, C.byref(k))
+        return int(k.value)
+
 
 class Generator:
     """One sequence (reng-model Generator, lib.rs:2807-3023)."""

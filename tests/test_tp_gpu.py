@@ -1,9 +1,11 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): every rank holds
-its shard, the o_proj/down_proj partials are all-reduced over NCCL inside the
-captured step, all ranks produce the same ids (the reference's coordinator
-rule, crates/reng-model/src/bin/tp.rs:604-675), and those ids follow the f32
-host forward of the full model under teacher forcing (near-tie margin 0.5),
-with the prompt's last logits within cosine 0.999 of it.
+its shard, the o_proj/down_proj partials are all-reduced inside the captured
+step (the fused peer all-reduce over NVLink for decode steps, NCCL for the
+prefill blocks; NCCL throughout with RENG_TP_P2P=0), all ranks produce the
+same ids (the reference's coordinator rule, crates/reng-model/src/bin/tp.rs:
+604-675), and those ids follow the f32 host forward of the full model under
+teacher forcing (near-tie margin 0.5), with the prompt's last logits within
+cosine 0.999 of it.
 """
 import os
 import socket
@@ -24,21 +26,22 @@ def _free_port():
     return p
 
 
-def _cfg(bias):
+def _cfg(bias, hidden=256):
     from reng.config import LlamaConfig
-    return LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+    return LlamaConfig(hidden_size=hidden, intermediate_size=512, num_hidden_layers=2,
                        num_attention_heads=4, num_key_value_heads=2, head_dim_=64, vocab_size=1024,
                        rms_norm_eps=1e-5, rope_theta=10000.0, attention_bias=bias,
                        model_type="qwen2" if bias else "llama")
 
 
-def _worker(rank, port, bias, q):
+def _worker(rank, port, bias, hidden, batch, p2p, q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "reciprocating-engine_b200"))
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
+    os.environ["RENG_TP_P2P"] = "1" if p2p else "0"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
@@ -46,23 +49,28 @@ def _worker(rank, port, bias, q):
         from reng.synth import prompt_ids
         from reng.tp import TpGenerator, check_agreement, share_unique_id
         from reng.weights import random_weights
-        cfg = _cfg(bias)
+        cfg = _cfg(bias, hidden)
         w = random_weights(cfg, seed=21)
         uid = share_unique_id(dist)
-        g = TpGenerator(w, cfg, rank, WORLD, uid, batch=1, capacity=64, device=rank)
+        g = TpGenerator(w, cfg, rank, WORLD, uid, batch=batch, capacity=64, device=rank)
+        kind = g.engine.tp_exchange()
         prompt = prompt_ids(13, cfg.vocab_size, seed=2)
         last = g.engine.prefill(0, prompt, last_logits=True)
+        for b in range(1, batch):  # the other slots decode the same prompt
+            g.engine.prefill(b, prompt)
         nxt = last[0]
-        ids = g.generate([nxt], 12)
-        check_agreement([nxt] + ids, dist)
-        q.put((rank, {"nxt": nxt, "ids": ids, "last": last[1]}))
+        ids = np.array(g.generate([nxt] * batch, 12)).reshape(12, batch)
+        check_agreement([nxt] + [int(x) for x in ids.reshape(-1)], dist)
+        q.put((rank, {"nxt": nxt, "ids": [int(x) for x in ids[:, 0]], "rows": ids.tolist(), "last": last[1],
+                      "kind": kind}))
         g.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("bias", [False, True])
-def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias):
+@pytest.mark.parametrize("bias,hidden,batch,p2p", [(False, 320, 1, True), (True, 256, 1, True),
+                                                   (False, 256, 3, True), (False, 320, 1, False)])
+def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias, hidden, batch, p2p):
     import torch
     if torch.cuda.device_count() < WORLD:
         pytest.skip("needs %d GPUs" % WORLD)
@@ -74,15 +82,16 @@ def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, port, bias, q)) for r in range(WORLD)]
+    ps = [ctx.Process(target=_worker, args=(r, port, bias, hidden, batch, p2p, q)) for r in range(WORLD)]
     for p in ps:
         p.start()
     out = dict(q.get(timeout=600) for _ in ps)
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert out[0]["ids"] == out[1]["ids"] and out[0]["nxt"] == out[1]["nxt"]
-    cfg = _cfg(bias)
+    assert out[0]["rows"] == out[1]["rows"] and out[0]["nxt"] == out[1]["nxt"]
+    assert out[0]["kind"] == out[1]["kind"] == (2 if p2p else 1)
+    cfg = _cfg(bias, hidden)
     w = random_weights(cfg, seed=21)
     prompt = prompt_ids(13, cfg.vocab_size, seed=2)
     seq = np.concatenate([prompt, [out[0]["nxt"]], out[0]["ids"][:-1]]).astype(np.uint32)
