@@ -488,15 +488,32 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     const int s = (int)cluster.block_rank(), ns = (int)cluster.num_blocks();
     const int grp = blockIdx.y, m = blockIdx.z;
     const int hd = a.hd, hpg = a.hpg, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_wait();
-    pdl_launch();
-    const int pos = a.row_pos[m];
+    // Before the wait on the q/k/v kernel: the row's position and slot (set
+    // by the step's embedding gather, two launches back) and this slice's
+    // first key tile except the keys that kernel writes (the current
+    // position; in a prefill block every position from the block's first).
+    const int pos = __ldcg(a.row_pos + m);
     const int nkeys = min(pos + 1, a.cap);
     const int per = (nkeys + ns - 1) / ns;
     const int k0 = min(nkeys, s * per), k1 = min(nkeys, k0 + per);
-    const int slot = a.row_slot[m];
+    const int slot = __ldcg(a.row_slot + m);
     const size_t cache_base = (((size_t)slot * a.n_kv + grp) * a.cap) * hd;
     const int q_dim = a.n_kv * hpg * hd;
+    const int vec_per_row = hd / 8;
+    const int old_end = pos - (a.contiguous ? m : 0);  // keys below were written by earlier launches
+    const int kn_first = min(CH, k1 - k0);
+    const int pre_end = max(k0, min(k0 + kn_first, old_end));
+    auto load_keys = [&](int c0, int j0, int j1) {  // keys [c0 + j0, c0 + j1) into tile rows j0..j1-1
+        for (int i = j0 * vec_per_row + tid; i < j1 * vec_per_row; i += kAttnThreads) {
+            const int j = i / vec_per_row, v = i % vec_per_row;
+            const size_t off = cache_base + (size_t)(c0 + j) * hd + v * 8;
+            *reinterpret_cast<uint4*>(&Ks[j * KP + v * 8]) = __ldcg(reinterpret_cast<const uint4*>(a.kcache + off));
+            *reinterpret_cast<uint4*>(&Vs[j * KP + v * 8]) = __ldcg(reinterpret_cast<const uint4*>(a.vcache + off));
+        }
+    };
+    if (k0 < k1) load_keys(k0, 0, pre_end - k0);
+    pdl_wait();
+    pdl_launch();
 
     const uint16_t* qrow = a.q + (size_t)m * q_dim + (size_t)grp * hpg * hd;
     for (int i = tid; i < hpg * hd; i += kAttnThreads) Qs[i] = bf16_bits_to_f32(qrow[i]);
@@ -509,17 +526,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     const int ph = tid / per_head, pd = (tid % per_head) * 4;
     const bool owns = tid < hpg * per_head;
     float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    const int vec_per_row = hd / 8;
 
     for (int c0 = k0; c0 < k1; c0 += CH) {
         const int kn = min(CH, k1 - c0);
         __syncthreads();  // previous tile fully consumed (and Qs/Ms ready on the first)
-        for (int i = tid; i < kn * vec_per_row; i += kAttnThreads) {
-            const int j = i / vec_per_row, v = i % vec_per_row;
-            const size_t off = cache_base + (size_t)(c0 + j) * hd + v * 8;
-            *reinterpret_cast<uint4*>(&Ks[j * KP + v * 8]) = ldg_nc(a.kcache + off);
-            *reinterpret_cast<uint4*>(&Vs[j * KP + v * 8]) = ldg_nc(a.vcache + off);
-        }
+        load_keys(c0, c0 == k0 ? pre_end - k0 : 0, kn);
         __syncthreads();
         // scores: thread -> key j, heads h = t/CH, t/CH + 4, ...
         {

@@ -104,6 +104,7 @@ struct AttnArgs {
     const int* row_slot;
     const int* row_pos;
     int M, n_kv, hpg, hd, cap;
+    int contiguous;         // rows are consecutive positions of one slot (a prefill block)
 };
 
 struct EmbedArgs {

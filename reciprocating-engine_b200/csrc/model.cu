@@ -402,8 +402,9 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
     return linear(m, qkv_args(m, l, M), EPI_QKV, 0, 0, st);
 }
 
-AttnArgs attn_args(reng_model* m, int l, int M) {
+AttnArgs attn_args(reng_model* m, int l, int M, int mode) {
     AttnArgs at{};
+    at.contiguous = mode == 1;
     at.q = m->qbuf;
     at.kcache = m->kcache + (size_t)l * m->layer_kv;
     at.vcache = m->vcache + (size_t)l * m->layer_kv;
@@ -418,8 +419,8 @@ AttnArgs attn_args(reng_model* m, int l, int M) {
     return at;
 }
 
-int k_attn_launch(reng_model* m, int l, int M, cudaStream_t st) {
-    CU(launch_attn(attn_args(m, l, M), kAttnChunk, true, st));
+int k_attn_launch(reng_model* m, int l, int M, int mode, cudaStream_t st) {
+    CU(launch_attn(attn_args(m, l, M, mode), kAttnChunk, true, st));
     m->launches++;
     return RENG_OK;
 }
@@ -518,7 +519,7 @@ int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_
     TRY(k_embed_launch(m, mode, M, slot, st));
     for (int l = 0; l < m->L; l++) {
         TRY(k_qkv_launch(m, l, M, st));
-        TRY(k_attn_launch(m, l, M, st));
+        TRY(k_attn_launch(m, l, M, mode, st));
         TRY(k_proj_launch(m, l, M, 0, st));
         TRY(k_gateup_launch(m, l, M, st));
         TRY(k_proj_launch(m, l, M, 1, st));
@@ -559,7 +560,7 @@ int build_step(reng_model* m) {
         gemv(qkv_args(m, l, M), EPI_QKV);
         StepPhase pa{};
         pa.kind = PH_ATTN;
-        pa.at = attn_args(m, l, M);
+        pa.at = attn_args(m, l, M, 0);
         ph.push_back(pa);
         gemv(proj_args(m, l, M, 0), EPI_RESID);
         gemv(gateup_args(m, l, M), EPI_SWIGLU);
@@ -1123,7 +1124,7 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
                 const int l = i % m->L;
                 switch (kind) {
                     case 0: TRY(k_qkv_launch(m, l, M, m->st)); break;
-                    case 1: TRY(k_attn_launch(m, l, M, m->st)); break;
+                    case 1: TRY(k_attn_launch(m, l, M, 0, m->st)); break;
                     case 2: TRY(k_proj_launch(m, l, M, 0, m->st)); break;
                     case 3: TRY(k_gateup_launch(m, l, M, m->st)); break;
                     case 4: TRY(k_proj_launch(m, l, M, 1, m->st)); break;
