@@ -33,9 +33,10 @@ namespace reng {
 // The device pieces shared with the persistent step kernel (x fragments,
 // block MMAs, tile epilogues, the TMA ring primitives) are in gemv_core.cuh.
 
-template <int PIPE>
+// Weight ring bytes of one warp with ST stages.
+template <int ST>
 __host__ __device__ constexpr int gemv_ring_bytes() {
-    return PIPE == PIPE_TMA ? kTmaRing : 0;
+    return ST * kChunkBytes;
 }
 
 // Ring stages issued before the wait on the previous kernel; the others go
@@ -44,7 +45,7 @@ __host__ __device__ constexpr int gemv_ring_bytes() {
 // weights per SM) and 3.38 with none.
 constexpr int kPreStages = 2;
 
-template <int EPI, int NWARP, int PIPE, int W8>
+template <int EPI, int NWARP, int ST, int W8>
 __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     extern __shared__ __align__(128) uint8_t smem_dyn[];
     // the warps' tile reduction; before the first tile it holds the RMS
@@ -56,7 +57,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     __shared__ float inv_s[kMaxRows];
     __shared__ int s_ids[kMaxRows];
     __shared__ int s_last;
-    __shared__ __align__(8) unsigned long long bars[PIPE == PIPE_TMA ? NWARP * kTmaStages : 1];
+    __shared__ __align__(8) unsigned long long bars[NWARP * ST];
     __shared__ __align__(8) unsigned long long xbar;
     const int K = a.K;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,31 +82,19 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     };
 
     // ---- start the weight stream (independent of the previous kernel) ----
-    uint4 rv[PIPE == PIPE_REG ? CB : 1][4];  // the chunk in flight (register pipeline)
-    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem_dyn) + warp * gemv_ring_bytes<PIPE>();  // per warp
-    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]) + warp * kTmaStages * 8;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(smem_dyn) + warp * gemv_ring_bytes<ST>();  // per warp
+    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]) + warp * ST * 8;
     bool failed = false;
     int issued = 0;  // lane 0: chunks whose copy was issued
     int waited = 0;  // chunks whose copy was waited for
-    auto rload = [&](int j) {
-        if (j >= nchunks) return;
-        int nb;
-        const uint8_t* src = chunk_src(j, nb);
-#pragma unroll
-        for (int b = 0; b < (PIPE == PIPE_REG ? CB : 1); b++)
-            if (b < nb) {
-#pragma unroll
-                for (int p = 0; p < NP; p++) rv[b][p] = ldg_stream(src + b * BB + poff[p]);
-            }
-    };
     auto tma_issue = [&](int j) {  // lane 0 only
         if (j >= nchunks || failed) return;
         int nb;
         const uint8_t* src = chunk_src(j, nb);
-        const uint32_t bar = bar0 + (j % kTmaStages) * 8;
+        const uint32_t bar = bar0 + (j % ST) * 8;
         const uint32_t bytes = (uint32_t)nb * BB;
         mbar_expect_tx(bar, bytes);
-        if (bytes) tma_load_1d(ring + (j % kTmaStages) * kChunkBytes, src, bytes, bar);
+        if (bytes) tma_load_1d(ring + (j % ST) * kChunkBytes, src, bytes, bar);
         issued = j + 1;
     };
     const uint32_t xbar_a = (uint32_t)__cvta_generic_to_shared(&xbar);
@@ -114,24 +103,13 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (PIPE == PIPE_TMA) {
-        if (lane == 0) {
-            for (int s2 = 0; s2 < kTmaStages; s2++) mbar_init(bar0 + s2 * 8, 1);
-            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            for (int j = 0; j < kPreStages; j++) tma_issue(j);
-        }
-        __syncwarp();
-    } else {
-        if (lane == 0 && nchunks > 0 && c1 > c0) {
-            // the rest of this warp's first tile range into L2
-            const uint8_t* p = a.w + ((size_t)blockIdx.x * a.kc + c0) * BB;
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p),
-                         "r"((uint32_t)(c1 - c0) * BB)
-                         : "memory");
-        }
-        rload(0);
+    if (lane == 0) {
+        for (int s2 = 0; s2 < ST; s2++) mbar_init(bar0 + s2 * 8, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int j = 0; j < kPreStages; j++) tma_issue(j);
     }
+    __syncwarp();
     // the RMSNorm gains of this thread's k-groups (constants: before the wait)
     constexpr int GV = NWARP == 4 ? 5 : 3;  // k-groups per thread: K <= 5120 (4 warps), 6144 (8)
     float4 gp[GV][2];
@@ -144,7 +122,7 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     // x rows (written by the previous kernel): one bulk copy per row into
     // shared memory, while the warps reduce the RMS partials
     const int xstride = gemv_xstride(K);
-    uint16_t* xsm = reinterpret_cast<uint16_t*>(smem_dyn + NWARP * gemv_ring_bytes<PIPE>());
+    uint16_t* xsm = reinterpret_cast<uint16_t*>(smem_dyn + NWARP * gemv_ring_bytes<ST>());
     // the RMS partials ride with x when they fit the reduction buffer (plain
     // loads here queue behind the weight stream already in flight: 2-3 us)
     const bool ss_tma = a.ss_in != nullptr && use_smem && (a.ss_tiles & 3) == 0 &&
@@ -165,12 +143,10 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     }
     // the rest of the ring behind x (the copies issued so far stand in front
     // of x in the SM's queue)
-    if (PIPE == PIPE_TMA) {
-        __syncwarp();
-        if (lane == 0)
-            for (int j = kPreStages; j < kTmaStages; j++) tma_issue(j);
-        __syncwarp();
-    }
+    __syncwarp();
+    if (lane == 0)
+        for (int j = kPreStages; j < ST; j++) tma_issue(j);
+    __syncwarp();
     if (a.ss_in != nullptr && !ss_tma) {
         for (int m = warp; m < a.M; m += NWARP) {
             float s = 0.0f;
@@ -222,43 +198,31 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < nchunks; j++) {
         const int b0 = c0 + (j % nct) * CB;
-        if (PIPE == PIPE_TMA) {
-            const uint32_t bar = bar0 + (j % kTmaStages) * 8;
-            if (!failed) {
-                if (mbar_wait_bounded(bar, (uint32_t)((j / kTmaStages) & 1))) {
-                    waited = j + 1;
-                } else {
-                    failed = true;
-                    if (lane == 0) atomicExch(a.err, RENG_E_TIMEOUT);
-                }
+        const uint32_t bar = bar0 + (j % ST) * 8;
+        if (!failed) {
+            if (mbar_wait_bounded(bar, (uint32_t)((j / ST) & 1))) {
+                waited = j + 1;
+            } else {
+                failed = true;
+                if (lane == 0) atomicExch(a.err, RENG_E_TIMEOUT);
             }
-            const uint32_t st = ring + (j % kTmaStages) * kChunkBytes;
-#pragma unroll
-            for (int b = 0; b < CB; b++)
-                if (b0 + b < c1) {
-                    uint4 v[4];
-#pragma unroll
-                    for (int p = 0; p < NP; p++) v[p] = lds128(st + b * BB + poff[p]);
-                    block_mma<W8>(acc, v, a, xs, xstride, K, b0 + b, g, q);
-                }
-            // the stage is read: let the async proxy refill it
-            __syncwarp();
-            if (lane == 0) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                tma_issue(j + kTmaStages);
-            }
-            __syncwarp();
-        } else {
-            uint4 cur[CB][4];
-#pragma unroll
-            for (int b = 0; b < CB; b++)
-#pragma unroll
-                for (int p = 0; p < NP; p++) cur[b][p] = rv[b][p];
-            rload(j + 1);
-#pragma unroll
-            for (int b = 0; b < CB; b++)
-                if (b0 + b < c1) block_mma<W8>(acc, cur[b], a, xs, xstride, K, b0 + b, g, q);
         }
+        const uint32_t st = ring + (j % ST) * kChunkBytes;
+#pragma unroll
+        for (int b = 0; b < CB; b++)
+            if (b0 + b < c1) {
+                uint4 v[4];
+#pragma unroll
+                for (int p = 0; p < NP; p++) v[p] = lds128(st + b * BB + poff[p]);
+                block_mma<W8>(acc, v, a, xs, xstride, K, b0 + b, g, q);
+            }
+        // the stage is read: let the async proxy refill it
+        __syncwarp();
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tma_issue(j + ST);
+        }
+        __syncwarp();
         if ((j % nct) != nct - 1) continue;
         // ---- a tile is complete: reduce the warps' k-slices on warp 0 ----
         const int tile = blockIdx.x + (j / nct) * gridDim.x;
@@ -289,10 +253,10 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         }
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
     }
-    if (PIPE == PIPE_TMA && failed && lane == 0) {
+    if (failed && lane == 0) {
         // drain this warp's own copies still in flight before exiting (bounded)
         for (int jj = waited; jj < issued; jj++)
-            if (!mbar_wait_bounded(bar0 + (jj % kTmaStages) * 8, (uint32_t)((jj / kTmaStages) & 1))) break;
+            if (!mbar_wait_bounded(bar0 + (jj % ST) * 8, (uint32_t)((jj / ST) & 1))) break;
     }
 
     if (EPI == EPI_LOGITS) {
@@ -335,33 +299,33 @@ static size_t gemv_xbytes(const GemvArgs& a) {
     return 0;
 }
 
-template <int EPI, int NW>
-static cudaError_t prepare_one() {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024);
+template <int EPI, int NW, int ST>
+static cudaError_t prepare_st() {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<EPI, NW, ST, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 200 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_REG, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 200 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EPI, NW, PIPE_TMA, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 200 * 1024);
+        e = cudaFuncSetAttribute(k_gemv<EPI, NW, ST, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     return e;
 }
 
-template <int EPI, int NW, int PIPE, int W8>
-static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStream_t st, int* grid_out) {
+// CTAs of k_gemv<EPI, NW, ST, W8> resident per SM with smem dynamic bytes.
+template <int EPI, int NW, int ST, int W8>
+static int gemv_per_sm(size_t smem) {
+    int per_sm = 0;
+    if (smem > 200 * 1024) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<EPI, NW, ST, W8>, NW * 32, smem) != cudaSuccess)
+        return 0;
+    return per_sm;
+}
+
+template <int EPI, int NW, int ST, int W8>
+static cudaError_t launch_one(const GemvArgs& a, int per_sm, int max_grid, bool pdl, cudaStream_t st,
+                              int* grid_out) {
     const size_t xbytes = gemv_xbytes(a);
-    const size_t smem = (size_t)NW * gemv_ring_bytes<PIPE>() + xbytes;
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    int per_sm = 0, dev = 0, sms = 148;
+    const size_t smem = (size_t)NW * gemv_ring_bytes<ST>() + xbytes;
+    int dev = 0;
     cudaGetDevice(&dev);
-    sms = num_sms(dev);
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<EPI, NW, PIPE, W8>, NW * 32, smem);
-    if (e != cudaSuccess || per_sm < 1) per_sm = 1;
-    int cap = sms * per_sm;
+    const int sms = num_sms(dev);
+    int cap = sms * std::max(1, per_sm);
     if (max_grid > 0 && max_grid < cap) cap = max_grid;
     // persistent grid of every resident slot (tiles interleaved over the
     // CTAs), so each SM holds the same number of CTAs: the weight stream of
@@ -386,13 +350,25 @@ static cudaError_t launch_one(const GemvArgs& a, int max_grid, bool pdl, cudaStr
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemv<EPI, NW, PIPE, W8>, a, xbytes > 0 ? 1 : 0);
+    return cudaLaunchKernelEx(&cfg, k_gemv<EPI, NW, ST, W8>, a, xbytes > 0 ? 1 : 0);
+}
+
+// Ring depth: 4 stages of 4 KB per warp, three 4-warp CTAs per SM.  Deeper
+// rings for the projections whose tiles fit one wave at two CTAs per SM
+// (o_proj 6 stages, down_proj 5, Llama-8B b1) made those kernels faster
+// alone but the step slower, 3.24 against 3.18 ms (their shared memory
+// keeps the next kernel's CTAs from starting early).
+template <int EPI, int NW, int W8>
+static cudaError_t launch_stages(const GemvArgs& a, int max_grid, bool pdl, cudaStream_t st, int* grid_out) {
+    const int p4 = gemv_per_sm<EPI, NW, 4, W8>((size_t)NW * gemv_ring_bytes<4>() + gemv_xbytes(a));
+    if (p4 < 1) return cudaErrorInvalidValue;
+    return launch_one<EPI, NW, 4, W8>(a, p4, max_grid, pdl, st, grid_out);
 }
 
 template <int EPI>
 static cudaError_t prepare_t() {
-    cudaError_t e = prepare_one<EPI, 4>();
-    if (e == cudaSuccess) e = prepare_one<EPI, 8>();
+    cudaError_t e = prepare_st<EPI, 4, 4>();
+    if (e == cudaSuccess) e = prepare_st<EPI, 8, 4>();
     return e;
 }
 
@@ -407,47 +383,21 @@ cudaError_t gemv_prepare() {
     return e;
 }
 
-// shape = warps per CTA (4 or 8) + 100 * pipeline (0 registers, 1 TMA ring)
+// shape = warps per CTA (4 or 8) + 100 (the TMA weight ring)
 template <int EPI>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int shape, int max_grid, bool pdl, cudaStream_t st,
                                  int* grid_out) {
     switch (shape) {
-        case 4: return a.w8 ? launch_one<EPI, 4, PIPE_REG, 1>(a, max_grid, pdl, st, grid_out)
-                            : launch_one<EPI, 4, PIPE_REG, 0>(a, max_grid, pdl, st, grid_out);
-        case 8: return a.w8 ? launch_one<EPI, 8, PIPE_REG, 1>(a, max_grid, pdl, st, grid_out)
-                            : launch_one<EPI, 8, PIPE_REG, 0>(a, max_grid, pdl, st, grid_out);
-        case 104: return a.w8 ? launch_one<EPI, 4, PIPE_TMA, 1>(a, max_grid, pdl, st, grid_out)
-                              : launch_one<EPI, 4, PIPE_TMA, 0>(a, max_grid, pdl, st, grid_out);
-        case 108: return a.w8 ? launch_one<EPI, 8, PIPE_TMA, 1>(a, max_grid, pdl, st, grid_out)
-                              : launch_one<EPI, 8, PIPE_TMA, 0>(a, max_grid, pdl, st, grid_out);
+        case 104: return a.w8 ? launch_stages<EPI, 4, 1>(a, max_grid, pdl, st, grid_out)
+                              : launch_stages<EPI, 4, 0>(a, max_grid, pdl, st, grid_out);
+        case 108: return a.w8 ? launch_stages<EPI, 8, 1>(a, max_grid, pdl, st, grid_out)
+                              : launch_stages<EPI, 8, 0>(a, max_grid, pdl, st, grid_out);
         default: return cudaErrorInvalidValue;
-    }
-}
-
-template <int EPI>
-static int blocks_t(int nwarp) {
-    int n = 0;
-    cudaError_t e = cudaErrorInvalidValue;
-    if (nwarp == 4) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 4, PIPE_REG, 0>, 128, 0);
-    if (nwarp == 8) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<EPI, 8, PIPE_REG, 0>, 256, 0);
-    return e == cudaSuccess ? n : 1;
-}
-
-int gemv_blocks_per_sm(int epi, int nwarp) {
-    switch (epi) {
-        case EPI_QKV: return blocks_t<EPI_QKV>(nwarp);
-        case EPI_RESID: return blocks_t<EPI_RESID>(nwarp);
-        case EPI_SWIGLU: return blocks_t<EPI_SWIGLU>(nwarp);
-        case EPI_LOGITS: return blocks_t<EPI_LOGITS>(nwarp);
-        case EPI_F32: return blocks_t<EPI_F32>(nwarp);
-        default: return 1;
     }
 }
 
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int shape, int max_grid, bool pdl, cudaStream_t st,
                         int* grid_out) {
-    const int nwarp = shape % 100;
-    (void)nwarp;
     switch (epi) {
         case EPI_QKV: return launch_gemv_t<EPI_QKV>(a, shape, max_grid, pdl, st, grid_out);
         case EPI_RESID: return launch_gemv_t<EPI_RESID>(a, shape, max_grid, pdl, st, grid_out);

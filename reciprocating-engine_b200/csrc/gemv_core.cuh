@@ -332,20 +332,16 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
 // Each warp walks a flat sequence of chunks (its k-range of a tile, tile
 // after tile of the CTA) so the stream never restarts at a tile boundary.
 //
-// PIPE_REG: the next chunk (kChunkBytes of blocks) is loaded into registers while
-// the current one is multiplied.
-// PIPE_TMA: each warp owns a ring of kTmaStages stages of kChunkBytes of
-// contiguous packed blocks in shared memory, filled by one
-// cp.async.bulk (TMA) copy per stage and an mbarrier with the transaction
-// byte count; lane 0 refills a stage as soon as the warp has read it.  The
-// bytes in flight are bounded by shared memory, not registers.  Every
-// mbarrier wait is bounded by a %globaltimer deadline: on expiry the kernel
-// records RENG_E_TIMEOUT in *a.err, stops issuing copies, drains its own
-// copies (again bounded) and finishes without waiting.
-enum { PIPE_REG = 0, PIPE_TMA = 1 };
+// Each warp owns a ring of stages of kChunkBytes of contiguous packed
+// blocks in shared memory (kTmaStages of them), filled by
+// one cp.async.bulk (TMA) copy per stage and an mbarrier with the
+// transaction byte count; lane 0 refills a stage as soon as the warp has
+// read it.  Every mbarrier wait is bounded by a %globaltimer deadline: on
+// expiry the kernel records RENG_E_TIMEOUT in *a.err, stops issuing
+// copies, drains its own copies (again bounded) and finishes without
+// waiting.
 constexpr int kChunkBytes = 4096;                             // weight bytes per pipeline chunk
 constexpr int kTmaStages = 4;
-constexpr int kTmaRing = kTmaStages * kChunkBytes;           // bytes per warp
 constexpr unsigned long long kWaitNs = 2000000000ull;           // 2 s per wait
 
 __device__ __forceinline__ unsigned long long globaltimer() {

@@ -24,7 +24,6 @@ cudaError_t launch_tp_residual(reng_model* m, const float* part, int M, bool pdl
 cudaError_t launch_tp_ar_residual(reng_model* m, const float* part, int M, cudaStream_t st);
 bool tp_p2p(reng_model* m, int M);
 int tp_exchange_kind(reng_model* m);
-int gemv_blocks_per_sm(int epi, int nwarp);
 }  // namespace reng
 
 struct LayerDev {
@@ -208,21 +207,17 @@ int upload_f32(reng_model* m, float** out, const float* src, size_t n, int mem) 
 
 // Launch shape of a GEMV kind (0 qkv, 1 o_proj, 2 gate/up, 3 down, 4 LM
 // head) for few (M <= 2) and many activation rows: warps per CTA (4 or 8)
-// + 100 for the TMA weight ring (else the register pipeline).  Measured on
-// B200 (Llama-8B widths, whole decode step in its CUDA graph): with every
-// kind on the 4-warp TMA ring the step is 3.36 ms against 3.91 ms when
-// o_proj/down use 8-warp register-pipeline CTAs, although those are as fast
-// alone: their registers keep the next kernel's CTAs from starting early,
-// which costs the programmatic-dependent-launch overlap.
+// + 100 (the TMA weight ring).  Measured on B200 (Llama-8B widths, whole
+// decode step in its CUDA graph): 4-warp ring CTAs for every kind, 3.36 ms
+// per step, against 3.91 ms with o_proj/down on 8-warp CTAs that streamed
+// through registers (as fast alone, but their registers kept the next
+// kernel's CTAs from starting early).
 // RENG_GEMV_SHAPES="qkv,o,gu,down,lm" overrides both (a tuning knob).
 void pick_shape(reng_model* m, int kind, int kc, int* shape_small, int* shape_big) {
     static const int small[5] = {104, 104, 104, 104, 104};
     static const int big[5] = {108, 108, 108, 108, 108};
     int ss = small[kind], sb = big[kind];
-    if (kc < 32) {  // short K: 8 warps would leave warps without blocks
-        ss = ss >= 100 ? 104 : 4;
-        sb = sb >= 100 ? 104 : 4;
-    }
+    if (kc < 32) ss = sb = 104;  // short K: 8 warps would leave warps without blocks
     const char* v = getenv("RENG_GEMV_SHAPES");
     if (v) {
         int vals[5] = {0, 0, 0, 0, 0}, n = 0;
@@ -233,7 +228,7 @@ void pick_shape(reng_model* m, int kind, int kc, int* shape_small, int* shape_bi
             if (*p == ',') p++;
         }
         const int x = kind < n ? vals[kind] : 0;
-        if (x == 4 || x == 8 || x == 104 || x == 108) ss = sb = x;
+        if (x == 104 || x == 108) ss = sb = x;
     }
     *shape_small = ss;
     *shape_big = sb;
