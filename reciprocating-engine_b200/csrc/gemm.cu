@@ -412,6 +412,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                     for (int j = 0; j < 16; j++) v[j] = 0.f;
                 tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
             }
+        } else if (g.gpart != nullptr) {
+            // split K without a cluster: this split's partial to global
+            // scratch [super-tile][split][128][N]; the last split of the
+            // super-tile to arrive adds all of them in split order
+            // (deterministic) and runs the epilogue
+            float* mine = g.gpart + (((size_t)S * g.ks + ksi) * 128 + lr) * N;
+            for (int cb = 0; cb < N / 16; cb++) {
+                float v[16];
+                tmem_ld16(trow + cb * 16, v);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    __stcg(reinterpret_cast<float4*>(mine + cb * 16) + j,
+                           zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            }
+            __threadfence();
+            named_sync_epilogue();
+            if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + S, 1) == g.ks - 1;
+            named_sync_epilogue();
+            if (s_flag) {
+                __threadfence();
+                for (int cb = 0; cb < N / 16; cb++) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = 0.f;
+                    for (int k = 0; k < g.ks; k++) {
+                        const float4* src =
+                            reinterpret_cast<const float4*>(g.gpart + (((size_t)S * g.ks + k) * 128 + lr) * N + cb * 16);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float4 x = __ldcg(src + j);
+                            v[4 * j] += x.x;
+                            v[4 * j + 1] += x.y;
+                            v[4 * j + 2] += x.z;
+                            v[4 * j + 3] += x.w;
+                        }
+                    }
+                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                }
+                if (threadIdx.x == 64) g.gcnt[S] = 0;
+            }
         } else {
             // split K: this split's partial into the (finished) stage buffers,
             // row lr at lr * (N + 4) floats (conflict-free 16-byte stores)
@@ -463,7 +504,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             }
         }
     }
-    if (g.ks > 1) {
+    if (g.ks > 1 && g.gpart == nullptr) {
         // the K splits of this super-tile are one cluster: once every
         // split's partial is in its shared memory, CTA r adds column blocks
         // r, r + ks, ... over the cluster in rank order (deterministic) and
@@ -566,7 +607,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool p
     cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages);
     cfg.stream = st;
     int na = 0;
-    if (g.ks > 1) {  // the K splits of a super-tile form one cluster
+    if (g.ks > 1 && g.gpart == nullptr) {  // the K splits of a super-tile form one cluster
         attr[na].id = cudaLaunchAttributeClusterDimension;
         attr[na].val.clusterDim.x = g.ks;
         attr[na].val.clusterDim.y = 1;
@@ -605,29 +646,40 @@ cudaError_t gemm_prepare() {
     return e;
 }
 
-void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, int* ks_out, int* stages_out) {
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks_out, int* stages_out,
+               bool* gsplit_out) {
     // Enough super-tiles to occupy the SMs (or the LM head, whose argmax
     // needs whole rows per CTA): one CTA per super-tile, two per SM at N <= 64.
-    // Else split K over a cluster of up to 8 CTAs; clusters of these kernels
-    // are scheduled one CTA per SM, so the splits fill the SMs once and each
-    // CTA gets a deep pipeline.
+    // Else split K over up to 8 CTAs.  At N = 16 the splits are plain CTAs
+    // adding their partials through global scratch, two per SM with 6-stage
+    // pipelines; wider, they form a cluster adding over shared memory
+    // (clusters of these kernels are scheduled one CTA per SM).  Measured on
+    // B200 (Llama-8B): down_proj at 8 rows 47 -> 30 us with plain splits (a
+    // cluster of 4 per super-tile, 128 CTAs of 4 stages, kept about 72 KB in
+    // flight per SM); at 64 rows plain splits lost (the last split reading
+    // 8 partials of 32 KB: b64 step 6.98 -> 9.55 ms).
     int ks = 1;
+    const bool gsplit = gsplit_ok && n <= 16;
+    const int slots = gsplit ? 2 * sms : sms;
     if (epi != EPI_LOGITS && super_tiles < sms) {
-        ks = sms / super_tiles;
+        ks = slots / super_tiles;
         ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
         if (ks > kGemmMaxSplits) ks = kGemmMaxSplits;
         const int kper = (kc + ks - 1) / ks;
         ks = (kc + kper - 1) / kper;  // every split gets at least one chunk
     }
     *ks_out = ks;
-    *stages_out = gemm_pick_stages(n, ks > 1 || n > 64, epi);
+    *gsplit_out = ks > 1 && gsplit;
+    *stages_out = gemm_pick_stages(n, (ks > 1 && !gsplit) || n > 64, epi);
 }
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
     if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
         g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1) || g.stages < 2 || g.stages > kGemmMaxStages ||
         gemm_smem_bytes(g.N, g.stages) > (size_t)kGemmMaxDynSmem ||
-        (g.ks > 1 && (size_t)g.stages * (kStageA + (size_t)g.N * 128) < (size_t)128 * (g.N + 4) * 4))
+        (g.ks > 1 && g.gpart == nullptr &&
+         (size_t)g.stages * (kStageA + (size_t)g.N * 128) < (size_t)128 * (g.N + 4) * 4) ||
+        (g.gpart != nullptr && g.gcnt == nullptr))
         return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_QKV: return launch_tc_t<EPI_QKV>(map, g, pdl, st);
@@ -719,7 +771,8 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     RENG_CHECK_ARG(w && x && y, "reng_gemm_bf16: NULL buffer");
     RENG_CHECK_ARG(rows >= 1 && K >= 8 && K % 8 == 0, "reng_gemm_bf16: rows >= 1 and K a positive multiple of 8");
     RENG_CHECK_ARG(M >= 1 && M <= kRowsCap, "reng_gemm_bf16: M must be in [1, 256]");
-    RENG_CHECK_ARG(splits >= 0 && iters >= 0 && (iters == 0 || ms_out), "reng_gemm_bf16: bad splits / iters");
+    RENG_CHECK_ARG(splits >= -kGemmMaxSplits && splits <= kGemmMaxSplits && iters >= 0 && (iters == 0 || ms_out),
+                   "reng_gemm_bf16: bad splits / iters");
     RENG_CHECK_ARG(mem == RENG_MEM_HOST || mem == RENG_MEM_DEVICE, "reng_gemm_bf16: bad mem");
     const cudaMemcpyKind h2d = mem == RENG_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
     const cudaMemcpyKind d2h = mem == RENG_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
@@ -770,13 +823,21 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
-    gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), &g.ks, &g.stages);
-    if (splits > 0) {
-        int s = splits > kc ? kc : splits;
+    bool gsplit = false;
+    gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), true, &g.ks, &g.stages, &gsplit);
+    if (splits != 0) {  // > 0: a cluster of that many splits; < 0: plain CTAs
+        int s = splits > 0 ? splits : -splits;
+        s = s > kc ? kc : s;
         if (s > kGemmMaxSplits) s = kGemmMaxSplits;
         const int kper = (kc + s - 1) / s;
         g.ks = (kc + kper - 1) / kper;
-        g.stages = gemm_pick_stages(N, g.ks > 1 || N > 64, EPI_F32);
+        gsplit = splits < 0 && g.ks > 1;
+        g.stages = gemm_pick_stages(N, (g.ks > 1 && !gsplit) || N > 64, EPI_F32);
+    }
+    if (gsplit) {
+        GEMM_CU(f.alloc(&g.gpart, (size_t)g.super_tiles * g.ks * 128 * N * 4));
+        GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * 4));
+        GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * 4));
     }
     CUtensorMap tmap;
     const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);

@@ -9,6 +9,7 @@ namespace reng {
 
 constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
 constexpr int kGemmMaxSplits = 8;     // K splits of a super-tile (a portable cluster)
+constexpr int kGemmCntMax = 1024;     // super-tiles of a split launch (arrival counts)
 
 struct GemmArgs {
     GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
@@ -19,6 +20,11 @@ struct GemmArgs {
     int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
     int stages;               // pipeline stages (2..8)
+    // ks > 1 without a cluster: f32 partials [super_tiles][ks][128][N] and
+    // one arrival count per super-tile (0 between launches); null: the
+    // splits form a cluster and add their partials over shared memory
+    float* gpart;
+    int* gcnt;
 };
 
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as
@@ -32,7 +38,7 @@ int gemm_pick_stages(int n, bool one_per_sm, int epi);
 // once per device before capture).
 cudaError_t gemm_prepare();
 // K splits and pipeline stages of a launch over super_tiles x kc blocks.
-void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, int* ks, int* stages);
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks, int* stages, bool* gsplit);
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps,

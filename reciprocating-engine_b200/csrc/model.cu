@@ -52,6 +52,9 @@ struct reng_model {
     uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
     uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
     int launches = 0;                // kernels of this library enqueued so far
+    float* gpart = nullptr;          // GEMM split-K partials (splits without a cluster)
+    size_t gpart_floats = 0;
+    int* gcnt = nullptr;             // GEMM split-K arrivals per super-tile
     // the persistent decode step (one cooperative launch per step) when the
     // shape allows it, else the per-projection kernels
     bool step_on = false;
@@ -362,7 +365,14 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.kc = g.kc;
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
-    gemm_plan(a.super_tiles, g.kc, N, epi, m->sms, &a.ks, &a.stages);
+    bool gsplit = false;
+    gemm_plan(a.super_tiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit);
+    if (gsplit) {
+        if ((size_t)a.super_tiles * a.ks * 128 * N > m->gpart_floats || a.super_tiles > kGemmCntMax)
+            return fail(RENG_E_STATE, "GEMM split-K scratch too small");
+        a.gpart = m->gpart;
+        a.gcnt = m->gcnt;
+    }
     if (epi == EPI_LOGITS && (size_t)a.super_tiles > (size_t)m->lm_grid)
         return fail(RENG_E_STATE, "LM head argmax partials too small");
     CU(launch_gemm_tc(map, a, epi, true, st));
@@ -849,6 +859,11 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
+    // split-K partials: at most two CTAs per SM of 128 rows x N <= 64
+    m->gpart_floats = (size_t)2 * m->sms * 128 * 64;
+    TRY(dalloc(m, &m->gpart, m->gpart_floats));
+    TRY(dalloc(m, &m->gcnt, (size_t)kGemmCntMax));
+    CU(cudaMemsetAsync(m->gcnt, 0, (size_t)kGemmCntMax * 4, m->st));
     TRY(dalloc(m, &m->am_key, (size_t)kRowsCap));
     CU(cudaMemsetAsync(m->am_key, 0, (size_t)kRowsCap * 8, m->st));
     CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
@@ -893,6 +908,11 @@ int check_device_error(reng_model* m) {
     if (*h != 0) {
         const int code = *h;
         CU(cudaMemsetAsync(m->err, 0, 4, m->st));
+        // a launch that gave up may leave arrival counts and argmax keys mid-count
+        CU(cudaMemsetAsync(m->gcnt, 0, (size_t)kGemmCntMax * 4, m->st));
+        CU(cudaMemsetAsync(m->am_key, 0, (size_t)kRowsCap * 8, m->st));
+        CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
+        CU(cudaStreamSynchronize(m->st));
         if (m->step_on) {  // a step that gave up may leave the barrier mid-count
             CU(cudaMemsetAsync(m->step_ctl.abort, 0, 4, m->st));
             CU(cudaMemsetAsync(m->step_ctl.bar, 0, 8, m->st));

@@ -27,9 +27,13 @@ def bits_to_f64(b):
     (128, 64, 16, 1),        # one CTA, one k chunk
     (256, 512, 9, 1),        # M padded to N = 16
     (200, 200, 33, 0),       # ragged rows (16-row tiles, 128-row CTA tiles) and K (zero fill past K)
-    (384, 1024, 64, 3),      # split K, 3 partials summed by the last CTA
+    (384, 1024, 64, 3),      # split K, a cluster of 3 adding over shared memory
+    (384, 1024, 24, -3),     # split K, 3 plain CTAs adding through global scratch
+    (300, 1000, 8, -5),      # ragged rows and K, 5 plain splits
     (1000, 576, 256, 0),     # N = 256, the widest MMA
     (4096, 4096, 64, 0),     # Llama-8B o_proj widths, automatic splits
+    (4096, 14336, 8, 0),     # Llama-8B down_proj at batch 8: plain splits
+    (512, 2048, 40, -4),     # plain splits at N = 48
 ])
 def test_gemm_matches_exact_sums(reng_lib, rows, K, M, splits):
     from reng.gemm import gemm_bf16
