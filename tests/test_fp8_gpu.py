@@ -46,6 +46,44 @@ def test_config0_matrix_bit_exact_device_memory(fp8, oracle_lib, fmt, scaling):
         assert np.count_nonzero((codes_o & 0x7f) == (0x77 if fmt == 0 else 0x7b)) >= rows
 
 
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("cols", [4096, 8192])
+def test_every_bf16_value_under_many_row_scales(fp8, oracle_lib, fmt, cols):
+    """Per-channel scaling of rows [A, every finite bf16 x with |x| < A]
+    for 48 absmax values A with awkward mantissas: the device forms most
+    codes from x * RN(1/s) and falls back to IEEE division near the
+    format's rounding boundaries; every code and scale must equal the
+    oracle's x / s (both the warp-per-row and the CTA-per-row kernels)."""
+    import torch
+    rng = np.random.default_rng(77 + fmt + cols)
+    bits = np.arange(1 << 16, dtype=np.uint32)
+    finite = bits[((bits >> 7) & 0xff) != 0xff].astype(np.uint16)
+    mag = (finite.astype(np.uint32) << 16).view(np.float32)
+    rows = []
+    for _ in range(48):
+        e = int(rng.integers(-20, 21))
+        a = np.float32(np.ldexp(1.0 + rng.integers(1, 128) / 128.0, e))
+        a_bits = np.uint16(a.view(np.uint32) >> 16)
+        a = (np.uint32(a_bits) << 16).view(np.float32)
+        body = finite[np.abs(mag) < a]
+        chunk = cols - 1
+        for i in range(0, body.size, chunk):
+            r = np.zeros(cols, np.uint16)
+            r[0] = a_bits
+            part = body[i:i + chunk]
+            r[1:1 + part.size] = part
+            rows.append(r)
+    w = np.stack(rows)
+    n = w.shape[0]
+    codes_o, scales_o, _ = oracle_lib.quantize(w.reshape(-1), n, cols, fmt, 0)
+    codes, scales, _ = fp8.quantize_device(torch.from_numpy(w.view(np.int16)).cuda(), n, cols, fmt, 0)
+    torch.cuda.synchronize()
+    assert np.array_equal(scales.cpu().numpy().view(np.uint32), scales_o.view(np.uint32))
+    got = codes.cpu().numpy().reshape(-1)
+    bad = np.flatnonzero(got != codes_o)
+    assert bad.size == 0, (bad.size, bad[:4], got[bad[:4]], codes_o[bad[:4]])
+
+
 def _special_row(rng, cols):
     x = rng.standard_normal(cols).astype(np.float32)
     sp = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-40, -1e-40, 3e38, 240.0, 248.0,
