@@ -272,8 +272,13 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
         __syncthreads();
         if (!s_last) return;
         __threadfence();
-        if (threadIdx.x < a.M) s_ids[threadIdx.x] = am_unpack(atomicExch(a.am_key + threadIdx.x, 0ull));
+        if (threadIdx.x < a.M) {
+            unsigned long long k = atomicExch(a.am_key + threadIdx.x, 0ull);
+            if (a.hx) k = head_exchange(a.hx, threadIdx.x, k, a.err);  // vocabulary shards of the ranks
+            s_ids[threadIdx.x] = am_unpack(k);
+        }
         __syncthreads();
+        if (a.hx && threadIdx.x == 0) *a.hx->epoch += 1;
         if (threadIdx.x == 0) {
             if (a.mode == 0) {
                 const int s = *a.step;

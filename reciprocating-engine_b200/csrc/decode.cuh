@@ -40,6 +40,19 @@ enum Epi : int {
     EPI_F32 = 4,     // f32 partial out (tensor-parallel o_proj / down_proj)
 };
 
+constexpr int kTpMaxWorld = 8;  // tensor-parallel ranks
+
+// The LM head sharded by vocabulary under tensor parallelism (decode
+// steps): every rank streams a contiguous range of the head's rows, and
+// the ranks swap their per-row argmax keys.  Key area of a rank (in its
+// exported region): [2 parities][kTpMaxWorld sources][kMaxRows][2 words],
+// each word (epoch << 32) | 32 bits of the key.
+struct HeadXchg {
+    unsigned long long* recv[kTpMaxWorld];  // every rank's key area (peer mappings; own at [rank])
+    unsigned* epoch;                         // exchanges done by this rank
+    int rank, world;
+};
+
 struct GemvArgs {
     // weights
     const uint8_t* w;  // packed blocks
@@ -94,6 +107,10 @@ struct GemvArgs {
     // f16 (x staged as f16) and the epilogue multiplies by the row's scale
     int w8;
     const float* wscale;    // [tiles*16] per packed row
+    // EPI_LOGITS: global index of the first row of tile 0 (a vocabulary
+    // shard), and the key exchange of a sharded head (null: every row here)
+    int row0;
+    const HeadXchg* hx;
 };
 
 struct AttnArgs {

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "gemv_core.cuh"
 
 namespace reng {
 
@@ -242,13 +243,14 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
         } else if (EPI == EPI_LOGITS) {
             float bv = -INFINITY;
             int bi = 0x7fffffff;
-            if (live && p < a.vocab) {
+            const int pg = a.row0 + p;  // global vocabulary row
+            if (live && pg < a.vocab) {
                 const uint16_t b = f32_to_bf16_bits(v[j]);
-                a.out[(size_t)m * a.ldo + p] = b;
+                a.out[(size_t)m * a.ldo + pg] = b;
                 const float f = bf16_bits_to_f32(b);
                 if (f > -INFINITY) {  // the reference takes a value only if it beats -inf (NaN never)
                     bv = f;
-                    bi = p;
+                    bi = pg;
                 }
             }
 #pragma unroll
@@ -484,9 +486,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             named_sync_epilogue();
             if (s_flag) {
                 __threadfence();
-                for (int m = threadIdx.x - 64; m < a.M; m += 128)
-                    am_i[m] = am_unpack(atomicExch(a.am_key + m, 0ull));
+                for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+                    unsigned long long k = atomicExch(a.am_key + m, 0ull);
+                    if (a.hx) k = head_exchange(a.hx, m, k, a.err);  // vocabulary shards of the ranks
+                    am_i[m] = am_unpack(k);
+                }
                 named_sync_epilogue();
+                if (a.hx && threadIdx.x == 64) *a.hx->epoch += 1;
                 if (threadIdx.x == 64) {
                     if (a.mode == 0) {
                         const int s = *a.step;

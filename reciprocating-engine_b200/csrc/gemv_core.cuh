@@ -304,7 +304,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const
             }
         }
     } else if (EPI == EPI_LOGITS) {
-        const int r0 = tile * kTileRows + g, r1 = r0 + 8;
+        const int r0 = a.row0 + tile * kTileRows + g, r1 = r0 + 8;  // global vocabulary rows
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             const int m = e ? m1 : m0;
@@ -377,6 +377,51 @@ __device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint3
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
+// 16-byte store / load of two 64-bit words, each single-copy atomic, that
+// bypass the non-coherent caches (peer memory written over NVLink).
+__device__ __forceinline__ void st_words(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_words(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Sharded LM head: this rank's argmax key of row m pushed to every peer,
+// the peers' keys of row m collected (bounded wait on their epoch words),
+// the maximum returned.  The maximum of am_pack keys is the largest value
+// with the smallest global index, so every rank gets the replicated head's
+// id.  Every calling thread reads the same epoch; the caller advances it
+// once all have finished.
+__device__ __forceinline__ unsigned long long head_exchange(const HeadXchg* hx, int m, unsigned long long key,
+                                                            int* err) {
+    const unsigned e = *reinterpret_cast<const volatile unsigned*>(hx->epoch) + 1;
+    const size_t par = (size_t)(e & 1) * kTpMaxWorld * kMaxRows * 2;
+    const unsigned long long w0 = ((unsigned long long)e << 32) | (key >> 32);
+    const unsigned long long w1 = ((unsigned long long)e << 32) | (key & 0xffffffffull);
+    for (int r = 0; r < hx->world; r++)
+        if (r != hx->rank) st_words(hx->recv[r] + par + ((size_t)hx->rank * kMaxRows + m) * 2, w0, w1);
+    unsigned long long best = key;
+    for (int r = 0; r < hx->world; r++) {
+        if (r == hx->rank) continue;
+        const unsigned long long* src = hx->recv[hx->rank] + par + ((size_t)r * kMaxRows + m) * 2;
+        unsigned long long a, b;
+        ld_words(src, a, b);
+        if ((a >> 32) != e || (b >> 32) != e) {
+            const unsigned long long t0 = globaltimer();
+            do {
+                ld_words(src, a, b);
+                if (globaltimer() - t0 > kWaitNs) {
+                    atomicExch(err, RENG_E_TIMEOUT);
+                    return best;
+                }
+            } while ((a >> 32) != e || (b >> 32) != e);
+        }
+        const unsigned long long k = ((a & 0xffffffffull) << 32) | (b & 0xffffffffull);
+        if (k > best) best = k;
+    }
+    return best;
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t saddr) {
     uint4 r;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(saddr));

@@ -23,6 +23,7 @@ cudaError_t tp_allreduce(reng_model* m, float* buf, size_t count, cudaStream_t s
 cudaError_t launch_tp_residual(reng_model* m, const float* part, int M, bool pdl, cudaStream_t st);
 cudaError_t launch_tp_ar_residual(reng_model* m, const float* part, int M, cudaStream_t st);
 bool tp_p2p(reng_model* m, int M);
+const HeadXchg* tp_head_xchg(reng_model* m);
 int tp_exchange_kind(reng_model* m);
 }  // namespace reng
 
@@ -75,6 +76,7 @@ struct reng_model {
     // M <= 2 and M > 2 activation rows
     int shape[5][2] = {};
     cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph_full = nullptr;  // the step with the whole LM head (logits requests) when `graph` shards it
     int kernels_per_step = 0;
     std::vector<int> host_pos;
     uint32_t* pinned = nullptr;  // pinned staging: ids [kRowsCap], positions [kRowsCap], error word
@@ -487,12 +489,23 @@ int k_gateup_launch(reng_model* m, int l, int M, cudaStream_t st) {
 }
 
 // LM head over rows [r0, r0 + M) of the step (logits and argmax rows 0..M-1).
-GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0) {
+// shard: this rank's vocabulary tiles only, the argmax keys exchanged with
+// the other ranks (tensor-parallel decode; the logits of other ranks' rows
+// are not written).
+GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0, bool shard = false) {
     GemvArgs h = norm_args(m, M, m->final_gamma);
     h.x = m->x_res + (size_t)r0 * m->hidden;
     h.ss_in = m->ss + (size_t)r0 * kSsStride;
     h.w = m->lm;
     h.tiles = m->lm_tiles;
+    if (shard) {
+        const int t0 = (int)((long long)m->rank * m->lm_tiles / m->world);
+        const int t1 = (int)((long long)(m->rank + 1) * m->lm_tiles / m->world);
+        h.w = m->lm + (size_t)t0 * proj_kc(m, m->hidden) * kBlockBytesBf16;
+        h.tiles = t1 - t0;
+        h.row0 = t0 * kTileRows;
+        h.hx = tp_head_xchg(m);
+    }
     h.out = m->logits;
     h.ldo = m->vocab;
     h.vocab = m->vocab;
@@ -510,15 +523,21 @@ GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0) {
     return h;
 }
 
-int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int r0 = 0) {
-    return linear(m, head_args(m, mode, M, slot, r0), EPI_LOGITS, 4, m->lm_grid, st);
+int k_head_launch(reng_model* m, int mode, int M, int slot, cudaStream_t st, int r0 = 0, bool shard = false) {
+    return linear(m, head_args(m, mode, M, slot, r0, shard), EPI_LOGITS, 4, m->lm_grid, st);
+}
+
+// Whether decode steps shard the LM head over the tensor-parallel ranks:
+// with the peer exchange set up and at most kMaxRows slots.
+bool head_sharded(reng_model* m) {
+    return m->world > 1 && m->B <= kMaxRows && tp_head_xchg(m) != nullptr;
 }
 
 // The kernels of one step.  mode 0: decode over the B slots (rows = slots,
 // ids from the device ring).  mode 1: prefill of `M` ids of slot `slot`
 // starting at the device position of that slot.  head: HEAD_NONE, HEAD_LAST
 // (the LM head on the last row only: its logits land in row 0) or HEAD_ALL.
-enum { HEAD_NONE = 0, HEAD_LAST = 1, HEAD_ALL = 2 };
+enum { HEAD_NONE = 0, HEAD_LAST = 1, HEAD_ALL = 2, HEAD_SHARD = 3 };
 int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_t st, int* nk) {
     const int before = m->launches;
     TRY(k_embed_launch(m, mode, M, slot, st));
@@ -530,6 +549,7 @@ int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_
         TRY(k_proj_launch(m, l, M, 1, st));
     }
     if (head == HEAD_ALL) TRY(k_head_launch(m, mode, M, slot, st));
+    else if (head == HEAD_SHARD) TRY(k_head_launch(m, mode, M, slot, st, 0, true));
     else if (head == HEAD_LAST) TRY(k_head_launch(m, mode, 1, slot, st, M - 1));
     if (nk) *nk = m->launches - before;
     return RENG_OK;
@@ -644,6 +664,23 @@ int build_step(reng_model* m) {
     return RENG_OK;
 }
 
+// One decode step (rows = the B slots) captured as a CUDA graph.
+int capture_step(reng_model* m, int head, cudaGraphExec_t* out, int* nk) {
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, 0, m->B, 0, head, m->st, nk);
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return RENG_OK;
+}
+
 int build_graph(reng_model* m) {
     cudaGraph_t g = nullptr;
     if (m->step_on) {
@@ -663,17 +700,9 @@ int build_graph(reng_model* m) {
         cudaGetLastError();
         m->step_on = false;
     }
-    CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, 0, m->B, 0, HEAD_ALL, m->st, &m->kernels_per_step);
-    cudaError_t e = cudaStreamEndCapture(m->st, &g);
-    if (rc) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
-    }
-    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&m->graph, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    const bool shard = head_sharded(m);
+    TRY(capture_step(m, shard ? HEAD_SHARD : HEAD_ALL, &m->graph, &m->kernels_per_step));
+    if (shard) TRY(capture_step(m, HEAD_ALL, &m->graph_full, nullptr));
     return RENG_OK;
 }
 
@@ -682,6 +711,7 @@ void free_model(reng_model* m) {
     cudaSetDevice(m->dev);
     if (m->st) cudaStreamSynchronize(m->st);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->graph_full) cudaGraphExecDestroy(m->graph_full);
     tp_destroy(m);
     for (void* p : m->allocs) cudaFree(p);
     if (m->pinned) cudaFreeHost(m->pinned);
@@ -1070,7 +1100,7 @@ extern "C" int reng_model_step_logits(reng_model* m, const uint32_t* ids, float*
     memcpy(m->pinned, ids, (size_t)m->B * 4);
     CU(cudaMemcpyAsync(m->ids_ring, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
     CU(cudaMemsetAsync(m->step, 0, 4, m->st));
-    CU(cudaGraphLaunch(m->graph, m->st));
+    CU(cudaGraphLaunch(m->graph_full ? m->graph_full : m->graph, m->st));
     std::vector<uint16_t> hl((size_t)m->B * m->vocab);
     CU(cudaMemcpyAsync(hl.data(), m->logits, hl.size() * 2, cudaMemcpyDeviceToHost, m->st));
     CU(cudaMemcpyAsync(m->pinned, m->ids_ring + m->B, (size_t)m->B * 4, cudaMemcpyDeviceToHost, m->st));

@@ -84,7 +84,6 @@ NcclApi* api() {
 
 constexpr int kArSlice = 256;    // hidden elements per CTA of the peer all-reduce
 constexpr int kArThreads = 64;   // a float4 of the slice per thread
-constexpr int kArMaxWorld = 8;
 
 // The peer all-reduce arguments.  Receive area of a rank: [2 parities]
 // [W source ranks][kMaxRows][hidden] 64-bit words, each (epoch << 32 |
@@ -93,7 +92,7 @@ constexpr int kArMaxWorld = 8;
 // the value stored with it: no fence, no separate flag, and every thread
 // waits only for the words of its own elements.
 struct ArArgs {
-    unsigned long long* recv[kArMaxWorld];  // every rank's receive area (peer mappings; own at [rank])
+    unsigned long long* recv[kTpMaxWorld];  // every rank's receive area (peer mappings; own at [rank])
     const float* part;             // this rank's partial [M][hidden]
     unsigned* epoch;               // [C] exchanges done per slice (this rank only)
     uint16_t* x_res;               // [M][hidden]
@@ -105,22 +104,18 @@ struct ArArgs {
 struct TpState {
     ncclComm_t comm = nullptr;
     bool p2p = false;              // the peer all-reduce is set up
-    void* region = nullptr;        // this rank's receive area (exported)
-    unsigned* epoch = nullptr;
+    void* region = nullptr;        // this rank's receive area + head key area (exported)
+    unsigned* epoch = nullptr;     // [C] all-reduce slices, then the head exchange count
+    HeadXchg* hx = nullptr;        // device copy of the head exchange (peer key areas)
     std::vector<void*> mapped;     // peers' regions opened in this process
     ArArgs ar{};
 };
 
 size_t ar_recv_words(int world, int hidden) { return (size_t)2 * world * kMaxRows * hidden; }
+constexpr size_t kHeadKeyWords = (size_t)2 * kTpMaxWorld * kMaxRows * 2;  // the head key area
 
 __device__ __forceinline__ unsigned long long ar_word(float v, unsigned e) {
     return ((unsigned long long)e << 32) | __float_as_uint(v);
-}
-__device__ __forceinline__ void st_words(unsigned long long* p, unsigned long long a, unsigned long long b) {
-    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
-}
-__device__ __forceinline__ void ld_words(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
-    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 __global__ void __launch_bounds__(kArThreads) k_tp_ar_residual(ArArgs a) {
@@ -206,26 +201,38 @@ __global__ void __launch_bounds__(kArThreads) k_tp_ar_residual(ArArgs a) {
 // Sets up the peer all-reduce: allocate and export this rank's region,
 // all-gather the IPC handles over NCCL, open the peers', and agree (an
 // NCCL min over the ranks' outcomes) so every rank takes the same path.
-// Returns false (after undoing what it did) when any rank could not.
-bool ar_setup(reng_model* m, TpState* s, NcclApi* a) {
+// Returns 1 when set up, 0 (after undoing what it did) when any rank could
+// not, -1 when this rank failed after the ranks agreed (the model is then
+// not created: the other ranks' exchanges would wait for it in vain).
+int ar_setup(reng_model* m, TpState* s, NcclApi* a) {
     const int W = tp_world_of(m), R = tp_rank_of(m), H = tp_hidden(m);
     const char* env = getenv("RENG_TP_P2P");
-    if (env && atoi(env) == 0) return false;  // every rank reads the same environment
-    int ok = W <= kArMaxWorld && H % 16 == 0 ? 1 : 0;
-    const size_t bytes = ar_recv_words(W, H) * 8;
+    if (env && atoi(env) == 0) return 0;  // every rank reads the same environment
+    int ok = W <= kTpMaxWorld && H % 16 == 0 ? 1 : 0;
+    const size_t words = ar_recv_words(W, H), bytes = (words + kHeadKeyWords) * 8;
     const int C = (H + kArSlice - 1) / kArSlice;
     cudaIpcMemHandle_t mine{};
     if (ok && cudaMalloc(&s->region, bytes) != cudaSuccess) ok = 0;
     if (ok && cudaMemset(s->region, 0, bytes) != cudaSuccess) ok = 0;
-    if (ok && cudaMalloc((void**)&s->epoch, (size_t)C * 4) != cudaSuccess) ok = 0;
-    if (ok && cudaMemset(s->epoch, 0, (size_t)C * 4) != cudaSuccess) ok = 0;
+    if (ok && cudaMalloc((void**)&s->epoch, (size_t)(C + 1) * 4) != cudaSuccess) ok = 0;
+    if (ok && cudaMemset(s->epoch, 0, (size_t)(C + 1) * 4) != cudaSuccess) ok = 0;
+    if (ok && cudaMalloc((void**)&s->hx, sizeof(HeadXchg)) != cudaSuccess) ok = 0;
     if (ok && cudaIpcGetMemHandle(&mine, s->region) != cudaSuccess) ok = 0;
     cudaGetLastError();
     // exchange: [W] handles, then the agreement word
     uint8_t* dev = nullptr;
     std::vector<cudaIpcMemHandle_t> all(W);
     int agree = 0;
-    if (cudaMalloc((void**)&dev, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t) + 16) != cudaSuccess) return false;
+    if (cudaMalloc((void**)&dev, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t) + 16) != cudaSuccess) {
+        // cannot take part in the exchange the other ranks are entering
+        if (s->region) cudaFree(s->region);
+        if (s->epoch) cudaFree(s->epoch);
+        if (s->hx) cudaFree(s->hx);
+        s->region = nullptr;
+        s->epoch = nullptr;
+        s->hx = nullptr;
+        return -1;
+    }
     uint8_t* send = dev + (size_t)W * sizeof(cudaIpcMemHandle_t);
     int* okd = reinterpret_cast<int*>(send + sizeof(cudaIpcMemHandle_t));
     bool done = cudaMemcpy(send, &mine, sizeof(mine), cudaMemcpyHostToDevice) == cudaSuccess &&
@@ -253,21 +260,31 @@ bool ar_setup(reng_model* m, TpState* s, NcclApi* a) {
            cudaMemcpy(&agree, okd, 4, cudaMemcpyDeviceToHost) == cudaSuccess;
     cudaFree(dev);
     if (done && agree == 1) {
-        s->p2p = true;
-        s->ar.epoch = s->epoch;
-        s->ar.rank = R;
-        s->ar.world = W;
-        s->ar.hidden = H;
-        return true;
+        HeadXchg hx{};
+        for (int r = 0; r < W; r++) hx.recv[r] = s->ar.recv[r] + words;
+        hx.epoch = s->epoch + C;
+        hx.rank = R;
+        hx.world = W;
+        if (cudaMemcpy(s->hx, &hx, sizeof(hx), cudaMemcpyHostToDevice) == cudaSuccess) {
+            s->p2p = true;
+            s->ar.epoch = s->epoch;
+            s->ar.rank = R;
+            s->ar.world = W;
+            s->ar.hidden = H;
+            return 1;
+        }
     }
+    const int rc = done && agree == 1 ? -1 : 0;  // -1: agreed, then this rank failed
     for (void* p : s->mapped) cudaIpcCloseMemHandle(p);
     s->mapped.clear();
     if (s->region) cudaFree(s->region);
     if (s->epoch) cudaFree(s->epoch);
+    if (s->hx) cudaFree(s->hx);
     s->region = nullptr;
     s->epoch = nullptr;
+    s->hx = nullptr;
     cudaGetLastError();
-    return false;
+    return rc;
 }
 }  // namespace
 
@@ -285,7 +302,7 @@ int tp_init(reng_model* m, const uint8_t* id) {
         return fail(RENG_E_NCCL, std::string("ncclCommInitRank: ") + a->GetErrorString(r));
     }
     tp_set_handle(m, s);
-    ar_setup(m, s, a);
+    if (ar_setup(m, s, a) < 0) return fail(RENG_E_CUDA, "tensor parallel: this rank could not set up the peer exchange");
     return RENG_OK;
 }
 
@@ -299,6 +316,7 @@ void tp_destroy(reng_model* m) {
     for (void* p : s->mapped) cudaIpcCloseMemHandle(p);
     if (s->region) cudaFree(s->region);
     if (s->epoch) cudaFree(s->epoch);
+    if (s->hx) cudaFree(s->hx);
     if (s->comm && api()->ok) api()->CommDestroy(s->comm);
     delete s;
     tp_set_handle(m, nullptr);
@@ -309,6 +327,12 @@ int tp_exchange_kind(reng_model* m) {
     TpState* s = static_cast<TpState*>(tp_handle(m));
     if (!s) return 0;
     return s->p2p ? 2 : 1;
+}
+
+// The device head exchange of a peer-mapped model (null otherwise).
+const HeadXchg* tp_head_xchg(reng_model* m) {
+    TpState* s = static_cast<TpState*>(tp_handle(m));
+    return s && s->p2p ? s->hx : nullptr;
 }
 
 bool tp_p2p(reng_model* m, int M) {

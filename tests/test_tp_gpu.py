@@ -1,8 +1,9 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): every rank holds
 its shard, the o_proj/down_proj partials are all-reduced inside the captured
 step (the fused peer all-reduce over NVLink for decode steps, NCCL for the
-prefill blocks; NCCL throughout with RENG_TP_P2P=0), all ranks produce the
-same ids (the reference's coordinator rule, crates/reng-model/src/bin/tp.rs:
+prefill blocks; NCCL throughout with RENG_TP_P2P=0), decode steps shard the
+LM head by vocabulary and swap argmax keys (the logits entry point runs the
+whole head and must agree on every rank), all ranks produce the same ids (the reference's coordinator rule, crates/reng-model/src/bin/tp.rs:
 604-675), and those ids follow the f32 host forward of the full model under
 teacher forcing (near-tie margin 0.5), with the prompt's last logits within
 cosine 0.999 of it.
@@ -61,15 +62,19 @@ def _worker(rank, port, bias, hidden, batch, p2p, q):
         nxt = last[0]
         ids = np.array(g.generate([nxt] * batch, 12)).reshape(12, batch)
         check_agreement([nxt] + [int(x) for x in ids.reshape(-1)], dist)
+        # one more step through the logits entry point (the whole LM head
+        # on every rank, while decode steps shard it over the ranks)
+        lg, nx = g.engine.step_logits(ids[-1])
         q.put((rank, {"nxt": nxt, "ids": [int(x) for x in ids[:, 0]], "rows": ids.tolist(), "last": last[1],
-                      "kind": kind}))
+                      "kind": kind, "step_logits": lg, "step_next": nx.tolist()}))
         g.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("bias,hidden,batch,p2p", [(False, 320, 1, True), (True, 256, 1, True),
-                                                   (False, 256, 3, True), (False, 320, 1, False)])
+                                                   (False, 256, 3, True), (False, 256, 4, True),
+                                                   (False, 320, 1, False)])
 def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias, hidden, batch, p2p):
     import torch
     if torch.cuda.device_count() < WORLD:
@@ -91,6 +96,9 @@ def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias, hidden, batch, p2p):
         assert p.exitcode == 0
     assert out[0]["rows"] == out[1]["rows"] and out[0]["nxt"] == out[1]["nxt"]
     assert out[0]["kind"] == out[1]["kind"] == (2 if p2p else 1)
+    assert np.array_equal(out[0]["step_logits"], out[1]["step_logits"])
+    assert out[0]["step_next"] == out[1]["step_next"]
+    assert out[0]["step_next"] == [int(x) for x in np.argmax(out[0]["step_logits"], axis=1)]
     cfg = _cfg(bias, hidden)
     w = random_weights(cfg, seed=21)
     prompt = prompt_ids(13, cfg.vocab_size, seed=2)
