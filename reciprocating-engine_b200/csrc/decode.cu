@@ -296,11 +296,13 @@ __global__ void __launch_bounds__(NWARP * 32) k_gemv(GemvArgs a, int use_smem) {
     }
 }
 
-// Shared x copy of a launch: staged when it fits (normalised inputs always).
-static size_t gemv_xbytes(const GemvArgs& a) {
+// Shared x copy of a launch with an nw-warp ring: staged when it fits beside
+// the ring (normalised inputs always: they are normalised in place); else
+// the fragments are read from global memory.
+static size_t gemv_xbytes(const GemvArgs& a, int nw) {
     size_t b = (size_t)a.M * gemv_xstride(a.K) * 2;
     const bool need = a.ss_in != nullptr;
-    if (b <= kGemvMaxSmem || need) return b;
+    if (need || (b <= kGemvMaxSmem && (size_t)nw * gemv_ring_bytes<kTmaStages>() + b <= 200 * 1024)) return b;
     return 0;
 }
 
@@ -325,7 +327,7 @@ static int gemv_per_sm(size_t smem) {
 template <int EPI, int NW, int ST, int W8>
 static cudaError_t launch_one(const GemvArgs& a, int per_sm, int max_grid, bool pdl, cudaStream_t st,
                               int* grid_out) {
-    const size_t xbytes = gemv_xbytes(a);
+    const size_t xbytes = gemv_xbytes(a, NW);
     const size_t smem = (size_t)NW * gemv_ring_bytes<ST>() + xbytes;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -365,7 +367,7 @@ static cudaError_t launch_one(const GemvArgs& a, int per_sm, int max_grid, bool 
 // keeps the next kernel's CTAs from starting early).
 template <int EPI, int NW, int W8>
 static cudaError_t launch_stages(const GemvArgs& a, int max_grid, bool pdl, cudaStream_t st, int* grid_out) {
-    const int p4 = gemv_per_sm<EPI, NW, 4, W8>((size_t)NW * gemv_ring_bytes<4>() + gemv_xbytes(a));
+    const int p4 = gemv_per_sm<EPI, NW, 4, W8>((size_t)NW * gemv_ring_bytes<4>() + gemv_xbytes(a, NW));
     if (p4 < 1) return cudaErrorInvalidValue;
     return launch_one<EPI, NW, 4, W8>(a, p4, max_grid, pdl, st, grid_out);
 }

@@ -180,6 +180,11 @@ __device__ __forceinline__ int am_unpack(unsigned long long key) {
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int nwarp, int max_grid, bool pdl, cudaStream_t st,
                         int* grid_out = nullptr);
 cudaError_t gemv_prepare();
+// The 3..8-row GEMV with register x fragments (gemv8.cu): whether it runs a
+// projection, its launch, and its shared-memory limits (before capture).
+bool gemv8_fits(const GemvArgs& a);
+cudaError_t launch_gemv8(const GemvArgs& a, int epi, bool pdl, cudaStream_t st);
+cudaError_t gemv8_prepare();
 cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
 cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);

@@ -53,6 +53,7 @@ struct reng_model {
     uint16_t *x_res = nullptr, *qbuf = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
     uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
     int launches = 0;                // kernels of this library enqueued so far
+    bool gemv8 = true;               // 3..8-row projections on the register-fragment GEMV (RENG_GEMV8=0: off)
     float* gpart = nullptr;          // GEMM split-K partials (splits without a cluster)
     size_t gpart_floats = 0;
     int* gcnt = nullptr;             // GEMM split-K arrivals per super-tile
@@ -347,7 +348,11 @@ bool use_gemm(const reng_model* m, int M, int kind) {
 // to 16 columns.  kind indexes the GEMV launch shapes.
 int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cudaStream_t st) {
     if (!use_gemm(m, g.M, kind)) {
-        CU(launch_gemv(g, epi, m->shape[kind][g.M > 2], max_grid, true, st));
+        if (m->gemv8 && gemv8_fits(g)) {
+            CU(launch_gemv8(g, epi, true, st));
+        } else {
+            CU(launch_gemv(g, epi, m->shape[kind][g.M > 2], max_grid, true, st));
+        }
         m->launches++;
         return RENG_OK;
     }
@@ -729,6 +734,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
     m->sms = num_sms(m->dev);
     CU(gemv_prepare());
+    CU(gemv8_prepare());
     CU(gemm_prepare());
     m->rank = d->tp_rank;
     m->world = d->tp_world;
@@ -884,6 +890,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     const int kch = (H + kChunkK - 1) / kChunkK;
     const int kcs[5] = {proj_kc(m, H), proj_kc(m, m->q_dim), proj_kc(m, H), proj_kc(m, m->inter), kch};
     for (int k = 0; k < 5; k++) pick_shape(m, k, kcs[k], &m->shape[k][0], &m->shape[k][1]);
+    {
+        const char* v = getenv("RENG_GEMV8");  // a tuning knob: 0 keeps the shared-memory GEMV
+        m->gemv8 = !(v && atoi(v) == 0);
+    }
     m->lm_grid = m->sms * 32;  // argmax partial slots: an upper bound of the persistent grid
     TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));

@@ -265,3 +265,36 @@ def test_persistent_step_matches_per_projection_kernels(lib, monkeypatch, batch,
     assert starts == sorted(starts) and rows[-1][3] > 0
     ref.close()
     eng.close()
+
+
+@pytest.mark.parametrize("batch,fp8", [(8, False), (3, False), (8, True)])
+def test_register_fragment_gemv_equals_shared_memory_gemv(lib, monkeypatch, batch, fp8):
+    """At 3..8 rows the Llama-8B-width q/k/v, o_proj and gate/up projections
+    run on the register-fragment GEMV (gemv8.cu).  It splits k over the
+    warps and adds their slices in the same order as the shared-memory GEMV
+    (RENG_GEMV8=0), so the logits are bit-identical."""
+    from reng.config import llama31_8b
+    from reng.model import Engine
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = llama31_8b()
+    w = random_weights(cfg, seed=3, layers=2)
+    cfg.num_hidden_layers = 2
+    q = ("e4m3", "pcs") if fp8 else None
+    monkeypatch.setenv("RENG_GEMV8", "0")
+    ref = Engine(cfg, w, batch=batch, capacity=64, fp8=q)
+    monkeypatch.delenv("RENG_GEMV8")
+    eng = Engine(cfg, w, batch=batch, capacity=64, fp8=q)
+    prompts = [prompt_ids(5 + b, cfg.vocab_size, seed=70 + b) for b in range(batch)]
+    seeds = [ref.prefill(b, prompts[b])[0] for b in range(batch)]
+    assert seeds == [eng.prefill(b, prompts[b])[0] for b in range(batch)]
+    ids = list(seeds)
+    for _ in range(3):
+        la, na = ref.step_logits(ids)
+        lb, nb = eng.step_logits(ids)
+        assert np.array_equal(la, lb)
+        assert np.array_equal(na, nb)
+        ids = [int(x) for x in na]
+    assert np.array_equal(eng.decode(ids, 3), ref.decode(ids, 3))
+    ref.close()
+    eng.close()
