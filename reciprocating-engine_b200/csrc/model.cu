@@ -334,13 +334,14 @@ GemvArgs norm_args(reng_model* m, int M, const float* gain) {
 // Rows of a step above which projections run on the tcgen05 GEMM (bf16
 // weights); at or below it the GEMV kernels (mma N = kMaxRows) stream the
 // weights with the rows in registers.
-// From 4 rows on, down_proj (kind 3) and the LM head (kind 4) also run on the
-// GEMM: their GEMV would stage 4-8 rows of a wide x (inter = 14336) or
-// share shared memory with it, leaving the weight ring short (measured at
-// batch 8: down 52 -> 47 us).
+// From 4 rows on, down_proj (kind 3) also runs on the GEMM: its GEMV would
+// stage 4-8 rows of a wide x (inter = 14336), leaving the weight ring short
+// (measured at batch 8: down 52 -> 30 us on the GEMM with plain K splits).
+// The LM head (kind 4) does too unless the register-fragment GEMV takes it
+// (173 against 206 us at batch 8).
 bool use_gemm(const reng_model* m, int M, int kind) {
     if (m->w8) return false;
-    return M > kMaxRows || (M >= 4 && (kind == 3 || kind == 4));
+    return M > kMaxRows || (M >= 4 && (kind == 3 || (kind == 4 && !m->gemv8)));
 }
 
 // One projection: the GEMV for few rows, else (RMSNorm of x into xn when the

@@ -270,9 +270,12 @@ def test_persistent_step_matches_per_projection_kernels(lib, monkeypatch, batch,
 @pytest.mark.parametrize("batch,fp8", [(8, False), (3, False), (8, True)])
 def test_register_fragment_gemv_equals_shared_memory_gemv(lib, monkeypatch, batch, fp8):
     """At 3..8 rows the Llama-8B-width q/k/v, o_proj and gate/up projections
-    run on the register-fragment GEMV (gemv8.cu).  It splits k over the
-    warps and adds their slices in the same order as the shared-memory GEMV
-    (RENG_GEMV8=0), so the logits are bit-identical."""
+    (and the LM head) run on the register-fragment GEMV (gemv8.cu).  It
+    splits k over the warps and adds their slices in the same order as the
+    shared-memory GEMV (RENG_GEMV8=0), so the layers' outputs are
+    bit-identical; with RENG_GEMV8=0 the bf16 LM head at 4..8 rows runs on
+    the tcgen05 GEMM, whose f32 sums differ in order (logits within a bf16
+    rounding there)."""
     from reng.config import llama31_8b
     from reng.model import Engine
     from reng.synth import prompt_ids
@@ -292,7 +295,10 @@ def test_register_fragment_gemv_equals_shared_memory_gemv(lib, monkeypatch, batc
     for _ in range(3):
         la, na = ref.step_logits(ids)
         lb, nb = eng.step_logits(ids)
-        assert np.array_equal(la, lb)
+        if batch < 4 or fp8:
+            assert np.array_equal(la, lb)
+        else:
+            assert np.all(np.abs(la - lb) <= 2.0 ** -7 * np.maximum(np.abs(la), np.abs(lb)) + 1e-6)
         assert np.array_equal(na, nb)
         ids = [int(x) for x in na]
     assert np.array_equal(eng.decode(ids, 3), ref.decode(ids, 3))
