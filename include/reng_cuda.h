@@ -286,6 +286,14 @@ int reng_tp_unique_id(uint8_t out[128]);
  * NCCL.  The reference exchanges through hcclAllReduce (hccl.rs:646-651). */
 int reng_model_tp_exchange(reng_model *m, int *kind);
 
+/* Check of the exchange's failure path on one GPU: the peer all-reduce
+ * kernel as rank 0 of two whose rank 1 never answers.  Its waits give up
+ * after their bound (2 s) and it reports RENG_E_TIMEOUT, which this call
+ * returns; the context stays usable (no fault, no hang).  Any other return
+ * is a failure of the check.  The reference's counterpart is the HCCL
+ * watchdog of hccl.rs:580-637. */
+int reng_tp_peer_wait_check(int device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -423,6 +423,59 @@ cudaError_t launch_tp_residual(reng_model* m, const float* part, int M, bool pdl
 
 }  // namespace reng
 
+// The failure path of the peer exchange on one GPU: the exchange kernel as
+// rank 0 of a two-rank group whose rank 1 never runs, so the epoch words it
+// waits for are never written.  Every wait gives up after its bound, the
+// kernel records RENG_E_TIMEOUT and returns; the context must stay usable.
+extern "C" int reng_tp_peer_wait_check(int device) {
+    using namespace reng;
+    RENG_CUDA_TRY(cudaSetDevice(device));
+    constexpr int H = 512, M = 1;
+    const size_t words = ar_recv_words(2, H);
+    unsigned long long *mine = nullptr, *peer = nullptr;
+    unsigned* epoch = nullptr;
+    float *part = nullptr, *ss = nullptr;
+    uint16_t* x = nullptr;
+    int* err = nullptr;
+    int rc = RENG_OK;
+    auto alloc = [&](void** p, size_t b) {
+        if (rc == RENG_OK && cudaMalloc(p, b) != cudaSuccess) rc = fail(RENG_E_NOMEM, "reng_tp_peer_wait_check: cudaMalloc");
+        if (rc == RENG_OK) cudaMemset(*p, 0, b);
+    };
+    alloc((void**)&mine, words * 8);
+    alloc((void**)&peer, words * 8);
+    alloc((void**)&epoch, 64);
+    alloc((void**)&part, (size_t)M * H * 4);
+    alloc((void**)&ss, (size_t)M * kSsStride * 4);
+    alloc((void**)&x, (size_t)M * H * 2);
+    alloc((void**)&err, 4);
+    if (rc == RENG_OK) {
+        ArArgs a{};
+        a.recv[0] = mine;  // rank 0: this launch
+        a.recv[1] = peer;  // rank 1: receives this rank's values, never answers
+        a.part = part;
+        a.epoch = epoch;
+        a.x_res = x;
+        a.ss = ss;
+        a.err = err;
+        a.rank = 0;
+        a.world = 2;
+        a.hidden = H;
+        a.M = M;
+        k_tp_ar_residual<<<(H + kArSlice - 1) / kArSlice, kArThreads>>>(a);
+        int h = 0;
+        if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = fail(RENG_E_CUDA, std::string("reng_tp_peer_wait_check: ") + cudaGetErrorString(cudaGetLastError()));
+        else if (h == RENG_E_TIMEOUT)
+            rc = fail(RENG_E_TIMEOUT, "reng_tp_peer_wait_check: the exchange gave up on its bounded wait (expected)");
+        else
+            rc = fail(RENG_E_STATE, "reng_tp_peer_wait_check: the exchange did not report the missing peer");
+    }
+    for (void* p : {(void*)mine, (void*)peer, (void*)epoch, (void*)part, (void*)ss, (void*)x, (void*)err})
+        if (p) cudaFree(p);
+    return rc;
+}
+
 extern "C" int reng_tp_unique_id(uint8_t out[128]) {
     RENG_CHECK_ARG(out != nullptr, "reng_tp_unique_id: out is NULL");
     reng::NcclApi* a = reng::api();

@@ -79,6 +79,7 @@ SIGNATURES = {
     "reng_model_reset": ([_P, C.c_int], C.c_int),
     "reng_model_position": ([_P, C.c_int, _P], C.c_int),
     "reng_model_tp_exchange": ([_P, _P], C.c_int),
+    "reng_tp_peer_wait_check": ([C.c_int], C.c_int),
     "reng_model_device_bytes": ([_P, _P], C.c_int),
     "reng_model_last_times": ([_P, _P], C.c_int),
     "reng_model_time_kernels": ([_P, C.c_int, _P], C.c_int),

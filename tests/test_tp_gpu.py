@@ -107,3 +107,18 @@ def test_tensor_parallel_decode_on_two_gpus(reng_lib, bias, hidden, batch, p2p):
     want = oracle_for(cfg, w).forward(seq, sin, cos, logits_from=prompt.size - 1)
     assert cosine(out[0]["last"], want[0]) >= 0.999
     check_greedy([out[0]["nxt"]] + out[0]["ids"], want)
+
+
+def test_peer_exchange_reports_a_missing_peer(reng_lib):
+    """The exchange's failure path on one GPU: rank 1 of the group never
+    answers, the kernel's bounded waits give up (2 s), the call reports
+    RENG_E_TIMEOUT, and the device keeps working (a model decodes after)."""
+    from reng._lib import RENG_E_TIMEOUT, lib
+    from reng.model import Engine
+    from reng.weights import random_weights
+    assert lib().reng_tp_peer_wait_check(0) == RENG_E_TIMEOUT
+    cfg = _cfg(False)
+    e = Engine(cfg, random_weights(cfg, seed=5), batch=1, capacity=32)
+    nxt = e.prefill(0, np.arange(5, dtype=np.uint32))[0]
+    assert e.decode([nxt], 3).shape == (3, 1)
+    e.close()
