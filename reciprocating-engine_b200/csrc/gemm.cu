@@ -598,7 +598,12 @@ int gemm_pick_stages(int n, bool one_per_sm, int epi) {
     // CTA per SM were slower than 4 (q/k/v 55 against 33 us).
     const unsigned stage = kStageA + (unsigned)n * 128u;
     const unsigned fixed = 2048u + (epi == EPI_LOGITS ? 9216u : 1024u);
-    int s = one_per_sm ? 4 : (int)((114u * 1024u - fixed) / stage);
+    static const int one_sm = [] {  // RENG_GEMM_STAGES1: stages at one CTA per SM (a tuning knob)
+        const char* v = getenv("RENG_GEMM_STAGES1");
+        const int x = v ? atoi(v) : 0;
+        return x >= 2 && x <= kGemmMaxStages ? x : 4;
+    }();
+    int s = one_per_sm ? one_sm : (int)((114u * 1024u - fixed) / stage);
     const int fit = (int)((unsigned)kGemmStageBudget / stage);
     if (s > fit) s = fit;
     return s < 2 ? 2 : (s > kGemmMaxStages ? kGemmMaxStages : s);
