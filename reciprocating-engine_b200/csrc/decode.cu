@@ -572,20 +572,20 @@ cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t
     if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.hpg * (a.hd / 4) > kAttnThreads)
         return cudaErrorInvalidValue;
     // key slices per (row, KV group): 8 (a cluster) when the rows x groups
-    // are few, fewer once they alone fill the GPU several times over
+    // are few, fewer as they grow
     int dev = 0;
     cudaGetDevice(&dev);
-    const long long units = (long long)a.M * a.n_kv, want = 4LL * num_sms(dev);
+    const long long units = (long long)a.M * a.n_kv;
     static const int fixed_ns = [] {  // RENG_ATTN_SLICES: a tuning knob fixing the slices (1, 2, 4 or 8)
         const char* v = getenv("RENG_ATTN_SLICES");
         const int x = v ? atoi(v) : 0;
         return x == 1 || x == 2 || x == 4 || x == 8 ? x : 0;
     }();
-    int ns = kAttnCluster;
-    while (ns > 1 && units * ns / 2 >= want) ns /= 2;
-    // rows x groups alone at twice the SMs: no slicing (Llama-8B b64: 512
-    // units, attention 27.9 us with 2 slices, 24.9 with 1, 39.5 with 4)
-    if (units >= 2LL * num_sms(dev)) ns = 1;
+    // Slices per (row, KV group), measured on B200 (Llama-8B, 8 KV groups):
+    // b1 (8 units) 8 slices; b8 (64 units) 4 beat 8 and 2 (7.9 against 10.0
+    // and 9.2 us); b16 4 beat 8 (10.6 against 19.2 us); b64 (512 units) 1
+    // beat 2 and 4 (24.9 against 27.9 and 39.5 us).
+    int ns = units >= 2LL * num_sms(dev) ? 1 : units >= 64 ? 4 : kAttnCluster;
     if (fixed_ns) ns = fixed_ns;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
