@@ -133,6 +133,37 @@ class LlamaConfig:
     def from_json(text):
         return LlamaConfig.from_dict(json.loads(text))
 
+    # ------------------------------------------------------ engine support --
+    ENGINE_TYPES = (None, "llama", "qwen2", "mistral")
+
+    def unsupported(self, capacity=None):
+        """What this engine's kernels do not compute for this config (empty
+        when it runs as written).  The reference parses more families than
+        its device graph covers and refuses what it has no node for
+        (`activation`, lib.rs:318-330; `mlp_bias`, :1479); this engine does
+        the same for the features outside the Llama/Qwen2 decoder it runs,
+        instead of computing a plain Llama in their place."""
+        out = []
+        raw = self.raw or {}
+        if self.model_type not in self.ENGINE_TYPES:
+            out.append("model_type %s" % self.model_type)
+        if (self.hidden_act or "silu") != "silu":
+            out.append("activation %s" % self.hidden_act)
+        if self.rotary_dim() != self.head_dim():
+            out.append("partial rotary (%d of %d head dims)" % (self.rotary_dim(), self.head_dim()))
+        if raw.get("mlp_bias"):
+            out.append("mlp_bias")
+        for k in ("embedding_multiplier", "attention_multiplier", "residual_multiplier", "logits_scaling",
+                  "final_logit_softcapping", "attn_logit_softcapping", "query_pre_attn_scalar"):
+            if raw.get(k) is not None:
+                out.append(k)
+        if raw.get("qk_norm") or raw.get("use_qk_norm"):
+            out.append("q/k RMSNorm")
+        win = raw.get("sliding_window")
+        if win and raw.get("use_sliding_window", True) and capacity is not None and capacity > int(win):
+            out.append("sliding window %d below the capacity %d" % (int(win), capacity))
+        return out
+
     @staticmethod
     def load(model_dir):
         with open(os.path.join(model_dir, "config.json")) as f:

@@ -56,6 +56,9 @@ def fp8_switch(value, flag=False):
 class Engine:
     def __init__(self, cfg, w, batch=1, capacity=1024, device=0, tp_rank=0, tp_world=1,
                  nccl_id=None, fp8=None):
+        missing = cfg.unsupported(capacity)
+        if missing:
+            raise ValueError("this engine does not run %s" % ", ".join(missing))
         self.cfg = cfg
         self.batch = batch
         self.capacity = capacity

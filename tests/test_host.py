@@ -134,3 +134,35 @@ def test_fp8_format_enums_mirror_the_reference():
     assert Fp8Format.from_name("hf8") is Fp8Format.E4M3 and Fp8Format.from_name("f8") is Fp8Format.E5M2
     assert Fp8Format.from_name("fp4") is None
     assert Scaling.from_name("per-channel") is Scaling.PerChannel and Scaling.from_name("x") is None
+
+
+def test_engine_refuses_what_its_kernels_do_not_compute():
+    """Configs the loader parses but the engine's decoder does not run are
+    refused before any device work, with the features named (the reference
+    refuses activations and MLP biases it has no node for,
+    crates/reng-model/src/lib.rs:318-330, :1479)."""
+    from reng.config import LlamaConfig, llama31_8b, qwen25_32b, smollm2_135m
+    from reng.model import Engine
+    base = {"hidden_size": 256, "intermediate_size": 512, "num_hidden_layers": 2,
+            "num_attention_heads": 4, "num_key_value_heads": 2, "vocab_size": 1024}
+    for c in (llama31_8b(), qwen25_32b(), smollm2_135m(), LlamaConfig.from_dict(dict(base, model_type="llama")),
+              LlamaConfig.from_dict(dict(base, model_type="qwen2", sliding_window=4096, use_sliding_window=False))):
+        assert c.unsupported(capacity=8192) == []
+    cases = [
+        (dict(base, model_type="qwen3"), "model_type qwen3"),
+        (dict(base, model_type="olmo2"), "model_type olmo2"),
+        (dict(base, model_type="llama", hidden_act="gelu_pytorch_tanh"), "activation"),
+        (dict(base, model_type="llama", partial_rotary_factor=0.5), "partial rotary"),
+        (dict(base, model_type="llama", mlp_bias=True), "mlp_bias"),
+        (dict(base, model_type="granite", embedding_multiplier=12.0), "embedding_multiplier"),
+        (dict(base, model_type="mistral", sliding_window=1024), "sliding window"),
+        ({"model_type": "gemma3", "text_config": {}}, "model_type gemma3_text"),
+    ]
+    for d, what in cases:
+        cfg = LlamaConfig.from_dict(d)
+        miss = cfg.unsupported(capacity=4096)
+        assert any(what in m for m in miss), (d, miss)
+        with pytest.raises(ValueError, match="does not run"):
+            Engine(cfg, {"embed": np.zeros((1, 1), np.uint16)}, capacity=4096)
+    # a sliding window at or above the capacity attends exactly as full attention
+    assert LlamaConfig.from_dict(dict(base, model_type="mistral", sliding_window=4096)).unsupported(4096) == []
