@@ -105,26 +105,32 @@ def dist_env():
 
 # --------------------------------------------------------------- CPU arm --
 
+_CPU_MODELS = {}
+
+
 def cpu_sample(cfg_full, tokens=32, layers=2, threads=0, seed=0, repeats=1):
     """Time the oracle (CPU f32 forward restating the reference's
     model_forward_cpu) on a layer-truncated model of the workload's widths:
     per-layer time and LM-head time over `tokens` teacher-forced tokens,
-    scaled to the full depth.  Returns (tok/s, cores, sample description)."""
-    import numpy as np
+    scaled to the full depth.  The sample model is built once per shape
+    (weight generation is not timed).  Returns (tok/s, cores, sample
+    description)."""
     import oracle
     from reng.rope import rope_caches_for
     from reng.synth import prompt_ids
     from reng.weights import random_weights
     cfg = cfg_full
-    w = random_weights(cfg, seed=seed, layers=layers)
-    sin, cos = rope_caches_for(cfg, tokens)
-    base = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_heads=cfg.num_attention_heads,
-                n_kv_heads=cfg.n_kv_heads(), head_dim=cfg.head_dim(), vocab=cfg.vocab_size,
-                eps=cfg.rms_norm_eps, attn_scale=cfg.attention_scale(), has_bias=int(cfg.has_bias()))
-    ids = prompt_ids(tokens, cfg.vocab_size, seed=seed)
-    m_layers = oracle.Model(dict(base, n_layers=layers), w["layers"], w["final_gamma"],
-                            w["lm_head"], w["embed"])
-    m_head = oracle.Model(dict(base, n_layers=0), [], w["final_gamma"], w["lm_head"], w["embed"])
+    key = (cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads, cfg.vocab_size, layers, tokens, seed)
+    if key not in _CPU_MODELS:
+        w = random_weights(cfg, seed=seed, layers=layers)
+        base = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_heads=cfg.num_attention_heads,
+                    n_kv_heads=cfg.n_kv_heads(), head_dim=cfg.head_dim(), vocab=cfg.vocab_size,
+                    eps=cfg.rms_norm_eps, attn_scale=cfg.attention_scale(), has_bias=int(cfg.has_bias()))
+        _CPU_MODELS[key] = (
+            oracle.Model(dict(base, n_layers=layers), w["layers"], w["final_gamma"], w["lm_head"], w["embed"]),
+            oracle.Model(dict(base, n_layers=0), [], w["final_gamma"], w["lm_head"], w["embed"]),
+            rope_caches_for(cfg, tokens), prompt_ids(tokens, cfg.vocab_size, seed=seed))
+    m_layers, m_head, (sin, cos), ids = _CPU_MODELS[key]
     cores = oracle.lib().orc_max_threads() if threads <= 0 else threads
     best = None
     for _ in range(repeats):
