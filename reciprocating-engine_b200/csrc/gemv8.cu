@@ -1,5 +1,5 @@
-// Packed-weight GEMV for 3..8 activation rows with the x fragments held in
-// registers (decode at batch 3..8).
+// Packed-weight GEMV for 2..8 activation rows with the x fragments held in
+// registers (decode at batch 2..8).
 //
 // The shared-memory GEMV (decode.cu) stages the x rows in each CTA: at 8
 // rows of 4096 that is 66 KB, which leaves one 8-warp CTA per SM with a
@@ -342,12 +342,19 @@ cudaError_t prepare8_e() {
 }
 }  // namespace
 
-// Whether the register-fragment GEMV runs this projection: 3..8 rows, every
+// Whether the register-fragment GEMV runs this projection: 2..8 rows, every
 // warp the same k-range of 8 or 10 packed blocks (K of 4096 or 5120), an x
 // row within three ring stages.
 bool gemv8_fits(const GemvArgs& a) {
-    return a.M >= 3 && a.M <= kMaxRows && (a.kc == 8 * kW8Warps || a.kc == 10 * kW8Warps) && a.K <= kW8MaxK &&
-           a.K % 8 == 0 && a.kc * kChunkK >= a.K;
+    // from 2 rows: measured on B200 (Llama-8B), b2 4.47 -> 4.07 ms per step;
+    // at 1 row the 444-CTA shared-memory GEMV stays ahead (3.20 against 3.36)
+    static const int min_rows = [] {  // RENG_GEMV8_MIN_ROWS: a tuning knob (1..8)
+        const char* v = getenv("RENG_GEMV8_MIN_ROWS");
+        const int x = v ? atoi(v) : 0;
+        return x >= 1 && x <= kMaxRows ? x : 2;
+    }();
+    return a.M >= min_rows && a.M <= kMaxRows && (a.kc == 8 * kW8Warps || a.kc == 10 * kW8Warps) &&
+           a.K <= kW8MaxK && a.K % 8 == 0 && a.kc * kChunkK >= a.K;
 }
 
 cudaError_t gemv8_prepare() {
