@@ -25,6 +25,14 @@ def test_header_declares_the_boundary():
         assert must in names
 
 
+def test_integration_ffi_stub_declares_every_function():
+    """The Rust FFI stub a maintainer would add binds
+    exactly the functions the header declares."""
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        stub = set(re.findall(r"pub fn (reng_[a-z0-9_]+)\(", f.read()))
+    assert stub == set(declared_functions()), sorted(stub ^ set(declared_functions()))
+
+
 def test_library_exports_every_declared_symbol(reng_lib):
     L = reng_lib.lib()
     missing = [n for n in declared_functions() if not hasattr(L, n)]
