@@ -329,10 +329,11 @@ def run_ours(args, cfg):
             "gpu_launches": kpl * args.steps,
             "roofline": {"bound": "hbm", "kernel": ("gemv<SWIGLU> gate/up" if B <= 8 or args.weights == "fp8"
                                                     else "rmsnorm rows + tcgen05 gemm<SWIGLU> gate/up")
-                         + " (layer-cycled)",
+                         + (" (layer-cycled, this rank's 1/%d of the columns)" % ws if ws > 1 else " (layer-cycled)"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": MEASURED_TRAFFIC.get((args.model, B, args.weights)),
+                         # ncu traffic was captured for the whole matrix on one GPU
+                         "traffic": MEASURED_TRAFFIC.get((args.model, B, args.weights)) if ws == 1 else None,
                          "bytes_per_launch": gu_bytes},
             "step_roofline": {"bytes_per_step": bytes_step, "achieved_gbs": step_gbs,
                               "frac_of_measured": step_gbs / peak,
