@@ -22,12 +22,12 @@ class Cfg(C.Structure):
     _fields_ = [("hidden", C.c_int32), ("inter", C.c_int32), ("n_layers", C.c_int32),
                 ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
                 ("vocab", C.c_int32), ("eps", C.c_float), ("attn_scale", C.c_float),
-                ("has_bias", C.c_int32)]
+                ("has_bias", C.c_int32), ("qn_width", C.c_int32), ("kn_width", C.c_int32)]
 
 
 class Layer(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in
-                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv")]
+                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv", "qn", "kn")]
 
 
 def build():
@@ -137,15 +137,24 @@ class Model:
 
     def __init__(self, cfg, layers, final_gamma, lm_head, embed):
         # cfg: dict with hidden, inter, n_layers, n_heads, n_kv_heads, head_dim, vocab,
-        # eps, attn_scale, has_bias.  layers: list of dicts of numpy arrays.
+        # eps, attn_scale, has_bias, and qn_width / kn_width (q / k norm part
+        # widths, 0 or absent = none).  layers: list of dicts of numpy arrays.
         self.cfg = cfg
         self._keep = []
         self.c = Cfg(cfg["hidden"], cfg["inter"], cfg["n_layers"], cfg["n_heads"],
                      cfg["n_kv_heads"], cfg["head_dim"], cfg["vocab"], cfg["eps"],
-                     cfg["attn_scale"], int(cfg.get("has_bias", 0)))
+                     cfg["attn_scale"], int(cfg.get("has_bias", 0)), int(cfg.get("qn_width", 0)),
+                     int(cfg.get("kn_width", 0)))
+        for key, width in (("qn", self.c.qn_width), ("kn", self.c.kn_width)):
+            for lw in layers:
+                g = lw.get(key)
+                if width and (g is None or np.asarray(g).size != width):
+                    raise ValueError("%s_width %d needs a [%d] %s gain in every layer"
+                                     % (key, width, width, key))
         arr = (Layer * len(layers))()
         for i, lw in enumerate(layers):
-            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv"):
+            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv",
+                         "qn", "kn"):
                 a = lw.get(name)
                 if a is None:
                     continue

@@ -57,6 +57,8 @@ class Engine:
     def __init__(self, cfg, w, batch=1, capacity=1024, device=0, tp_rank=0, tp_world=1,
                  nccl_id=None, fp8=None):
         missing = cfg.unsupported(capacity)
+        if any(lw.get(k) is not None for lw in w.get("layers", ()) for k in ("qn", "kn")):
+            missing = missing + ["q/k RMSNorm gains"]
         if missing:
             raise ValueError("this engine does not run %s" % ", ".join(missing))
         self.cfg = cfg

@@ -29,9 +29,10 @@ NAMES = {
     "wg": "mlp.gate_proj.weight", "wu": "mlp.up_proj.weight", "wd": "mlp.down_proj.weight",
     "g1": "input_layernorm.weight", "g2": "post_attention_layernorm.weight",
     "bq": "self_attn.q_proj.bias", "bk": "self_attn.k_proj.bias", "bv": "self_attn.v_proj.bias",
+    "qn": "self_attn.q_norm.weight", "kn": "self_attn.k_norm.weight",
 }
 MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
-VECS = ("g1", "g2", "bq", "bk", "bv")
+VECS = ("g1", "g2", "bq", "bk", "bv", "qn", "kn")
 
 _DT = {"BF16": (np.uint16, 2), "F32": (np.float32, 4), "F16": (np.float16, 2)}
 
@@ -139,6 +140,14 @@ def load_weights(model_dir, cfg):
         if cfg.has_bias():
             for k in ("bq", "bk", "bv"):
                 lw[k] = get("model.layers.%d.%s" % (l, NAMES[k]), "f32", shapes[k])
+        for k, full in (("qn", qd), ("kn", kvd)):
+            # optional q/k norm gains: [head_dim] per head (Qwen3) or the whole
+            # projection row (OLMo-2), as reng-model reads them
+            # (crates/reng-model/src/lib.rs:1607-1609)
+            name = "model.layers.%d.%s" % (l, NAMES[k])
+            if name in where:
+                n = where[name].shape(name)
+                lw[k] = get(name, "f32", (hd,) if tuple(n) == (hd,) else (full,))
         layers.append(lw)
     embed = get("model.embed_tokens.weight", "bf16", (cfg.vocab_size, h))
     if cfg.tie_word_embeddings or "lm_head.weight" not in where:

@@ -3,9 +3,12 @@
 The reference's external oracle (tools/oracle/oracle.py) runs a checkpoint
 through transformers' AutoModelForCausalLM in f32 and records the logits.
 This script does the same on seeded random weights written as a
-config.json + model.safetensors pair, for a Llama decoder and a Qwen2
-decoder (q/k/v biases), and stores the weights (bf16 bits), the prompt ids
-and the transformers logits in tests/golden/forward_golden.npz.
+config.json + model.safetensors pair, for a Llama decoder, a Qwen2
+decoder (q/k/v biases) and a Qwen3 decoder (per-head q/k RMSNorm, no
+biases), and stores the weights (bf16 bits), the prompt ids and the
+transformers logits in tests/golden/forward_golden.npz.  The Qwen3 norm
+gains are drawn after everything else, so the Llama / Qwen2 arrays do not
+depend on them.
 
     python tests/golden/make_forward_golden.py
 
@@ -33,7 +36,7 @@ TOKENS = 24
 
 def main():
     import torch
-    from transformers import LlamaConfig, LlamaForCausalLM, Qwen2Config, Qwen2ForCausalLM
+    from transformers import LlamaForCausalLM, Qwen2ForCausalLM, Qwen3ForCausalLM
 
     from reng.config import LlamaConfig as RCfg
     from reng.synth import bf16_bits_to_f32, f32_to_bf16_bits
@@ -62,19 +65,25 @@ def main():
     fg = (1.0 + 0.1 * rng.standard_normal(h)).astype(np.float32)
     ids = rng.integers(0, V, TOKENS).astype(np.uint32)
 
+    norms = [{"qn": (1.0 + 0.2 * rng.standard_normal(hd)).astype(np.float32),
+              "kn": (1.0 + 0.2 * rng.standard_normal(hd)).astype(np.float32)}
+             for _ in layers]
+
     out = {"ids": ids, "embed": embed, "lm_head": lm, "final_gamma": fg}
     for l, lw in enumerate(layers):
-        for k, v in lw.items():
+        for k, v in list(lw.items()) + list(norms[l].items()):
             out["l%d_%s" % (l, k)] = v
-    for arch in ("llama", "qwen2"):
+    classes = {"llama": LlamaForCausalLM, "qwen2": Qwen2ForCausalLM, "qwen3": Qwen3ForCausalLM}
+    for arch, cls in classes.items():
         with tempfile.TemporaryDirectory() as d:
             rc = RCfg.from_dict(dict(CFG, model_type=arch, attention_bias=arch == "qwen2"))
-            ws = {"layers": [dict(lw) if arch == "qwen2" else
-                             {k: v for k, v in lw.items() if not k.startswith("b")}
-                             for lw in layers],
-                  "embed": embed, "lm_head": lm, "final_gamma": fg}
-            save_checkpoint(d, rc, ws)
-            cls = LlamaForCausalLM if arch == "llama" else Qwen2ForCausalLM
+            ls = []
+            for l, lw in enumerate(layers):
+                x = {k: v for k, v in lw.items() if arch == "qwen2" or not k.startswith("b")}
+                if arch == "qwen3":
+                    x.update(norms[l])
+                ls.append(x)
+            save_checkpoint(d, rc, {"layers": ls, "embed": embed, "lm_head": lm, "final_gamma": fg})
             m = cls.from_pretrained(d, torch_dtype=torch.float32, attn_implementation="eager")
             m.eval()
             with torch.no_grad():

@@ -1,7 +1,7 @@
 """The f32 forward oracle against HF transformers (the reference's
-tools/oracle method) on the committed golden logits, plus its own
-invariants: causality and prefix consistency (a longer prompt does not change
-earlier positions' logits)."""
+tools/oracle method) on the committed golden logits (Llama, Qwen2, Qwen3),
+plus its own invariants: causality and prefix consistency (a longer prompt
+does not change earlier positions' logits)."""
 import os
 
 import numpy as np
@@ -15,7 +15,7 @@ def load():
     return {k: z[k] for k in z.files}
 
 
-def oracle_model(z, bias):
+def oracle_model(z, bias, qk_norm=False):
     import oracle
     from reng.config import LlamaConfig
     cfg = LlamaConfig(hidden_size=128, intermediate_size=256, num_hidden_layers=2,
@@ -26,17 +26,25 @@ def oracle_model(z, bias):
         lw = {k: z["l%d_%s" % (l, k)] for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2")}
         if bias:
             lw.update({k: z["l%d_%s" % (l, k)] for k in ("bq", "bk", "bv")})
+        if qk_norm:
+            lw.update({k: z["l%d_%s" % (l, k)] for k in ("qn", "kn")})
         layers.append(lw)
+    width = 64 if qk_norm else 0
     c = dict(hidden=128, inter=256, n_layers=2, n_heads=2, n_kv_heads=1, head_dim=64, vocab=256,
-             eps=1e-5, attn_scale=cfg.attention_scale(), has_bias=int(bias))
+             eps=1e-5, attn_scale=cfg.attention_scale(), has_bias=int(bias), qn_width=width,
+             kn_width=width)
     return cfg, oracle.Model(c, layers, z["final_gamma"], z["lm_head"], z["embed"])
 
 
-@pytest.mark.parametrize("arch,bias", [("llama", False), ("qwen2", True)])
-def test_oracle_matches_transformers(oracle_lib, arch, bias):
+@pytest.mark.parametrize("arch,bias,qk_norm", [("llama", False, False), ("qwen2", True, False),
+                                               ("qwen3", False, True)])
+def test_oracle_matches_transformers(oracle_lib, arch, bias, qk_norm):
+    """qwen3: per-head q/k RMSNorm before RoPE, the attention scale on the
+    q norm gain instead of wq (the reference's layer_cpu,
+    crates/reng-synapse/src/model.rs:2962-3006)."""
     from reng.rope import rope_caches_for
     z = load()
-    cfg, m = oracle_model(z, bias)
+    cfg, m = oracle_model(z, bias, qk_norm)
     sin, cos = rope_caches_for(cfg, 64)
     got = m.forward(z["ids"], sin, cos)
     want = z["logits_" + arch]

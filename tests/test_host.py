@@ -110,6 +110,38 @@ def test_config_json_round_trip_and_safetensors_loader(tmp_path):
         load_weights(str(tmp_path), cfg2)
 
 
+def test_qk_norm_gains_round_trip_and_are_refused_by_the_engine(tmp_path):
+    """q/k norm gains (Qwen3's [head_dim] form) survive save/load as the
+    reference reads them (crates/reng-model/src/lib.rs:1607-1609); an
+    engine given them refuses, whatever the model_type says, instead of
+    decoding without the norm."""
+    from reng.config import LlamaConfig
+    from reng.model import Engine
+    from reng.weights import load_weights, random_weights, save_checkpoint
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim_=16, vocab_size=96,
+                      rms_norm_eps=1e-6, rope_theta=1e6, model_type="qwen3")
+    w = random_weights(cfg, seed=6)
+    rng = np.random.default_rng(6)
+    for lw in w["layers"]:
+        lw["qn"] = rng.standard_normal(16).astype(np.float32)
+        lw["kn"] = rng.standard_normal(16).astype(np.float32)
+    save_checkpoint(str(tmp_path), cfg, w)
+    w2 = load_weights(str(tmp_path), LlamaConfig.load(str(tmp_path)))
+    for l in range(2):
+        for k in ("qn", "kn"):
+            assert np.array_equal(w2["layers"][l][k], w["layers"][l][k]), (l, k)
+    as_llama = LlamaConfig.from_dict(dict(cfg.to_dict(), model_type="llama"))
+    assert as_llama.unsupported(capacity=64) == []
+    with pytest.raises(ValueError, match="q/k RMSNorm"):
+        Engine(as_llama, w2, capacity=64)
+    # a plain Llama checkpoint loads without them
+    del w["layers"][0]["qn"], w["layers"][0]["kn"], w["layers"][1]["qn"], w["layers"][1]["kn"]
+    save_checkpoint(str(tmp_path / "plain"), as_llama, w)
+    w3 = load_weights(str(tmp_path / "plain"), as_llama)
+    assert all("qn" not in lw and "kn" not in lw for lw in w3["layers"])
+
+
 def test_fp8_switch_grammar():
     from reng.model import fp8_switch
     assert fp8_switch(None) is None
