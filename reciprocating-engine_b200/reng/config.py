@@ -3,8 +3,11 @@
 Mirrors crates/reng-model/src/lib.rs: `LlamaConfig` (lib.rs:84-193),
 `from_json` (lib.rs:488-618), `n_kv_heads` / `head_dim` / `rotary_dim` /
 `q_dim` / `attention_scale` (lib.rs:666-705) and `shard` (lib.rs:725-742),
-for the decoder families this path runs (Llama, Qwen2 with q/k/v biases).
-A multimodal Gemma-3 style config parses through its `text_config`.
+and the per-family rules of lib.rs:268-420 (windows, Gemma sliding layers
+and softcaps, embedding scale, post-norm).  The engine runs the Llama /
+Qwen2 / Mistral decoder and refuses the rest (`unsupported`); the loader and
+the f32 oracle take every family the reference's host forward does.  A
+multimodal Gemma-3 config parses through its `text_config`.
 """
 import copy
 import json
@@ -23,6 +26,11 @@ GEMMA3_TEXT_DEFAULTS = {
     "query_pre_attn_scalar": 256, "sliding_window": 4096, "sliding_window_pattern": 6,
     "rope_theta": 1000000.0, "rope_local_base_freq": 10000.0,
 }
+
+
+# Gemma text model types: zero-centred norm gains, sqrt(hidden) embedding
+# scale, GELU-tanh, per-layer sliding windows, tied head by default
+GEMMA_TYPES = ("gemma2", "gemma3_text")
 
 
 @dataclass
@@ -62,6 +70,7 @@ class LlamaConfig:
     max_position_embeddings: Optional[int] = None
     hidden_act: str = "silu"
     rope_local_base_freq: Optional[float] = None
+    weight_prefix: Optional[str] = None
     raw: dict = field(default_factory=dict, repr=False)
 
     # ----------------------------------------------------------- parsing --
@@ -78,6 +87,9 @@ class LlamaConfig:
             t = dict(GEMMA3_TEXT_DEFAULTS)
             t.update(d["text_config"])
             d = t
+            prefix = "language_model.model."
+        else:
+            prefix = None
         rp = d.get("rope_parameters")
         rope_theta = d.get("rope_theta")
         rs = d.get("rope_scaling")
@@ -117,11 +129,11 @@ class LlamaConfig:
             rms_norm_eps=float(d.get("rms_norm_eps", 1e-6)),
             rope_theta=float(rope_theta if rope_theta is not None else 10000.0),
             rope_scaling=scaling, partial_rotary_factor=d.get("partial_rotary_factor"),
-            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", mt in GEMMA_TYPES)),
             attention_bias=bool(d.get("attention_bias", mt == "qwen2")),
             model_type=mt, max_position_embeddings=d.get("max_position_embeddings"),
-            hidden_act=d.get("hidden_act", d.get("hidden_activation", "silu")),
-            rope_local_base_freq=d.get("rope_local_base_freq"), raw=d)
+            hidden_act=d.get("hidden_activation") or d.get("hidden_act") or "silu",
+            rope_local_base_freq=d.get("rope_local_base_freq"), weight_prefix=prefix, raw=d)
         if cfg.partial_rotary_factor is not None:
             f, rd = float(cfg.partial_rotary_factor), cfg.rotary_dim()
             if not (0.0 < f <= 1.0) or rd == 0 or rd % 2:
@@ -132,6 +144,89 @@ class LlamaConfig:
     @staticmethod
     def from_json(text):
         return LlamaConfig.from_dict(json.loads(text))
+
+    # ------------------------------------------------------ family rules --
+    # crates/reng-model/src/lib.rs:268-420 and :697-712, read from the
+    # config.json keys this dataclass keeps in `raw`.
+    def _opt(self, key):
+        v = (self.raw or {}).get(key)
+        return None if v is None else v
+
+    def is_gemma(self):
+        """gemma2 / gemma3_text (lib.rs:290-292)."""
+        return self.model_type in GEMMA_TYPES
+
+    def post_norm(self):
+        """OLMo-2 normalises the branch outputs, not the inputs (lib.rs:707-712)."""
+        return self.model_type == "olmo2"
+
+    def tied(self):
+        return bool(self.tie_word_embeddings)
+
+    def embed_scale(self):
+        """Factor on the gathered embedding rows, f32 (lib.rs:303-312):
+        Gemma's sqrt(hidden) times Granite's embedding_multiplier."""
+        import numpy as np
+        g = np.sqrt(np.float32(self.hidden_size)) if self.is_gemma() else np.float32(1.0)
+        m = self._opt("embedding_multiplier")
+        return float(np.float32(g) * np.float32(1.0 if m is None else m))
+
+    def activation(self):
+        """"silu" or "gelu_tanh"; anything else is an error (lib.rs:319-331)."""
+        name = self.hidden_act or "silu"
+        if name == "silu":
+            return "silu"
+        if name == "gelu_pytorch_tanh":
+            return "gelu_tanh"
+        raise ValueError("config.json: activation %s is not supported" % name)
+
+    def window(self):
+        """The model-wide sliding window (lib.rs:275-287): Phi-3 and Mistral
+        always, Qwen2/Qwen3 only with use_sliding_window true."""
+        w = self._opt("sliding_window")
+        w = int(w) if w else None
+        if self.model_type in ("phi3", "mistral"):
+            return w
+        if self.model_type in ("qwen2", "qwen3") and self._opt("use_sliding_window") is True:
+            return w
+        return None
+
+    def sliding(self, li):
+        """Whether Gemma layer li is a sliding-attention layer (lib.rs:337-350)."""
+        if not self.is_gemma():
+            return False
+        types = self._opt("layer_types")
+        if types is not None:
+            return li < len(types) and types[li] == "sliding_attention"
+        pattern = 2 if self.model_type == "gemma2" else int(self._opt("sliding_window_pattern") or 6)
+        return (li + 1) % pattern != 0
+
+    def layer_window(self, li):
+        """Layer li's window (lib.rs:356-366)."""
+        if not self.is_gemma():
+            return self.window()
+        if not self.sliding(li):
+            return None
+        w = self._opt("sliding_window")
+        return int(w) if w else None
+
+    def attn_softcap(self):
+        """Gemma-2's attn_logit_softcapping (lib.rs:370-377)."""
+        c = self._opt("attn_logit_softcapping")
+        return float(c) if self.model_type == "gemma2" and c is not None and c > 0 else None
+
+    def final_softcap(self):
+        c = self._opt("final_logit_softcapping")
+        return float(c) if c is not None and c > 0 else None
+
+    def local_rope(self, li):
+        """Gemma-3 sliding layers read the local RoPE table (lib.rs:387-390)."""
+        return self.model_type == "gemma3_text" and self.sliding(li)
+
+    def use_rope(self, li):
+        """False on SmolLM3's NoPE layers (no_rope_layers[li] == 0)."""
+        v = self._opt("no_rope_layers")
+        return v is None or li >= len(v) or v[li] != 0
 
     # ------------------------------------------------------ engine support --
     ENGINE_TYPES = (None, "llama", "qwen2", "mistral")
@@ -159,9 +254,11 @@ class LlamaConfig:
                 out.append(k)
         if raw.get("qk_norm") or raw.get("use_qk_norm"):
             out.append("q/k RMSNorm")
-        win = raw.get("sliding_window")
-        if win and raw.get("use_sliding_window", True) and capacity is not None and capacity > int(win):
-            out.append("sliding window %d below the capacity %d" % (int(win), capacity))
+        if any(not self.use_rope(li) for li in range(self.num_hidden_layers)):
+            out.append("NoPE layers")
+        win = self.window()
+        if win and capacity is not None and capacity > win:
+            out.append("sliding window %d below the capacity %d" % (win, capacity))
         return out
 
     @staticmethod
@@ -201,9 +298,16 @@ class LlamaConfig:
         return self.num_attention_heads * self.head_dim()
 
     def attention_scale(self):
-        """1/sqrt(head_dim) (lib.rs:701-705), as an f32."""
+        """The softmax scale on q.k, as an f32 (lib.rs:697-705): Granite's
+        attention_multiplier, else Gemma's 1/sqrt(query_pre_attn_scalar),
+        else 1/sqrt(head_dim)."""
         import numpy as np
-        return float(np.float32(1.0) / np.sqrt(np.float32(self.head_dim())))
+        m = self._opt("attention_multiplier")
+        if m is not None:
+            return float(np.float32(m))
+        s = self._opt("query_pre_attn_scalar")
+        base = np.float32(s) if s is not None else np.float32(self.head_dim())
+        return float(np.float32(1.0) / np.sqrt(base))
 
     def has_bias(self):
         return bool(self.attention_bias)

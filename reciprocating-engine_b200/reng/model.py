@@ -57,10 +57,19 @@ class Engine:
     def __init__(self, cfg, w, batch=1, capacity=1024, device=0, tp_rank=0, tp_world=1,
                  nccl_id=None, fp8=None):
         missing = cfg.unsupported(capacity)
-        if any(lw.get(k) is not None for lw in w.get("layers", ()) for k in ("qn", "kn")):
+        layers = w.get("layers", ())
+        if any(lw.get(k) is not None for lw in layers for k in ("qn", "kn")):
             missing = missing + ["q/k RMSNorm gains"]
+        if any(lw.get(k) is not None for lw in layers for k in ("g_post_attn", "g_post_mlp")):
+            missing = missing + ["branch-output norms"]
         if missing:
             raise ValueError("this engine does not run %s" % ", ".join(missing))
+        # q/k/v biases where the checkpoint has them, as the reference's
+        # optional biases (crates/reng-model/src/lib.rs:1604-1606, 1628)
+        has = [[lw.get(k) is not None for k in ("bq", "bk", "bv")] for lw in layers]
+        if any(any(b) != all(b) for b in has) or len({all(b) for b in has}) > 1:
+            raise ValueError("q/k/v biases must be all present or all absent in every layer")
+        with_bias = bool(has) and all(has[0])
         self.cfg = cfg
         self.batch = batch
         self.capacity = capacity
@@ -100,7 +109,7 @@ class Engine:
         desc.vocab = cfg.vocab_size
         desc.eps = cfg.rms_norm_eps
         desc.attn_scale = cfg.attention_scale()
-        desc.has_qkv_bias = 1 if cfg.has_bias() else 0
+        desc.has_qkv_bias = 1 if with_bias else 0
         desc.weights = _lib.RENG_WEIGHTS_BF16 if fp8 is None else _lib.RENG_WEIGHTS_FP8_E4M3
         desc.batch = batch
         desc.capacity = capacity

@@ -138,3 +138,13 @@ def rope_caches_for(cfg, positions, seq_len=None):
     """The global table pair of a config for `positions` rows (lib.rs:394-420)."""
     return rope_caches_partial(positions, cfg.head_dim(), cfg.rotary_dim(), cfg.rope_theta,
                                cfg.rope_scaling, positions if seq_len is None else seq_len)
+
+
+def rope_local_caches_for(cfg, positions):
+    """The local table pair (Gemma-3 sliding layers): rope_local_base_freq,
+    default 1e4, without rope_scaling (lib.rs:411-420); None when no layer
+    reads it."""
+    if not any(cfg.local_rope(li) for li in range(cfg.num_hidden_layers)):
+        return None
+    theta = cfg.rope_local_base_freq if cfg.rope_local_base_freq is not None else 1e4
+    return rope_caches_partial(positions, cfg.head_dim(), cfg.rotary_dim(), theta, None, positions)

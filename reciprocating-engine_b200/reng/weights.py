@@ -3,13 +3,15 @@
 `load_weights(dir)` mirrors crates/reng-model/src/lib.rs:1477-1688: it maps
 `model.safetensors` (or the shards of `model.safetensors.index.json`) and
 returns bf16 views without copying (the reference's `Bf16Slice`,
-lib.rs:755-999), with q/k/v biases when present (lib.rs:1605-1630) and the
-embedding as the LM head when the embeddings are tied (lib.rs:1666-1674).
-Tensor names are the HF Llama / Qwen2 ones.
+lib.rs:755-999) where no family rule rewrites a tensor, with q/k/v biases
+and q/k norm gains when present (lib.rs:1605-1630) and the embedding as the
+LM head when the embeddings are tied (lib.rs:1666-1674).  Tensor names are
+the HF ones of the families the reference loads.
 
 A weights object is a dict:
   {"layers": [{"wq","wk","wv","wo","wg","wu","wd": bf16 bits [out, in] (u16),
-               "g1","g2": f32 [hidden], "bq","bk","bv": f32 or absent}],
+               "g1","g2": f32 [hidden], "bq","bk","bv": f32 or absent,
+               "qn","kn","g_post_attn","g_post_mlp": f32 or absent}],
    "embed": u16 [vocab, hidden], "lm_head": u16 [vocab, hidden],
    "final_gamma": f32 [hidden]}
 with numpy arrays (host) or torch tensors on a CUDA device (device memory).
@@ -102,20 +104,48 @@ def _as_f32(st, name):
     return v.astype(np.float32)
 
 
-def load_weights(model_dir, cfg):
-    """Map the checkpoint of `model_dir` (reng-model load_weights)."""
+def scale_bf16(w, s):
+    """bf16(f32(w) * s), round to nearest even (the reference's scale_bf16,
+    crates/reng-synapse/src/lib.rs:61-69): a scaled copy of bf16 bits."""
+    return f32_to_bf16_bits(bf16_bits_to_f32(np.asarray(w)) * np.float32(s))
+
+
+def permute_head_rows(m, hd, perm):
+    """Rows of every hd-row head block reordered: row e of a block is the
+    block's row perm[e] (lib.rs:2253-2275); works for matrices and vectors."""
+    m = np.asarray(m)
+    blocks = m.reshape((m.shape[0] // hd, hd) + m.shape[1:])
+    return np.ascontiguousarray(blocks[:, perm].reshape(m.shape))
+
+
+def _open(model_dir):
     idx = os.path.join(model_dir, "model.safetensors.index.json")
-    files = {}
     if os.path.exists(idx):
         with open(idx) as f:
             wm = json.load(f)["weight_map"]
-        for name, fn in wm.items():
-            files.setdefault(fn, None)
-        sts = {fn: SafeTensors(os.path.join(model_dir, fn)) for fn in files}
-        where = {name: sts[fn] for name, fn in wm.items()}
-    else:
-        st = SafeTensors(os.path.join(model_dir, "model.safetensors"))
-        where = {n: st for n in st.names()}
+        sts = {fn: SafeTensors(os.path.join(model_dir, fn)) for fn in set(wm.values())}
+        return {name: sts[fn] for name, fn in wm.items()}
+    st = SafeTensors(os.path.join(model_dir, "model.safetensors"))
+    return {n: st for n in st.names()}
+
+
+def load_weights(model_dir, cfg):
+    """Map the checkpoint of `model_dir` (reng-model load_weights,
+    crates/reng-model/src/lib.rs:1477-1688).  Per family, as the reference:
+    Phi-3's fused qkv_proj / gate_up_proj split into row blocks; Gemma's
+    zero-centred gains applied as 1 + w, its four norms (pre-norms g1 / g2,
+    branch-output norms g_post_attn / g_post_mlp) and a final norm carrying
+    1 / final softcap; OLMo-2's branch-output norms as g1 / g2; optional
+    q/k/v biases and q/k norm gains; a partial rotation's q/k head dims put
+    in the kernel's pair order (rope_head_perm); Granite's residual
+    multiplier folded into o_proj / down_proj and 1 / logits_scaling into
+    the LM head's own copy (scale_bf16).  The embedding stays as stored
+    (its scale is applied at the gather)."""
+    from .rope import rope_head_perm
+    raw = cfg.raw or {}
+    if raw.get("mlp_bias"):
+        raise ValueError("mlp_bias is not supported")
+    where = _open(model_dir)
 
     def get(name, kind, shape):
         if name not in where:
@@ -126,35 +156,92 @@ def load_weights(model_dir, cfg):
         return _as_bf16(st, name) if kind == "bf16" else _as_f32(st, name)
 
     h, hd = cfg.hidden_size, cfg.head_dim()
-    qd, kvd, inter = cfg.q_dim(), cfg.n_kv_heads() * hd, cfg.intermediate_size
-    shapes = {"wq": (qd, h), "wk": (kvd, h), "wv": (kvd, h), "wo": (h, qd), "wg": (inter, h),
-              "wu": (inter, h), "wd": (h, inter), "g1": (h,), "g2": (h,), "bq": (qd,),
-              "bk": (kvd,), "bv": (kvd,)}
+    qd, kvd, inter, V = cfg.q_dim(), cfg.n_kv_heads() * hd, cfg.intermediate_size, cfg.vocab_size
+    pre = cfg.weight_prefix or "model."
+    gemma, post = cfg.is_gemma(), cfg.post_norm()
+
+    def plus_one(v):
+        return (v + np.float32(1.0)).astype(np.float32) if gemma else v
+
+    perm = rope_head_perm(hd, cfg.rotary_dim()) if cfg.rotary_dim() < hd else None
+    rmul = raw.get("residual_multiplier")
+    embed = get(pre + "embed_tokens.weight", "bf16", (V, h))
     layers = []
     for l in range(cfg.num_hidden_layers):
+        p = "%slayers.%d." % (pre, l)
+
+        def opt(name, lens):
+            n = p + name
+            if n not in where:
+                return None
+            shp = where[n].shape(n)
+            if len(shp) != 1 or shp[0] not in lens:
+                raise ValueError("%s: shape %s, expected one of %s" % (n, shp, lens))
+            return _as_f32(where[n], n)
+
         lw = {}
-        for k in MATS:
-            lw[k] = get("model.layers.%d.%s" % (l, NAMES[k]), "bf16", shapes[k])
-        for k in ("g1", "g2"):
-            lw[k] = get("model.layers.%d.%s" % (l, NAMES[k]), "f32", shapes[k])
-        if cfg.has_bias():
-            for k in ("bq", "bk", "bv"):
-                lw[k] = get("model.layers.%d.%s" % (l, NAMES[k]), "f32", shapes[k])
-        for k, full in (("qn", qd), ("kn", kvd)):
-            # optional q/k norm gains: [head_dim] per head (Qwen3) or the whole
-            # projection row (OLMo-2), as reng-model reads them
-            # (crates/reng-model/src/lib.rs:1607-1609)
-            name = "model.layers.%d.%s" % (l, NAMES[k])
-            if name in where:
-                n = where[name].shape(name)
-                lw[k] = get(name, "f32", (hd,) if tuple(n) == (hd,) else (full,))
+        if p + "self_attn.qkv_proj.weight" in where:
+            qkv = get(p + "self_attn.qkv_proj.weight", "bf16", (qd + 2 * kvd, h))
+            lw["wq"], lw["wk"], lw["wv"] = qkv[:qd], qkv[qd:qd + kvd], qkv[qd + kvd:]
+        else:
+            lw["wq"] = get(p + NAMES["wq"], "bf16", (qd, h))
+            lw["wk"] = get(p + NAMES["wk"], "bf16", (kvd, h))
+            lw["wv"] = get(p + NAMES["wv"], "bf16", (kvd, h))
+        if p + "mlp.gate_up_proj.weight" in where:
+            gu = get(p + "mlp.gate_up_proj.weight", "bf16", (2 * inter, h))
+            lw["wg"], lw["wu"] = gu[:inter], gu[inter:]
+        else:
+            lw["wg"] = get(p + NAMES["wg"], "bf16", (inter, h))
+            lw["wu"] = get(p + NAMES["wu"], "bf16", (inter, h))
+        lw["wo"] = get(p + NAMES["wo"], "bf16", (h, qd))
+        lw["wd"] = get(p + NAMES["wd"], "bf16", (h, inter))
+        if rmul is not None:
+            lw["wo"], lw["wd"] = scale_bf16(lw["wo"], rmul), scale_bf16(lw["wd"], rmul)
+
+        def g(name):
+            return plus_one(get(p + name, "f32", (h,)))
+
+        if gemma:
+            lw["g1"], lw["g2"] = g("input_layernorm.weight"), g("pre_feedforward_layernorm.weight")
+            lw["g_post_attn"] = g("post_attention_layernorm.weight")
+            lw["g_post_mlp"] = g("post_feedforward_layernorm.weight")
+        elif post:
+            lw["g1"] = g("post_attention_layernorm.weight")
+            lw["g2"] = g("post_feedforward_layernorm.weight")
+        else:
+            lw["g1"], lw["g2"] = g("input_layernorm.weight"), g("post_attention_layernorm.weight")
+        for k, lens in (("bq", (qd,)), ("bk", (kvd,)), ("bv", (kvd,))):
+            v = opt(NAMES[k], lens)
+            if v is not None:
+                lw[k] = v
+        for k, lens in (("qn", (hd, qd)), ("kn", (hd, kvd))):
+            # per head (Qwen3, Gemma-3) or over the whole projection (OLMo-2),
+            # lib.rs:1607-1609
+            v = opt(NAMES[k], lens)
+            if v is not None:
+                lw[k] = plus_one(v)
+        if perm is not None:
+            for k in ("wq", "wk", "bq", "bk", "qn", "kn"):
+                if k in lw:
+                    lw[k] = permute_head_rows(lw[k], hd, perm)
         layers.append(lw)
-    embed = get("model.embed_tokens.weight", "bf16", (cfg.vocab_size, h))
-    if cfg.tie_word_embeddings or "lm_head.weight" not in where:
+    fg = plus_one(get(pre + "norm.weight", "f32", (h,)))
+    cap = cfg.final_softcap()
+    if cap is not None:
+        # Gemma-2: tanh(logits / cap) * cap, the division on the final gain
+        fg = (fg / np.float32(cap)).astype(np.float32)
+    outer = pre[:-len("model.")] if pre.endswith("model.") else ""
+    heads = [outer + "lm_head.weight"] + (["lm_head.weight"] if outer else [])
+    head = next((n for n in heads if n in where), None)
+    if head is not None:
+        lm = get(head, "bf16", (V, h))
+    elif cfg.tied():
         lm = embed
     else:
-        lm = get("lm_head.weight", "bf16", (cfg.vocab_size, h))
-    fg = get("model.norm.weight", "f32", (h,))
+        raise ValueError("lm_head.weight missing and embeddings are not tied")
+    ls = raw.get("logits_scaling")
+    if ls is not None:
+        lm = scale_bf16(lm, np.float32(1.0) / np.float32(ls))
     return {"layers": layers, "embed": embed, "lm_head": lm, "final_gamma": fg}
 
 
