@@ -29,6 +29,23 @@ int fail(int code, const std::string& msg);
         if (!(cond)) return ::reng::fail(RENG_E_INVAL, (msg));                      \
     } while (0)
 
+// Up to four CUDA events, destroyed on every return path of the host call
+// that made them.
+struct EventSet {
+    cudaEvent_t e[4] = {};
+    int n = 0;
+    cudaError_t create(int k) {
+        for (; n < k && n < 4; n++) {
+            cudaError_t r = cudaEventCreate(&e[n]);
+            if (r != cudaSuccess) return r;
+        }
+        return cudaSuccess;
+    }
+    ~EventSet() {
+        for (int i = 0; i < n; i++) cudaEventDestroy(e[i]);
+    }
+};
+
 // ------------------------------------------------------------ bf16 bits --
 __host__ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) {
 #ifdef __CUDA_ARCH__

@@ -619,7 +619,13 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
         pos = a.pos[a.slot] + m;
         id = a.prefill_ids[m];
     }
-    if (id >= (uint32_t)a.vocab) id = 0;  // the host refuses such ids; never read out of range
+    if (id >= (uint32_t)a.vocab) {
+        // host ids are checked before the launch; a device id (the caller's
+        // seeds of decode_device) is reported through the error word, and
+        // the gather never reads out of range
+        if (threadIdx.x == 0) atomicCAS(a.err, 0, RENG_E_INVAL);
+        id = 0;
+    }
     if (threadIdx.x == 0) {
         a.row_slot[m] = slot;
         a.row_pos[m] = pos;

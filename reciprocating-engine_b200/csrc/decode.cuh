@@ -139,6 +139,7 @@ struct EmbedArgs {
     const uint32_t* prefill_ids;
     int slot;
     int batch;
+    int* err;               // an id outside the vocabulary records RENG_E_INVAL here
 };
 
 struct Pack8Args {

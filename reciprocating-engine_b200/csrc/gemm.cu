@@ -856,9 +856,9 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
     GEMM_CU(cudaDeviceSynchronize());
     if (iters > 0) {
-        cudaEvent_t e0, e1;
-        GEMM_CU(cudaEventCreate(&e0));
-        GEMM_CU(cudaEventCreate(&e1));
+        EventSet evs;
+        GEMM_CU(evs.create(2));
+        cudaEvent_t e0 = evs.e[0], e1 = evs.e[1];
         GEMM_CU(cudaEventRecord(e0, 0));
         for (int i = 0; i < iters; i++) GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
         GEMM_CU(cudaEventRecord(e1, 0));
@@ -866,8 +866,6 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
         float ms = 0.f;
         cudaEventElapsedTime(&ms, e0, e1);
         *ms_out = ms / (float)iters;
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
     }
     int herr = 0;
     GEMM_CU(cudaMemcpy(&herr, err, 4, cudaMemcpyDeviceToHost));

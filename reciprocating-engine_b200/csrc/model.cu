@@ -293,6 +293,7 @@ EmbedArgs embed_args(reng_model* m, int mode, int M, int slot) {
     e.prefill_ids = m->prefill_ids;
     e.slot = slot;
     e.batch = m->B;
+    e.err = m->err;
     return e;
 }
 
@@ -959,7 +960,9 @@ int check_device_error(reng_model* m) {
             CU(cudaMemsetAsync(m->step_ctl.bar, 0, 8, m->st));
             CU(cudaStreamSynchronize(m->st));
         }
-        return fail(code, "a kernel of the step gave up on a bounded wait; the results are invalid");
+        return fail(code, code == RENG_E_INVAL
+                              ? "a token id on the device was outside the vocabulary; the results are invalid"
+                              : "a kernel of the step gave up on a bounded wait; the results are invalid");
     }
     return RENG_OK;
 }
@@ -1078,8 +1081,9 @@ extern "C" int reng_model_decode(reng_model* m, const uint32_t* seeds, int n, ui
         RENG_CHECK_ARG(seeds[b] < (uint32_t)m->vocab, "reng_model_decode: seed id out of range");
     }
     CU(cudaSetDevice(m->dev));
-    cudaEvent_t ev[4];
-    for (auto& e : ev) CU(cudaEventCreate(&e));
+    EventSet evs;
+    CU(evs.create(4));
+    cudaEvent_t* ev = evs.e;
     CU(cudaEventRecord(ev[0], m->st));
     memcpy(m->pinned, seeds, (size_t)m->B * 4);
     CU(cudaMemcpyAsync(m->ids_ring, m->pinned, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->st));
@@ -1095,7 +1099,6 @@ extern "C" int reng_model_decode(reng_model* m, const uint32_t* seeds, int n, ui
     cudaEventElapsedTime(&m->times.readback_ms, ev[2], ev[3]);
     m->times.steps = n;
     m->times.kernels_per_step = m->kernels_per_step;
-    for (auto& e : ev) cudaEventDestroy(e);
     for (int b = 0; b < m->B; b++) m->host_pos[b] += n;
     return check_device_error(m);
 }
@@ -1166,9 +1169,9 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
     CU(cudaSetDevice(m->dev));
     CU(cudaStreamSynchronize(m->st));
     const int M = m->B;
-    cudaEvent_t e0, e1;
-    CU(cudaEventCreate(&e0));
-    CU(cudaEventCreate(&e1));
+    EventSet evs;
+    CU(evs.create(2));
+    cudaEvent_t e0 = evs.e[0], e1 = evs.e[1];
     // rows as the decode step sees them
     TRY(k_embed_launch(m, 0, M, 0, m->st));
     for (int kind = 0; kind < RENG_KERNEL_KINDS; kind++) {
@@ -1194,8 +1197,6 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
         CU(cudaEventElapsedTime(&ms, e0, e1));
         ms_out[kind] = ms / (float)iters;
     }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
     TRY(check_device_error(m));
     // the QKV launches rewrote the cache row at each slot's last position
     // with other activations: the cached prefix is no longer valid

@@ -300,7 +300,10 @@ __device__ void embed_phase(const EmbedArgs& e) {
         if (live) {
             const int pos = e.pos[m];
             uint32_t id = e.ids_ring[(size_t)step * e.batch + m];
-            if (id >= (uint32_t)e.vocab) id = 0;
+            if (id >= (uint32_t)e.vocab) {  // reported, never read out of range
+                if (i == 0) atomicCAS(e.err, 0, RENG_E_INVAL);
+                id = 0;
+            }
             if (i == 0) {
                 e.row_slot[m] = m;
                 e.row_pos[m] = pos;
