@@ -139,7 +139,60 @@ class LlamaConfig:
             if not (0.0 < f <= 1.0) or rd == 0 or rd % 2:
                 raise ValueError("config.json: partial_rotary_factor %r rotates %d of %d head dims"
                                  % (f, rd, cfg.head_dim()))
+        cfg._check_scaling()
+        cfg.activation()
         return cfg
+
+    def _check_scaling(self):
+        """Every parameter the rope type's table needs, and longrope's one
+        factor per rotary pair, refused at load as the reference does
+        (lib.rs:553-612, after transformers' validate_rope)."""
+        s = self.rope_scaling
+        if s is None:
+            return
+        t = s.rope_type or "default"
+
+        def need(name, have):
+            if not have:
+                raise ValueError("config.json: rope_scaling.%s is required by rope_type %s" % (name, t))
+
+        factor = s.factor is not None or (s.max_position_embeddings is not None and
+                                          s.original_max_position_embeddings is not None)
+        orig = s.original_max_position_embeddings is not None
+        if t == "llama3":
+            need("factor", s.factor is not None)
+            need("low_freq_factor", s.low_freq_factor is not None)
+            need("high_freq_factor", s.high_freq_factor is not None)
+            need("original_max_position_embeddings", orig)
+        elif t == "linear":
+            need("factor", s.factor is not None)
+        elif t == "yarn":
+            need("factor", factor)
+            need("original_max_position_embeddings", orig)
+        elif t == "longrope":
+            need("factor", factor)
+            need("original_max_position_embeddings", orig)
+            need("short_factor", s.short_factor is not None)
+            need("long_factor", s.long_factor is not None)
+            half = self.rotary_dim() // 2
+            for name, lst in (("short_factor", s.short_factor), ("long_factor", s.long_factor)):
+                if len(lst) != half:
+                    raise ValueError("config.json: rope_scaling.%s has %d entries for %d rotary pairs"
+                                     % (name, len(lst), half))
+
+    def longrope_capacity_warning(self, capacity):
+        """The warning a cached run deserves when its capacity, past the
+        pretraining length, makes every position read longrope's long
+        factors (lib.rs:445-458); None otherwise."""
+        s = self.rope_scaling
+        if s is None or s.rope_type != "longrope" or s.original_max_position_embeddings is None:
+            return None
+        orig = int(s.original_max_position_embeddings)
+        if capacity <= orig:
+            return None
+        return ("rope_scaling: cache capacity %d is past the pretraining length %d, so the longrope "
+                "long factors serve every position; size the cache to the run's length to match "
+                "transformers" % (capacity, orig))
 
     @staticmethod
     def from_json(text):
