@@ -198,3 +198,71 @@ def test_engine_refuses_what_its_kernels_do_not_compute():
             Engine(cfg, {"embed": np.zeros((1, 1), np.uint16)}, capacity=4096)
     # a sliding window at or above the capacity attends exactly as full attention
     assert LlamaConfig.from_dict(dict(base, model_type="mistral", sliding_window=4096)).unsupported(4096) == []
+
+
+def _raw_safetensors(path, parts):
+    """A safetensors file of (name, dtype, shape, bytes) packed back to back
+    with no padding between tensors, so a one-byte U8 tensor puts the next
+    one on an odd offset (as in large real checkpoints)."""
+    import json as _json
+    import struct as _struct
+    header, data = {}, b""
+    for name, dt, shape, raw in parts:
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [len(data), len(data) + len(raw)]}
+        data += raw
+    hb = _json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(_struct.pack("<Q", len(hb)) + hb + data)
+
+
+def test_mapped_views_odd_offsets_and_conversions(tmp_path):
+    """The reference's loader test (crates/reng-model/src/lib.rs:4163-4215):
+    an aligned bf16 tensor is a view of the mapped file (no copy), one on an
+    odd byte offset still reads its own values, f32 tensors convert to bf16
+    (round to nearest even) and bf16 reads back as f32."""
+    from reng.synth import f32_to_bf16_bits
+    from reng.weights import SafeTensors, _as_bf16, _as_f32
+    a = f32_to_bf16_bits(np.arange(6, dtype=np.float32) * 0.5).reshape(2, 3)
+    c = f32_to_bf16_bits(np.array([-1.0, 2.0], np.float32))
+    d = np.array([0.25, -8.0], np.float32)
+    p = str(tmp_path / "model.safetensors")
+    _raw_safetensors(p, [("a", "BF16", (2, 3), a.tobytes()), ("b", "U8", (1,), b"\x07"),
+                         ("c", "BF16", (2,), c.tobytes()), ("d", "F32", (2,), d.tobytes())])
+    st = SafeTensors(p)
+    va = _as_bf16(st, "a")
+    assert va.shape == (2, 3) and np.array_equal(va, a)
+    assert not va.flags.owndata                       # a view of the map, not a copy
+    vc = _as_bf16(st, "c")
+    assert (st._base + st.header["c"]["data_offsets"][0]) % 2 == 1
+    assert np.array_equal(vc, c)
+    assert np.array_equal(_as_bf16(st, "d"), f32_to_bf16_bits(d))
+    assert np.array_equal(_as_f32(st, "d"), d) and _as_f32(st, "a")[1, 0] == 1.5
+
+
+def test_loader_reads_a_checkpoint_with_odd_offsets(tmp_path):
+    """Every tensor of a small Llama checkpoint on an odd byte: the loaded
+    weights equal the aligned checkpoint's."""
+    from reng.config import LlamaConfig
+    from reng.weights import load_weights, random_weights, save_checkpoint
+    cfg = LlamaConfig(hidden_size=32, intermediate_size=64, num_hidden_layers=1,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim_=16, vocab_size=40,
+                      model_type="llama")
+    w = random_weights(cfg, seed=9)
+    save_checkpoint(str(tmp_path / "a"), cfg, w)
+    ref = load_weights(str(tmp_path / "a"), cfg)
+    from reng.weights import SafeTensors
+    st = SafeTensors(str(tmp_path / "a" / "model.safetensors"))
+    parts = []
+    for name in st.names():
+        parts.append(("pad." + name, "U8", (1,), b"\x00"))
+        v = st.view(name)
+        parts.append((name, st.dtype(name), v.shape, np.ascontiguousarray(v).tobytes()))
+    (tmp_path / "b").mkdir()
+    _raw_safetensors(str(tmp_path / "b" / "model.safetensors"), parts)
+    import shutil
+    shutil.copy(str(tmp_path / "a" / "config.json"), str(tmp_path / "b" / "config.json"))
+    odd = load_weights(str(tmp_path / "b"), cfg)
+    for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2"):
+        assert np.array_equal(odd["layers"][0][k], ref["layers"][0][k]), k
+    assert np.array_equal(odd["embed"], ref["embed"]) and np.array_equal(odd["lm_head"], ref["lm_head"])
