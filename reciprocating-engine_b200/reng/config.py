@@ -198,6 +198,31 @@ class LlamaConfig:
     def from_json(text):
         return LlamaConfig.from_dict(json.loads(text))
 
+    # ----------------------------------------------------------- context --
+    def trained_context(self):
+        """max_position_embeddings when positive (lib.rs:627-629)."""
+        n = self.max_position_embeddings
+        return int(n) if n else None
+
+    def original_context(self):
+        """The pre-scaling context a rope_scaling states (lib.rs:636-641)."""
+        s = self.rope_scaling
+        n = None if s is None else s.original_max_position_embeddings
+        return int(n) if n else None
+
+    def context_warning(self, positions):
+        """A warning when `positions` runs past the trained context, else
+        None (lib.rs:646-663)."""
+        trained = self.trained_context()
+        if trained is None or positions <= trained:
+            return None
+        o = self.original_context()
+        scaled = (" (rope scaling stretches a %d-position model to %d)" % (o, trained)
+                  if o is not None and o < trained else "")
+        return ("warning: %d positions exceed this model's trained context of %d%s; the engine will "
+                "run it, but the rotary embeddings are extrapolating and the output past position %d "
+                "is not what the checkpoint was trained to produce" % (positions, trained, scaled, trained))
+
     # ------------------------------------------------------ family rules --
     # crates/reng-model/src/lib.rs:268-420 and :697-712, read from the
     # config.json keys this dataclass keeps in `raw`.

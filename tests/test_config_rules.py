@@ -3,7 +3,7 @@
 reng.rope with the same known answers: the RoPE scaling types, Phi-3's
 legacy names and partial rotation, load-time refusal of incomplete
 scalings, the longrope capacity warning, the multimodal Gemma-3 flattening,
-Granite's multipliers and the Gemma layer kinds."""
+Granite's multipliers, the Gemma layer kinds and the trained-context warning."""
 import json
 
 import numpy as np
@@ -242,3 +242,19 @@ def test_config_round_trips_through_json(tmp_path):
     h = LlamaConfig.from_json(json.dumps(g.to_dict()))
     assert [h.layer_window(i) for i in range(6)] == [g.layer_window(i) for i in range(6)]
     assert (h.attn_softcap(), h.attention_scale(), h.tied()) == (50.0, 0.0625, True)
+
+
+def test_trained_context_warns_only_past_it():
+    """lib.rs:4791-4807."""
+    c = cfg_of({"model_type": "llama", "hidden_size": 4096, "intermediate_size": 14336,
+                "num_hidden_layers": 32, "num_attention_heads": 32, "num_key_value_heads": 8,
+                "rms_norm_eps": 1e-5, "vocab_size": 128256, "max_position_embeddings": 131072,
+                "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                 "high_freq_factor": 4.0, "original_max_position_embeddings": 8192}})
+    assert c.trained_context() == 131072 and c.original_context() == 8192
+    assert c.context_warning(131072) is None
+    w = c.context_warning(131073)
+    assert "131072" in w and "rope scaling" in w
+    bare = cfg_of({"hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 1,
+                   "num_attention_heads": 4, "rms_norm_eps": 1e-5, "vocab_size": 16})
+    assert bare.trained_context() is None and bare.context_warning(1000000) is None
