@@ -258,3 +258,19 @@ def test_trained_context_warns_only_past_it():
     bare = cfg_of({"hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 1,
                    "num_attention_heads": 4, "rms_norm_eps": 1e-5, "vocab_size": 16})
     assert bare.trained_context() is None and bare.context_warning(1000000) is None
+
+
+def test_conversions_and_position_zero():
+    """lib.rs:4406-4436: small integers and powers of two survive bf16, f16
+    reads as the reference's conversion, position 0 is the identity rotation,
+    argmax_rows picks the first maximum of each row."""
+    from reng.model import argmax_rows
+    from reng.rope import rope_caches_partial
+    from reng.synth import bf16_bits_to_f32, f32_to_bf16_bits
+    v = np.array([0.0, 1.0, -2.0, 0.5, 256.0, -0.125], np.float32)
+    assert np.array_equal(bf16_bits_to_f32(f32_to_bf16_bits(v)), v)
+    h = np.array([0x3C00, 0xC000, 0x0000, 0x3555], np.uint16).view(np.float16).astype(np.float32)
+    assert h[0] == 1.0 and h[1] == -2.0 and h[2] == 0.0 and abs(h[3] - 0.33325) < 1e-4
+    sin, cos = rope_caches_partial(2, 4, 4, 10000.0)
+    assert np.all(sin[0] == 0.0) and np.all(cos[0] == 1.0) and np.any(sin[1] != 0.0)
+    assert argmax_rows(np.array([[0.1, 0.9, 0.3], [2.0, -1.0, 0.0]], np.float32)) == [1, 0]
