@@ -98,6 +98,130 @@ class Quantized:
     def scale_operand(self):
         return self.scales if self.scaling == Scaling.PerChannel else None
 
+    def dequantize(self):
+        """The matrix back in f32, [rows * cols] row-major: decode(code) *
+        scale, one f32 multiply per element (lib.rs:316-327)."""
+        codes = np.asarray(self.codes, np.uint8).reshape(self.rows, self.cols)
+        vals = decode_table(self.format)[codes]
+        return (vals * np.asarray(self.scales, np.float32)[:, None]).astype(np.float32).reshape(-1)
+
+    def dequantize_bf16(self):
+        """bf16 bits of dequantize(), one rounding per element (lib.rs:331-335)."""
+        from .synth import f32_to_bf16_bits
+        return f32_to_bf16_bits(self.dequantize())
+
+
+def _pow2(e):
+    """2^e as an exact f32 for e in -149..127 (lib.rs:229-236)."""
+    return np.float32(np.ldexp(np.float32(1.0), int(e)))
+
+
+_DECODE = {}
+
+
+def decode_table(fmt):
+    """f32 value of every code (decode, lib.rs:205-225): the finite values
+    exactly, the reserved top exponent field as an infinity (zero mantissa)
+    or a NaN."""
+    fmt = Fp8Format(fmt)
+    if fmt not in _DECODE:
+        mb, bias, eb = fmt.mantissa_bits, fmt.exponent_bias, fmt.exponent_bits
+        out = np.empty(256, np.float32)
+        for code in range(256):
+            sign = np.float32(-1.0 if code & 0x80 else 1.0)
+            mant = code & ((1 << mb) - 1)
+            ef = (code & 0x7F) >> mb
+            if ef == (1 << eb) - 1:
+                out[code] = sign * np.float32(np.inf) if mant == 0 else np.float32(np.nan)
+                continue
+            frac = np.float32(mant) / np.float32(1 << mb)
+            if ef == 0:
+                out[code] = sign * frac * _pow2(1 - bias)
+            else:
+                out[code] = sign * (np.float32(1.0) + frac) * _pow2(ef - bias)
+        out.setflags(write=False)
+        _DECODE[fmt] = out
+    return _DECODE[fmt]
+
+
+def decode(code, fmt):
+    """One code to f32 (lib.rs:205-225)."""
+    return float(decode_table(fmt)[int(code) & 0xFF])
+
+
+@dataclass
+class RowError:
+    """Mean and maximum of |w - dequant(w)| / |w| over one row's non-zero
+    weights (lib.rs:339-345)."""
+    mean_rel: float
+    max_rel: float
+
+
+def _row_error(w_row, codes_row, scale, fmt):
+    from .synth import bf16_bits_to_f32
+    want = bf16_bits_to_f32(np.asarray(w_row, np.uint16))
+    nz = want != 0.0
+    if not nz.any():
+        return RowError(0.0, 0.0)
+    got = decode_table(fmt)[np.asarray(codes_row, np.uint8)[nz]] * np.float32(scale)
+    rel = np.abs((got - want[nz]) / want[nz]).astype(np.float32)
+    # the reference sums in order in f64: a running sum, not a pairwise one
+    total = np.cumsum(rel.astype(np.float64))[-1]
+    # the scan's f32::max starts at 0 and never takes a NaN
+    seen = rel[~np.isnan(rel)]
+    mx = seen.max() if seen.size else np.float32(0.0)
+    return RowError(float(np.float32(total / rel.size)), float(np.float32(mx)))
+
+
+def row_errors(w, q):
+    """Per-row relative error of `q` against the bf16 bits `w` it came from
+    (row_errors, lib.rs:347-386); an all-zero row reports 0.0 for both."""
+    w = np.asarray(w, np.uint16).reshape(-1)
+    if w.size != q.rows * q.cols:
+        raise ValueError("weight length against the shape")
+    codes = np.asarray(q.codes, np.uint8).reshape(q.rows, q.cols)
+    w = w.reshape(q.rows, q.cols)
+    return [_row_error(w[r], codes[r], q.scales[r], q.format) for r in range(q.rows)]
+
+
+def sample_row_errors(w, q, max_rows):
+    """row_errors over at most `max_rows` evenly spaced rows, every
+    ceil(rows / n)-th from row 0 (sample_row_errors, lib.rs:388-430)."""
+    w = np.asarray(w, np.uint16).reshape(-1)
+    if w.size != q.rows * q.cols:
+        raise ValueError("weight length against the shape")
+    if max_rows <= 0:
+        raise ValueError("max_rows must be positive")
+    n = min(max_rows, q.rows)
+    step = -(-q.rows // n)
+    codes = np.asarray(q.codes, np.uint8).reshape(q.rows, q.cols)
+    w = w.reshape(q.rows, q.cols)
+    return [_row_error(w[r], codes[r], q.scales[r], q.format) for r in range(0, q.rows, step)]
+
+
+def row_absmax(w, rows, cols):
+    """Largest magnitude of each row of bf16 bits [rows, cols], NaN never
+    chosen (row_absmax, lib.rs:432-455)."""
+    from .synth import bf16_bits_to_f32
+    w = np.asarray(w, np.uint16).reshape(-1)
+    if w.size != rows * cols:
+        raise ValueError("weight length against the shape")
+    a = np.abs(bf16_bits_to_f32(w).reshape(rows, cols))
+    a = np.where(np.isnan(a), np.float32(0.0), a)
+    return a.max(axis=1).astype(np.float32)
+
+
+def choose_exp_bias(absmax, fmt):
+    """The largest hardware exponent bias whose range max_finite *
+    2^(default - b) still covers `absmax`; the widest bias otherwise
+    (choose_exp_bias, lib.rs:457-475)."""
+    fmt = Fp8Format(fmt)
+    a = np.float32(absmax)
+    for b in fmt.hw_exponent_biases:
+        if a <= np.float32(fmt.max_finite) * _pow2(fmt.exponent_bias - b):
+            return b
+    return fmt.hw_exponent_biases[-1]
+
 
 def _check(w_size, rows, cols, backoff):
     if rows <= 0 or cols <= 0:
