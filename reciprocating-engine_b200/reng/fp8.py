@@ -269,3 +269,71 @@ def quantize_device(w, rows, cols, fmt, scaling, backoff=DEFAULT_BACKOFF, codes=
               float(backoff), codes.data_ptr(), scales.data_ptr(), C.byref(bias),
               _lib.RENG_MEM_DEVICE, st)
     return codes, scales, int(bias.value)
+
+
+# Rows per matrix the model-level pass measures its error on (FP8_ERROR_ROWS,
+# crates/reng-model/src/lib.rs:1853).
+FP8_ERROR_ROWS = 8
+PROJECTIONS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
+
+
+@dataclass
+class Fp8Report:
+    """What one model quantization pass produced (Fp8Report,
+    crates/reng-model/src/lib.rs:1827-1876)."""
+    matrices: int = 0
+    bf16_bytes: int = 0
+    fp8_bytes: int = 0
+    scale_bytes: int = 0
+    mean_rel: float = 0.0
+    max_rel: float = 0.0
+    secs: float = 0.0
+
+    def __str__(self):
+        gib = 1024.0 ** 3
+        return ("%d matrices, %.2f GiB bf16 -> %.2f GiB fp8 + %d KiB scales, mean rel %.4f, "
+                "max rel %.4f, %.2f s" % (self.matrices, self.bf16_bytes / gib, self.fp8_bytes / gib,
+                                           self.scale_bytes // 1024, self.mean_rel, self.max_rel,
+                                           self.secs))
+
+
+def quantize_model(w, cfg, fmt=Fp8Format.E4M3, scaling=Scaling.PerChannel, backoff=DEFAULT_BACKOFF,
+                   quantizer=None):
+    """The seven projections of every layer quantized, norms / embedding /
+    LM head left bf16 (LlamaWeights::quantize_fp8, lib.rs:1878-1937).
+    Returns (layers, report): layers[l] maps "wq".."wd" to Quantized, and the
+    report samples FP8_ERROR_ROWS rows per matrix.  `quantizer(w, rows,
+    cols, fmt, scaling, backoff) -> Quantized` defaults to quantize_with
+    (the GPU quantizer).  The engine's own FP8 path quantizes on the device
+    at create time with the same rules; this is the host API around it."""
+    import time
+    q = quantizer or quantize_with
+    t0 = time.perf_counter()
+    h, inter, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim()
+    qd, kvd = cfg.q_dim(), cfg.n_kv_heads() * hd
+    shapes = {"wq": (qd, h), "wk": (kvd, h), "wv": (kvd, h), "wo": (h, qd), "wg": (inter, h),
+              "wu": (inter, h), "wd": (h, inter)}
+    rep, errors, out = Fp8Report(), [], []
+    for li, lw in enumerate(w["layers"]):
+        layer = {}
+        for name in PROJECTIONS:
+            rows, cols = shapes[name]
+            m = np.asarray(lw[name], np.uint16).reshape(-1)
+            if m.size != rows * cols:
+                raise ValueError("layer %d %s: %d elements, expected %d x %d"
+                                 % (li, name, m.size, rows, cols))
+            qm = q(m, rows, cols, fmt, scaling, backoff)
+            rep.matrices += 1
+            rep.bf16_bytes += m.size * 2
+            rep.fp8_bytes += qm.code_bytes()
+            rep.scale_bytes += len(qm.scales) * 4
+            errors += sample_row_errors(m, qm, FP8_ERROR_ROWS)
+            layer[name] = qm
+        out.append(layer)
+    if errors:
+        rep.mean_rel = float(np.float32(np.cumsum(np.array([e.mean_rel for e in errors],
+                                                            np.float64))[-1] / len(errors)))
+        rep.max_rel = float(max(0.0, max((e.max_rel for e in errors
+                                          if not np.isnan(e.max_rel)), default=0.0)))
+    rep.secs = time.perf_counter() - t0
+    return out, rep

@@ -93,3 +93,35 @@ def test_row_absmax_and_exp_bias_choice_equal_the_restatement(oracle_lib):
         for a in (0.0, 0.5, 0.9375, 0.94, 15.0, 15.5, 240.0, 241.0, 3840.0, 5000.0, 57344.0, 1e6):
             assert choose_exp_bias(a, fmt) == lib.orc_choose_exp_bias(a, int(fmt)), (fmt, a)
     assert choose_exp_bias(15.0, Fp8Format.E4M3) == 11 and choose_exp_bias(5000.0, Fp8Format.E4M3) == 3
+
+
+def test_model_quantization_pass_and_report(oracle_lib):
+    """quantize_model over a small Llama: seven matrices per layer, byte
+    counts, the sampled error summary, and the reference's report line
+    (lib.rs:1827-1937).  The quantizer is the C restatement here (CPU)."""
+    import oracle
+    from reng.config import LlamaConfig
+    from reng.fp8 import Fp8Format, Quantized, Scaling, quantize_model, row_errors
+    from reng.weights import random_weights
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim_=16, vocab_size=50,
+                      model_type="llama")
+    w = random_weights(cfg, seed=4)
+
+    def host_quantizer(m, rows, cols, fmt, scaling, backoff):
+        c, s, b = oracle.quantize(m, rows, cols, int(fmt), int(scaling), backoff)
+        return Quantized(Fp8Format(fmt), Scaling(scaling), rows, cols, c, s, b)
+
+    layers, rep = quantize_model(w, cfg, quantizer=host_quantizer)
+    assert len(layers) == 2 and sorted(layers[0]) == sorted(("wq", "wk", "wv", "wo", "wg", "wu", "wd"))
+    per_layer = 64 * 64 * 2 + 32 * 64 * 2 + 96 * 64 * 3
+    assert rep.matrices == 14 and rep.fp8_bytes == 2 * per_layer and rep.bf16_bytes == 4 * per_layer
+    assert rep.scale_bytes == 4 * 2 * (64 + 32 + 32 + 64 + 96 + 96 + 64)
+    full = row_errors(w["layers"][1]["wd"], layers[1]["wd"])
+    assert rep.max_rel >= max(e.max_rel for e in full[::8])
+    assert 0.0 < rep.mean_rel < 0.05 and rep.max_rel < 0.07
+    line = str(rep)
+    assert line.startswith("14 matrices, 0.00 GiB bf16 -> 0.00 GiB fp8 + ") and "mean rel" in line
+    with pytest.raises(ValueError):
+        bad = {"layers": [dict(w["layers"][0], wq=w["layers"][0]["wq"][:10])]}
+        quantize_model(bad, cfg, quantizer=host_quantizer)
