@@ -266,6 +266,11 @@ int validate(const reng_model_desc* d) {
     RENG_CHECK_ARG(std::isfinite(d->eps) && d->eps >= 0.f && std::isfinite(d->attn_scale),
                    "reng_model_create: eps / attn_scale not finite");
     RENG_CHECK_ARG(d->capacity <= (1 << 20), "reng_model_create: capacity above 1048576 positions");
+    // the FP8 GEMV reads x 16 columns at a time: every K it sees (hidden,
+    // q width, intermediate per rank) must be a multiple of 16
+    if (d->weights == RENG_WEIGHTS_FP8_E4M3 && (d->inter / d->tp_world) % 16 != 0)
+        return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights need the intermediate size per rank (" +
+                                            std::to_string(d->inter / d->tp_world) + ") to be a multiple of 16");
     if (d->weights == RENG_WEIGHTS_FP8_E4M3 && d->batch > kMaxRows)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights run batch <= " + std::to_string(kMaxRows) +
                                             ", not " + std::to_string(d->batch));
