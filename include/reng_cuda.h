@@ -192,7 +192,9 @@ int reng_model_prefill(reng_model *m, int slot, const uint32_t *ids, int n, uint
 int reng_model_decode(reng_model *m, const uint32_t *seeds, int n, uint32_t *ids_out);
 
 /* The same with device-resident seeds [batch] and ids_out [n, batch], on
- * `stream`; asynchronous (no host synchronisation). */
+ * `stream`; asynchronous (no host synchronisation).  A seed outside the
+ * vocabulary cannot be checked on the host: the gather reads row 0 for it and
+ * the next synchronous call on the model returns RENG_E_INVAL. */
 int reng_model_decode_device(reng_model *m, const uint32_t *seeds, int n, uint32_t *ids_out,
                              void *stream);
 
