@@ -139,3 +139,32 @@ def test_requests_that_cannot_fit_are_refused(mods):
     with pytest.raises(ValueError):
         ContinuousBatcher(SlotEngine(2, 16), chunk=0)
     assert cb.pending() == 0
+
+
+@pytest.mark.gpu
+def test_continuous_batching_on_the_engine_matches_the_oracle(reng_lib, oracle_lib):
+    """Over the CUDA engine (4 slots): every request's ids are the greedy
+    ids of the f32 oracle teacher-forced on them, up to near-ties, whatever
+    slot and neighbours it ran with."""
+    from test_decode_gpu import check_greedy, oracle_for, small_cfg
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.serve import ContinuousBatcher, Request
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg()
+    w = random_weights(cfg, seed=21)
+    eng = Engine(cfg, w, batch=4, capacity=96)
+    cb = ContinuousBatcher(eng, chunk=6)
+    reqs = [Request(prompt_ids(3 + 2 * i, cfg.vocab_size, seed=40 + i).tolist(), 4 + 3 * (i % 5), rid=i)
+            for i in range(9)]
+    done = cb.run(reqs)
+    assert sorted(r.rid for r in done) == list(range(9))
+    sin, cos = rope_caches_for(cfg, 96)
+    orc = oracle_for(cfg, w)
+    for r in reqs:
+        assert len(r.output) == r.max_new
+        seq = np.array(list(r.prompt) + r.output[:-1], np.uint32)
+        want = orc.forward(seq, sin, cos, logits_from=len(r.prompt) - 1)
+        check_greedy(r.output, want)
+    eng.close()
