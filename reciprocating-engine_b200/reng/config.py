@@ -307,27 +307,32 @@ class LlamaConfig:
         return v is None or li >= len(v) or v[li] != 0
 
     # ------------------------------------------------------ engine support --
-    ENGINE_TYPES = (None, "llama", "qwen2", "mistral")
+    # the families whose layers are this engine's decoder as loaded: Granite
+    # once load_weights has folded its multipliers into the weights (the
+    # embedding one is applied at the gather), Phi-3 once its partial
+    # rotation is permuted into the kernels' pair order
+    ENGINE_TYPES = (None, "llama", "qwen2", "mistral", "granite", "phi3")
 
     def unsupported(self, capacity=None):
         """What this engine's kernels do not compute for this config (empty
         when it runs as written).  The reference parses more families than
         its device graph covers and refuses what it has no node for
         (`activation`, lib.rs:318-330; `mlp_bias`, :1479); this engine does
-        the same for the features outside the Llama/Qwen2 decoder it runs,
-        instead of computing a plain Llama in their place."""
+        the same for the features outside the decoder it runs, instead of
+        computing a plain Llama in their place.  It runs weights in the form
+        load_weights gives them: Granite's residual multiplier and
+        1/logits_scaling folded in, a partial rotation's q/k head dims in
+        pair order (the RoPE tables carry the identity on the pass-through
+        pairs)."""
         out = []
         raw = self.raw or {}
         if self.model_type not in self.ENGINE_TYPES:
             out.append("model_type %s" % self.model_type)
         if (self.hidden_act or "silu") != "silu":
             out.append("activation %s" % self.hidden_act)
-        if self.rotary_dim() != self.head_dim():
-            out.append("partial rotary (%d of %d head dims)" % (self.rotary_dim(), self.head_dim()))
         if raw.get("mlp_bias"):
             out.append("mlp_bias")
-        for k in ("embedding_multiplier", "attention_multiplier", "residual_multiplier", "logits_scaling",
-                  "final_logit_softcapping", "attn_logit_softcapping", "query_pre_attn_scalar"):
+        for k in ("final_logit_softcapping", "attn_logit_softcapping", "query_pre_attn_scalar"):
             if raw.get(k) is not None:
                 out.append(k)
         if raw.get("qk_norm") or raw.get("use_qk_norm"):

@@ -53,6 +53,16 @@ def fp8_switch(value, flag=False):
             Scaling.from_name(sch).short_name if sch else "pcs")
 
 
+def _scaled_table(t, s):
+    """bf16 bits of bf16(f32(t) * f32(s)), host array or device tensor."""
+    if isinstance(t, np.ndarray):
+        from .synth import bf16_bits_to_f32, f32_to_bf16_bits
+        return f32_to_bf16_bits(bf16_bits_to_f32(t) * np.float32(s))
+    import torch
+    f = t.view(torch.bfloat16).to(torch.float32) * torch.tensor(np.float32(s), device=t.device)
+    return f.to(torch.bfloat16).view(t.dtype)
+
+
 class Engine:
     def __init__(self, cfg, w, batch=1, capacity=1024, device=0, tp_rank=0, tp_world=1,
                  nccl_id=None, fp8=None):
@@ -126,10 +136,20 @@ class Engine:
             keep.append(fg)
         emb = w["embed"]
         lm = w["lm_head"]
+        es = cfg.embed_scale()
+        if es != 1.0:
+            # the gather's factor (Granite's embedding_multiplier): one f32
+            # product per element rounded to bf16, the value the reference's
+            # host gather hands its bf16 device graph (embed_tokens,
+            # crates/reng-model/src/lib.rs:2286-2305); a scaled copy, so a
+            # tied LM head keeps the table as stored
+            emb = _scaled_table(emb, es)
         if isinstance(emb, np.ndarray):
             emb = np.ascontiguousarray(emb)
+            keep.append(emb)
+        if isinstance(lm, np.ndarray):
             lm = np.ascontiguousarray(lm)
-            keep += [emb, lm]
+            keep.append(lm)
         h = C.c_void_p()
         _lib.call("reng_model_create", C.byref(desc), arr, _ptr(emb), _ptr(lm), _ptr(fg),
                   sin_p, cos_p, mem, C.byref(h))

@@ -312,3 +312,49 @@ def test_register_fragment_gemv_equals_shared_memory_gemv(lib, monkeypatch, batc
     assert np.array_equal(eng.decode(ids, 3), ref.decode(ids, 3))
     ref.close()
     eng.close()
+
+
+FAMILY_CASES = {
+    # Granite: every multiplier, folded by the loader (residual into o/down,
+    # 1/logits_scaling into the head), attention scale into wq, embedding
+    # scale at the gather
+    "granite": dict(model_type="granite", embedding_multiplier=12.0, attention_multiplier=0.0625,
+                    residual_multiplier=0.25, logits_scaling=8.0),
+    # Phi-3 with half the head dims rotated: q/k head dims permuted into the
+    # kernels' pair order, identity RoPE entries on the pass-through pairs
+    "phi3": dict(model_type="phi3", partial_rotary_factor=0.5),
+}
+
+
+@pytest.mark.parametrize("fam", sorted(FAMILY_CASES))
+def test_loaded_family_checkpoint_matches_the_oracle(lib, fam, tmp_path):
+    """A checkpoint of the family written in its HF layout, read back by
+    load_weights: prefill logits and greedy decode on the engine against
+    the f32 oracle with the reference's per-family settings
+    (oracle.Model.for_config, pinned to transformers for these families)."""
+    import oracle
+    from reng.config import LlamaConfig
+    from reng.model import Generator
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import load_weights, random_weights, save_checkpoint
+    d = dict(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+             num_key_value_heads=2, head_dim=64, vocab_size=1024, rms_norm_eps=1e-5,
+             rope_theta=10000.0, tie_word_embeddings=False, max_position_embeddings=4096)
+    d.update(FAMILY_CASES[fam])
+    cfg0 = LlamaConfig.from_dict(d)
+    save_checkpoint(str(tmp_path), cfg0, random_weights(cfg0, seed=31))
+    cfg = LlamaConfig.load(str(tmp_path))
+    assert cfg.unsupported(capacity=128) == []
+    w = load_weights(str(tmp_path), cfg)
+    orc = oracle.Model.for_config(cfg, w)
+    sin, cos = rope_caches_for(cfg, 128)
+    ids = prompt_ids(19, cfg.vocab_size, seed=8)
+    g = Generator(w, cfg, capacity=128)
+    check_rows(g.feed_all(ids), orc.forward(ids, sin, cos), fam + " prefill")
+    g.reset()
+    nxt = g.feed_id(ids)
+    out = g.generate(nxt, 12)
+    seq = np.concatenate([ids, [nxt], out[:-1]]).astype(np.uint32)
+    check_greedy([nxt] + out, orc.forward(seq, sin, cos, logits_from=ids.size - 1))
+    g.close()

@@ -184,9 +184,8 @@ def test_engine_refuses_what_its_kernels_do_not_compute():
         (dict(base, model_type="qwen3"), "model_type qwen3"),
         (dict(base, model_type="olmo2"), "model_type olmo2"),
         (dict(base, model_type="llama", hidden_act="gelu_pytorch_tanh"), "activation"),
-        (dict(base, model_type="llama", partial_rotary_factor=0.5), "partial rotary"),
         (dict(base, model_type="llama", mlp_bias=True), "mlp_bias"),
-        (dict(base, model_type="granite", embedding_multiplier=12.0), "embedding_multiplier"),
+        (dict(base, model_type="gemma2", attn_logit_softcapping=50.0), "attn_logit_softcapping"),
         (dict(base, model_type="mistral", sliding_window=1024), "sliding window"),
         ({"model_type": "gemma3", "text_config": {}}, "model_type gemma3_text"),
     ]
@@ -196,6 +195,11 @@ def test_engine_refuses_what_its_kernels_do_not_compute():
         assert any(what in m for m in miss), (d, miss)
         with pytest.raises(ValueError, match="does not run"):
             Engine(cfg, {"embed": np.zeros((1, 1), np.uint16)}, capacity=4096)
+    # Granite's multipliers (folded by the loader) and a partial rotation run
+    for d in (dict(base, model_type="granite", embedding_multiplier=12.0, residual_multiplier=0.25,
+                   attention_multiplier=0.0625, logits_scaling=8.0),
+              dict(base, model_type="phi3", partial_rotary_factor=0.5)):
+        assert LlamaConfig.from_dict(d).unsupported(capacity=4096) == [], d
     # a sliding window at or above the capacity attends exactly as full attention
     assert LlamaConfig.from_dict(dict(base, model_type="mistral", sliding_window=4096)).unsupported(4096) == []
 
@@ -266,3 +270,17 @@ def test_loader_reads_a_checkpoint_with_odd_offsets(tmp_path):
     for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2"):
         assert np.array_equal(odd["layers"][0][k], ref["layers"][0][k]), k
     assert np.array_equal(odd["embed"], ref["embed"]) and np.array_equal(odd["lm_head"], ref["lm_head"])
+
+
+def test_the_engine_scales_its_embedding_table_like_the_gather():
+    """bf16(f32(e) * f32(m)) per element, the same bits from a host array and
+    a torch tensor (the device path's arithmetic, run here on CPU)."""
+    import torch
+    from reng.model import _scaled_table
+    from reng.synth import bf16_bits_to_f32, f32_to_bf16_bits
+    e = f32_to_bf16_bits(np.random.default_rng(2).standard_normal((16, 32)).astype(np.float32) * 0.02)
+    want = f32_to_bf16_bits(bf16_bits_to_f32(e) * np.float32(12.0))
+    assert np.array_equal(_scaled_table(e, 12.0), want)
+    t = torch.from_numpy(e.view(np.int16).copy())
+    got = _scaled_table(t, 12.0)
+    assert got.dtype == torch.int16 and np.array_equal(got.numpy().view(np.uint16), want)
