@@ -5,8 +5,9 @@ Mirrors crates/reng-model/src/lib.rs: `LlamaConfig` (lib.rs:84-193),
 `q_dim` / `attention_scale` (lib.rs:666-705) and `shard` (lib.rs:725-742),
 and the per-family rules of lib.rs:268-420 (windows, Gemma sliding layers
 and softcaps, embedding scale, post-norm).  The engine runs the Llama /
-Qwen2 / Mistral decoder and refuses the rest (`unsupported`); the loader and
-the f32 oracle take every family the reference's host forward does.  A
+Qwen2 / Mistral decoder and Granite / Phi-3 checkpoints as loaded, and
+refuses the rest (`unsupported`); the loader and the f32 oracle take every
+family the reference's host forward does.  A
 multimodal Gemma-3 config parses through its `text_config`.
 """
 import copy
