@@ -80,6 +80,10 @@ class Engine:
         if any(any(b) != all(b) for b in has) or len({all(b) for b in has}) > 1:
             raise ValueError("q/k/v biases must be all present or all absent in every layer")
         with_bias = bool(has) and all(has[0])
+        warn = cfg.longrope_capacity_warning(capacity)
+        if warn:  # as the reference's generators do at construction (lib.rs:2870, 3059, 3272)
+            import sys
+            print(warn, file=sys.stderr)
         self.cfg = cfg
         self.batch = batch
         self.capacity = capacity
