@@ -51,8 +51,22 @@ const char *reng_last_error(void);
 int reng_version(void);
 
 /* Number of CUDA devices (replaces reng-hal's Gaudi accel discovery,
- * crates/reng-hal/src/lib.rs:62). */
+ * crates/reng-hal/src/lib.rs:62).  A host without a CUDA driver or device
+ * has 0 devices, not an error, as the reference's enumeration is empty on a
+ * host without the accel class. */
 int reng_device_count(int *count);
+
+/* One device's record (the role of reng-hal's GaudiDevice: index, kind,
+ * PCI address, silicon revision; crates/reng-hal/src/lib.rs:24-33). */
+typedef struct reng_device_info {
+    int32_t ordinal;        /* CUDA device ordinal */
+    char name[96];          /* the device's product name */
+    char pci_bus_id[32];    /* "0000:cc:00.0" form */
+    uint64_t total_bytes;   /* device memory */
+    int32_t sm_count;       /* streaming multiprocessors */
+    int32_t cc_major, cc_minor; /* compute capability (10.0 on B200) */
+} reng_device_info;
+int reng_device_info_get(int device, reng_device_info *out);
 
 /* ===================================================== FP8 quantizer ===
  * Replaces reng_fp8::quantize_with (crates/reng-fp8/src/lib.rs:519-563)

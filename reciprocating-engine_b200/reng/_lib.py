@@ -58,12 +58,19 @@ class StepTimes(C.Structure):
                 ("steps", C.c_int32), ("kernels_per_step", C.c_int32)]
 
 
+class DeviceInfo(C.Structure):
+    _fields_ = [("ordinal", C.c_int32), ("name", C.c_char * 96), ("pci_bus_id", C.c_char * 32),
+                ("total_bytes", C.c_uint64), ("sm_count", C.c_int32), ("cc_major", C.c_int32),
+                ("cc_minor", C.c_int32)]
+
+
 # Every exported symbol with its argument types (restype int unless noted).
 _P = C.c_void_p
 SIGNATURES = {
     "reng_last_error": ([], C.c_char_p),
     "reng_version": ([], C.c_int),
     "reng_device_count": ([_P], C.c_int),
+    "reng_device_info_get": ([C.c_int, _P], C.c_int),
     "reng_fp8_quantize": ([_P, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_float, _P, _P, _P,
                            C.c_int, _P], C.c_int),
     "reng_fp8_quantize_noalloc": ([_P, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_float, _P, _P,
@@ -117,3 +124,20 @@ def check(rc):
 
 def call(name, *args):
     return check(getattr(lib(), name)(*args))
+
+
+def devices():
+    """The CUDA devices of this host, one dict each (reng-hal's
+    enumerate_devices, crates/reng-hal/src/lib.rs:62: empty, not an error,
+    on a host without devices)."""
+    n = C.c_int(0)
+    call("reng_device_count", C.byref(n))
+    out = []
+    for d in range(n.value):
+        info = DeviceInfo()
+        call("reng_device_info_get", d, C.byref(info))
+        out.append({"ordinal": info.ordinal, "name": info.name.decode(errors="replace"),
+                    "pci_bus_id": info.pci_bus_id.decode(errors="replace"),
+                    "total_bytes": int(info.total_bytes), "sm_count": info.sm_count,
+                    "compute_capability": (info.cc_major, info.cc_minor)})
+    return out

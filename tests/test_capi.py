@@ -73,3 +73,50 @@ def test_model_create_refuses_bad_descriptors_without_a_device(reng_lib):
     rc = L.reng_model_create(C.byref(d), None, None, None, None, None, None, 1, C.byref(out))
     assert rc == reng_lib.RENG_E_INVAL
     assert out.value is None
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """Size and field offsets of every struct the header declares, as gcc
+    lays them out, against the ctypes mirrors the Python host passes."""
+    import ctypes as C
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    from reng import _lib
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    structs = {"reng_model_desc": _lib.ModelDesc, "reng_layer_weights": _lib.LayerWeights,
+               "reng_step_times": _lib.StepTimes, "reng_device_info": _lib.DeviceInfo}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "reng_cuda.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append('printf("%s size %%zu\\n", sizeof(%s));' % (cname, cname))
+        for fname, _ in py._fields_:
+            lines.append('printf("%s %s %%zu\\n", offsetof(%s, %s));' % (cname, fname, cname, fname))
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(root, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        a, b, v = line.split()
+        got[(a, b)] = int(v)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+
+
+@pytest.mark.gpu
+def test_device_discovery_agrees_with_torch(reng_lib):
+    import torch
+    from reng._lib import devices
+    d = devices()
+    assert len(d) == torch.cuda.device_count() >= 1
+    for i, rec in enumerate(d):
+        p = torch.cuda.get_device_properties(i)
+        assert rec["ordinal"] == i and rec["name"] and ":" in rec["pci_bus_id"]
+        assert rec["sm_count"] == p.multi_processor_count
+        assert rec["compute_capability"] == (p.major, p.minor)
+        assert rec["total_bytes"] == p.total_memory
