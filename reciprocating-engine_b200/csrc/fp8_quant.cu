@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fp8_product.h"
 
 namespace reng {
 
@@ -58,13 +59,29 @@ __device__ __forceinline__ uint32_t encode2(float a, float b) {
     return c;
 }
 
-// x / s as the reference's host computes it: IEEE division, and a NaN
-// generated by the division (not carried in from x) is x86's default NaN,
-// whose sign bit is set.
+// x / s as the reference's host computes it: IEEE division; a NaN weight
+// comes through as itself, sign included (x86 returns the NaN operand; GPU
+// arithmetic would return its canonical positive NaN), and a NaN generated
+// by the division is x86's default NaN, whose sign bit is set.
 __device__ __forceinline__ float div_host(float x, float s) {
+    if (isnan(x)) return x;
     float q = __fdiv_rn(x, s);
-    if (isnan(q) && !isnan(x)) q = __uint_as_float(0xffc00000u);
+    if (isnan(q)) q = __uint_as_float(0xffc00000u);
     return q;
+}
+
+// The same quotient without the division (fp8_product.h: Markstein's
+// correction of x * RN(1 / s)), for rows fp8_product_ok admits.
+template <int FMT>
+__device__ __forceinline__ uint2 encode8_product(uint4 v, float s, float r) {
+    uint2 o;
+    uint32_t c0 = encode2<FMT>(fp_quotient(bf16lo(v.x), s, r), fp_quotient(bf16hi(v.x), s, r));
+    uint32_t c1 = encode2<FMT>(fp_quotient(bf16lo(v.y), s, r), fp_quotient(bf16hi(v.y), s, r));
+    uint32_t c2 = encode2<FMT>(fp_quotient(bf16lo(v.z), s, r), fp_quotient(bf16hi(v.z), s, r));
+    uint32_t c3 = encode2<FMT>(fp_quotient(bf16lo(v.w), s, r), fp_quotient(bf16hi(v.w), s, r));
+    o.x = c0 | (c1 << 16);
+    o.y = c2 | (c3 << 16);
+    return o;
 }
 
 // 8 bf16 (one uint4) / s -> 8 codes (one uint2).
@@ -116,7 +133,7 @@ template <int FMT, int R>
 __global__ void __launch_bounds__(256) k_fp8_rows_vec(const uint16_t* __restrict__ w,
                                                       int64_t rows, int64_t cols, int mode,
                                                       float full, uint8_t* __restrict__ codes,
-                                                      float* __restrict__ scales) {
+                                                      float* __restrict__ scales, int product) {
     __shared__ float red[33];
     const int nch = (int)(cols >> 3);
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -147,10 +164,20 @@ __global__ void __launch_bounds__(256) k_fp8_rows_vec(const uint16_t* __restrict
             if (threadIdx.x == 0) scales[row] = s;
         }
         uint2* dst = reinterpret_cast<uint2*>(codes + row * cols);
+        // m bounds this thread's weights (its own absmax, or the row's)
+        const float rq = __frcp_rn(s);
+        if (product && fp8_product_ok(s, rq, m)) {
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            int c = threadIdx.x + r * blockDim.x;
-            if (c < nch) dst[c] = encode8<FMT>(v[r], s);
+            for (int r = 0; r < R; r++) {
+                int c = threadIdx.x + r * blockDim.x;
+                if (c < nch) dst[c] = encode8_product<FMT>(v[r], s, rq);
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                int c = threadIdx.x + r * blockDim.x;
+                if (c < nch) dst[c] = encode8<FMT>(v[r], s);
+            }
         }
     }
 }
@@ -261,19 +288,23 @@ template <int FMT>
 static void launch_rows(const uint16_t* w, int64_t rows, int64_t cols, int mode, float full,
                         uint8_t* codes, float* scales, bool vec, cudaStream_t st) {
     int grid = (int)std::min<int64_t>(rows, 148 * 64);
+    // RENG_FP8_PRODUCT=1: the division-free quotient (bit-identical; off by
+    // default until it is timed against the division on the GPU)
+    const char* pe = getenv("RENG_FP8_PRODUCT");
+    const int product = pe && atoi(pe) == 1 ? 1 : 0;
     if (!vec) {
         k_fp8_rows_any<FMT><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
         return;
     }
     int64_t nch = cols / 8;
     if (nch <= 256)
-        k_fp8_rows_vec<FMT, 1><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
+        k_fp8_rows_vec<FMT, 1><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales, product);
     else if (nch <= 512)
-        k_fp8_rows_vec<FMT, 2><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
+        k_fp8_rows_vec<FMT, 2><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales, product);
     else if (nch <= 1024)
-        k_fp8_rows_vec<FMT, 4><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
+        k_fp8_rows_vec<FMT, 4><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales, product);
     else if (nch <= 2048)
-        k_fp8_rows_vec<FMT, 8><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
+        k_fp8_rows_vec<FMT, 8><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales, product);
     else
         k_fp8_rows_any<FMT><<<grid, 256, 0, st>>>(w, rows, cols, mode, full, codes, scales);
 }

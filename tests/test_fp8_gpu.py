@@ -155,3 +155,45 @@ def test_decode_matches_the_oracle(reng_lib, oracle_lib):
         nan = np.isnan(want)
         assert np.array_equal(np.isnan(got), nan)
         assert np.array_equal(got[~nan], want[~nan])
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+@pytest.mark.parametrize("scaling", [0, 2])
+def test_division_free_quotient_is_bit_exact(fp8, oracle_lib, monkeypatch, fmt, scaling):
+    """RENG_FP8_PRODUCT=1 (Markstein's correction of x * RN(1/s) in place
+    of the division, csrc/fp8_product.h): the config-0 matrix and the rows
+    of special values, bit for bit against the oracle's x / s."""
+    import torch
+    from reng.synth import f32_to_bf16_bits, fp8_config0_matrix
+    monkeypatch.setenv("RENG_FP8_PRODUCT", "1")
+    rows = cols = 4096
+    w = fp8_config0_matrix(rows, cols, seed=99)
+    co, so, bo = oracle_lib.quantize(w, rows, cols, fmt, scaling)
+    codes, scales, bias = fp8.quantize_device(torch.from_numpy(w.view(np.int16)).cuda(), rows, cols, fmt, scaling)
+    torch.cuda.synchronize()
+    assert bias == bo
+    assert np.array_equal(scales.cpu().numpy().view(np.uint32), so.view(np.uint32))
+    got = codes.cpu().numpy().reshape(-1)
+    bad = np.flatnonzero(got != co)
+    assert bad.size == 0, (bad[:4], got[bad[:4]], co[bad[:4]])
+    rng = np.random.default_rng(5)
+    x = np.concatenate([_special_row(rng, 4104) for _ in range(9)])
+    ws = f32_to_bf16_bits(x)
+    co, so, bo = oracle_lib.quantize(ws, 9, 4104, fmt, scaling)
+    q = fp8.quantize(ws, 9, 4104, fmt, scaling)
+    assert np.array_equal(q.scales.view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(q.codes, co)
+
+
+@pytest.mark.parametrize("product", ["0", "1"])
+def test_a_negative_nan_weight_keeps_its_sign(fp8, oracle_lib, monkeypatch, product):
+    """The reference's x86 division returns a NaN operand as it is, sign
+    included: a negative NaN weight encodes to 0xff, a positive one to 0x7f
+    (division and division-free paths)."""
+    monkeypatch.setenv("RENG_FP8_PRODUCT", product)
+    w = np.array([0x3F80, 0xFFC0, 0x7FC0, 0xBF00, 0x4000, 0x0000, 0x8000, 0x3E00] * 2, np.uint16)
+    for fmt in (0, 1):
+        co, so, _ = oracle_lib.quantize(w, 2, 8, fmt, 0)
+        q = fp8.quantize(w, 2, 8, fmt, 0)
+        assert co[1] == 0xFF and co[2] == 0x7F
+        assert np.array_equal(q.codes, co), (fmt, q.codes, co)
