@@ -152,6 +152,12 @@ typedef struct reng_model_desc {
     int32_t tp_world;       /* tensor-parallel world size (1 without TP) */
     int32_t device;         /* CUDA device ordinal the model lives on */
     const uint8_t *nccl_id; /* 128-byte ncclUniqueId when tp_world > 1, else NULL */
+    int32_t qk_norm;        /* 1: per-head RMSNorm of q and k before RoPE (Qwen3,
+                               model.rs:2962-3010); the layers carry qn / kn
+                               [head_dim] gains, and attn_scale rides on qn, not
+                               on wq.  Gated: RENG_E_UNSUPPORTED unless the
+                               environment sets RENG_QK_NORM=1 (not yet
+                               parity-tested on a GPU).  0 otherwise. */
 } reng_model_desc;
 
 /* One decoder layer's weights (layer.rs:16-136): bf16 [out, in] projections
@@ -164,6 +170,7 @@ typedef struct reng_layer_weights {
     const uint16_t *wg, *wu, *wd;      /* [inter,h] [inter,h] [h,inter] */
     const float *g1, *g2;              /* input_layernorm, post_attention_layernorm [h] */
     const float *bq, *bk, *bv;         /* [q_dim] [kv_dim] [kv_dim] or NULL */
+    const float *qn, *kn;              /* [head_dim] q / k norm gains with qk_norm, else NULL */
 } reng_layer_weights;
 
 /*

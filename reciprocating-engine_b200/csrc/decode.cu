@@ -603,6 +603,61 @@ cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t
     return cudaLaunchKernelEx(&cfg, k_attn, a);
 }
 
+// --------------------------------------------------------------- q/k norm --
+// One warp per (head, row): RMS over the head, the gain, then rotate-half
+// RoPE at the row's position (crates/reng-synapse/src/model.rs:2962-3010:
+// head_norm before rope_head).  The head is staged in shared memory for the
+// rotation's partner element.
+__global__ void __launch_bounds__(32) k_qk_norm(QkNormArgs a) {
+    __shared__ float t[kAttnMaxHd];
+    const int j = blockIdx.x, m = blockIdx.y, lane = threadIdx.x;
+    pdl_wait();
+    pdl_launch();
+    const int pos = __ldcg(a.row_pos + m);
+    if (pos >= a.cap) return;  // as the q/k/v epilogue: such a row wrote nothing
+    const int hd = a.hd, half = hd >> 1;
+    uint16_t* p;
+    const float* g;
+    if (j < a.nq) {
+        p = a.q + (size_t)m * a.q_dim + (size_t)j * hd;
+        g = a.qn;
+    } else {
+        const int slot = __ldcg(a.row_slot + m);
+        p = a.kcache + (((size_t)slot * a.n_kv + (j - a.nq)) * a.cap + pos) * hd;
+        g = a.kn;
+    }
+    float ss = 0.f;
+    for (int d = lane; d < hd; d += 32) {
+        const float v = bf16_bits_to_f32(p[d]);
+        t[d] = v;
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hd + a.eps);
+    for (int d = lane; d < hd; d += 32) t[d] = t[d] * inv * g[d];  // each lane its own elements
+    __syncwarp();
+    const float* cs = a.rope_cos + (size_t)pos * hd;
+    const float* sn = a.rope_sin + (size_t)pos * hd;
+    for (int d = lane; d < hd; d += 32) {
+        const float rot = d < half ? -t[d + half] : t[d - half];
+        p[d] = f32_to_bf16_bits(t[d] * cs[d] + rot * sn[d]);
+    }
+}
+
+cudaError_t launch_qk_norm(const QkNormArgs& a, bool pdl, cudaStream_t st) {
+    if (a.hd > kAttnMaxHd || a.hd % 2 || a.M < 1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(a.nq + a.n_kv, a.M);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_qk_norm, a);
+}
+
 // ----------------------------------------------------------------- embed --
 __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
     const int m = blockIdx.x;

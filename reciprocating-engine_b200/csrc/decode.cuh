@@ -113,6 +113,22 @@ struct GemvArgs {
     const HeadXchg* hx;
 };
 
+// Per-head q/k RMSNorm and RoPE (Qwen3's q_norm / k_norm) of the rows a
+// q/k/v launch wrote raw (it rotated with the identity table): q heads in the
+// q buffer, K heads at each row's cache position, in place.
+struct QkNormArgs {
+    uint16_t* q;                 // [M][q_dim]
+    uint16_t* kcache;            // this layer's K cache [slot][n_kv][cap][hd]
+    const float* qn;             // [hd] q gains, the attention scale folded in
+    const float* kn;             // [hd] k gains
+    const float* rope_cos;       // [cap][hd] the model's tables
+    const float* rope_sin;
+    const int* row_slot;
+    const int* row_pos;
+    int M, nq, n_kv, hd, cap, q_dim;
+    float eps;
+};
+
 struct AttnArgs {
     const uint16_t* q;      // [M][q_dim]
     const uint16_t* kcache; // this layer [B][n_kv][cap][hd]
@@ -188,6 +204,7 @@ cudaError_t launch_gemv8(const GemvArgs& a, int epi, bool pdl, cudaStream_t st);
 cudaError_t gemv8_prepare();
 cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
 cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
+cudaError_t launch_qk_norm(const QkNormArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);
 cudaError_t launch_pack8(const Pack8Args& a, cudaStream_t st);
 cudaError_t launch_gather_scales(const float* src, const int* rowmap, int n, float mul, int mul_rows,

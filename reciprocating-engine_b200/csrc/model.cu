@@ -30,6 +30,7 @@ int tp_exchange_kind(reng_model* m);
 struct LayerDev {
     uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
     float *g1 = nullptr, *g2 = nullptr, *bqkv = nullptr;
+    float *qn = nullptr, *kn = nullptr;  // q/k norm gains [hd] (qk_norm; qn carries the attention scale)
     // FP8 weights: per packed row scales (null for bf16)
     float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sd = nullptr;
 };
@@ -47,6 +48,10 @@ struct reng_model {
     uint8_t* lm = nullptr;
     uint16_t* embed = nullptr;
     float *final_gamma = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    // q/k norm (Qwen3): the q/k/v launch rotates with the identity table and
+    // k_qk_norm normalises and rotates with the real one
+    bool qk_norm = false;
+    float *rope_cos_id = nullptr, *rope_sin_id = nullptr;
     uint16_t *kcache = nullptr, *vcache = nullptr;
     size_t layer_kv = 0;  // elements per layer
     // work buffers
@@ -200,6 +205,11 @@ std::vector<int> plain_map(int rows) {
     return v;
 }
 
+__global__ void k_fill_f32(float* p, size_t n, float v) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = v;
+}
+
 int upload_f32(reng_model* m, float** out, const float* src, size_t n, int mem) {
     TRY(dalloc(m, out, n));
     if (src == nullptr) {
@@ -271,6 +281,14 @@ int validate(const reng_model_desc* d) {
     if (d->weights == RENG_WEIGHTS_FP8_E4M3 && (d->inter / d->tp_world) % 16 != 0)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights need the intermediate size per rank (" +
                                             std::to_string(d->inter / d->tp_world) + ") to be a multiple of 16");
+    RENG_CHECK_ARG(d->qk_norm == 0 || d->qk_norm == 1, "reng_model_create: qk_norm must be 0 or 1");
+    if (d->qk_norm) {
+        // written and checked by reading, not yet parity-tested on a GPU
+        const char* g = getenv("RENG_QK_NORM");
+        if (!(g && atoi(g) == 1))
+            return fail(RENG_E_UNSUPPORTED, "reng_model_create: q/k norm models run with RENG_QK_NORM=1 only, "
+                                            "until their GPU parity run");
+    }
     if (d->weights == RENG_WEIGHTS_FP8_E4M3 && d->batch > kMaxRows)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights run batch <= " + std::to_string(kMaxRows) +
                                             ", not " + std::to_string(d->batch));
@@ -409,8 +427,8 @@ GemvArgs qkv_args(reng_model* m, int l, int M) {
     g.q_tiles = m->q_tiles;
     g.k_tiles = m->k_tiles;
     g.n_kv = m->nkv;
-    g.rope_cos = m->rope_cos;
-    g.rope_sin = m->rope_sin;
+    g.rope_cos = m->qk_norm ? m->rope_cos_id : m->rope_cos;  // q/k norm: raw q/k, rotated after the norm
+    g.rope_sin = m->qk_norm ? m->rope_sin_id : m->rope_sin;
     g.kcache = m->kcache + (size_t)l * m->layer_kv;
     g.vcache = m->vcache + (size_t)l * m->layer_kv;
     g.cap = m->cap;
@@ -418,7 +436,28 @@ GemvArgs qkv_args(reng_model* m, int l, int M) {
 }
 
 int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
-    return linear(m, qkv_args(m, l, M), EPI_QKV, 0, 0, st);
+    TRY(linear(m, qkv_args(m, l, M), EPI_QKV, 0, 0, st));
+    if (m->qk_norm) {  // per-head RMSNorm of q and k, then RoPE (model.rs:2962-3010)
+        QkNormArgs a{};
+        a.q = m->qbuf;
+        a.kcache = m->kcache + (size_t)l * m->layer_kv;
+        a.qn = m->layers[l].qn;
+        a.kn = m->layers[l].kn;
+        a.rope_cos = m->rope_cos;
+        a.rope_sin = m->rope_sin;
+        a.row_slot = m->row_slot;
+        a.row_pos = m->row_pos;
+        a.M = M;
+        a.nq = m->nh;
+        a.n_kv = m->nkv;
+        a.hd = m->hd;
+        a.cap = m->cap;
+        a.q_dim = m->q_dim;
+        a.eps = m->d.eps;
+        CU(launch_qk_norm(a, true, st));
+        m->launches++;
+    }
+    return RENG_OK;
 }
 
 AttnArgs attn_args(reng_model* m, int l, int M, int mode) {
@@ -578,7 +617,7 @@ int build_step(reng_model* m) {
     m->step_on = false;
     const char* env = getenv("RENG_STEP_KERNEL");
     if (!env || atoi(env) != 1) return RENG_OK;
-    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep) return RENG_OK;
+    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep || m->qk_norm) return RENG_OK;
     const int M = m->B;
     std::vector<StepPhase> ph;
     StepPhase pe{};
@@ -746,6 +785,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;
+    m->qk_norm = d->qk_norm == 1;
+    // the attention scale rides on wq (and bq), or on the q norm gain
+    // (scaled_wq, model.rs:148-157)
+    const float wq_scale = m->qk_norm ? 1.0f : d->attn_scale;
     const int W = m->world, R = m->rank;
     m->hidden = d->hidden;
     m->L = d->n_layers;
@@ -804,16 +847,18 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
         if (d->has_qkv_bias)
             RENG_CHECK_ARG(s.bq && s.bk && s.bv, "reng_model_create: layer " + std::to_string(l) + " lacks a bias");
         LayerDev& w = m->layers[l];
+        if (m->qk_norm)
+            RENG_CHECK_ARG(s.qn && s.kn, "reng_model_create: layer " + std::to_string(l) + " lacks q/k norm gains");
         // q, k, v row blocks of this rank
         TRY(copy_matrix(stage, s.wq + (size_t)R * m->q_dim * H, m->q_dim, H, H, mem, m->st));
         TRY(copy_matrix(stage + (size_t)m->q_dim * H, s.wk + (size_t)R * m->kv_dim * H, m->kv_dim, H, H, mem, m->st));
         TRY(copy_matrix(stage + (size_t)(m->q_dim + m->kv_dim) * H, s.wv + (size_t)R * m->kv_dim * H, m->kv_dim, H, H,
                         mem, m->st));
         if (m->w8)
-            TRY(pack_fp8(m, &w.wqkv, &w.sqkv, stage, m->q_dim + 2 * m->kv_dim, qkv_map, H, d->attn_scale, m->q_dim,
+            TRY(pack_fp8(m, &w.wqkv, &w.sqkv, stage, m->q_dim + 2 * m->kv_dim, qkv_map, H, wq_scale, m->q_dim,
                          &m->qkv_tiles));
         else
-            TRY(pack(m, &w.wqkv, stage, qkv_map, H, d->attn_scale, m->q_dim, &m->qkv_tiles));
+            TRY(pack(m, &w.wqkv, stage, qkv_map, H, wq_scale, m->q_dim, &m->qkv_tiles));
         // o_proj column window
         TRY(copy_matrix(stage, s.wo + (size_t)R * m->q_dim, H, m->q_dim, q_full, mem, m->st));
         if (m->w8)
@@ -846,11 +891,21 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
             TRY(fetch(hb.data(), s.bq, q_full));
             TRY(fetch(hb.data() + q_full, s.bk, kv_full));
             TRY(fetch(hb.data() + q_full + kv_full, s.bv, kv_full));
-            for (int i = 0; i < m->q_dim; i++) bias[i] = hb[(size_t)R * m->q_dim + i] * d->attn_scale;
+            for (int i = 0; i < m->q_dim; i++) bias[i] = hb[(size_t)R * m->q_dim + i] * wq_scale;
             for (int i = 0; i < m->kv_dim; i++) bias[m->q_dim + i] = hb[q_full + (size_t)R * m->kv_dim + i];
             for (int i = 0; i < m->kv_dim; i++)
                 bias[m->q_dim + m->kv_dim + i] = hb[q_full + kv_full + (size_t)R * m->kv_dim + i];
             TRY(upload_f32(m, &w.bqkv, bias.data(), bias.size(), RENG_MEM_HOST));
+            CU(cudaStreamSynchronize(m->st));
+        }
+        if (m->qk_norm) {
+            // the attention scale rides on the q gain, in f32 (model.rs:2989-2991)
+            std::vector<float> g((size_t)m->hd);
+            if (mem == RENG_MEM_HOST) memcpy(g.data(), s.qn, g.size() * 4);
+            else CU(cudaMemcpy(g.data(), s.qn, g.size() * 4, cudaMemcpyDeviceToHost));
+            for (float& v : g) v *= d->attn_scale;
+            TRY(upload_f32(m, &w.qn, g.data(), g.size(), RENG_MEM_HOST));
+            TRY(upload_f32(m, &w.kn, s.kn, (size_t)m->hd, mem));
             CU(cudaStreamSynchronize(m->st));
         }
     }
@@ -863,6 +918,13 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(upload_f32(m, &m->final_gamma, final_gamma, H, mem));
     TRY(upload_f32(m, &m->rope_cos, rope_cos, (size_t)m->cap * m->hd, mem));
     TRY(upload_f32(m, &m->rope_sin, rope_sin, (size_t)m->cap * m->hd, mem));
+    if (m->qk_norm) {  // identity rotation for the q/k/v launch: cos 1, sin 0
+        const size_t n = (size_t)m->cap * m->hd;
+        TRY(upload_f32(m, &m->rope_sin_id, nullptr, n, RENG_MEM_HOST));
+        TRY(dalloc(m, &m->rope_cos_id, n));
+        k_fill_f32<<<m->sms * 4, 256, 0, m->st>>>(m->rope_cos_id, n, 1.0f);
+        CU(cudaGetLastError());
+    }
 
     // ---- KV cache and work buffers ----
     m->layer_kv = (size_t)m->B * m->nkv * m->cap * m->hd;

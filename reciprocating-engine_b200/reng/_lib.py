@@ -45,12 +45,12 @@ class ModelDesc(C.Structure):
                 ("vocab", C.c_int32), ("eps", C.c_float), ("attn_scale", C.c_float),
                 ("has_qkv_bias", C.c_int32), ("weights", C.c_int32), ("batch", C.c_int32),
                 ("capacity", C.c_int32), ("tp_rank", C.c_int32), ("tp_world", C.c_int32),
-                ("device", C.c_int32), ("nccl_id", C.c_void_p)]
+                ("device", C.c_int32), ("nccl_id", C.c_void_p), ("qk_norm", C.c_int32)]
 
 
 class LayerWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in
-                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv")]
+                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv", "qn", "kn")]
 
 
 class StepTimes(C.Structure):

@@ -27,6 +27,10 @@ def _ptr(x):
     return x.data_ptr()
 
 
+def _numel(x):
+    return x.size if isinstance(x, np.ndarray) else x.numel()
+
+
 def _is_device(w):
     x = w["embed"]
     return not isinstance(x, np.ndarray)
@@ -68,8 +72,17 @@ class Engine:
                  nccl_id=None, fp8=None):
         missing = cfg.unsupported(capacity)
         layers = w.get("layers", ())
-        if any(lw.get(k) is not None for lw in layers for k in ("qn", "kn")):
+        qk = any(lw.get(k) is not None for lw in layers for k in ("qn", "kn"))
+        # q/k norm (Qwen3's per-head form) runs only with RENG_QK_NORM=1 until
+        # its GPU parity run; the library holds the same gate
+        qk_gate = os.environ.get("RENG_QK_NORM", "0") == "1"
+        if qk_gate:
+            missing = [x for x in missing if x != "model_type qwen3"]
+        if qk and not qk_gate:
             missing = missing + ["q/k RMSNorm gains"]
+        elif qk and not all(lw.get(k) is not None and _numel(lw[k]) == cfg.head_dim()
+                            for lw in layers for k in ("qn", "kn")):
+            missing = missing + ["whole-row q/k norm"]
         if any(lw.get(k) is not None for lw in layers for k in ("g_post_attn", "g_post_mlp")):
             missing = missing + ["branch-output norms"]
         if missing:
@@ -105,7 +118,7 @@ class Engine:
         n = len(w["layers"])
         arr = (_lib.LayerWeights * n)()
         for i, lw in enumerate(w["layers"]):
-            for k in MATS + ("g1", "g2", "bq", "bk", "bv"):
+            for k in MATS + ("g1", "g2", "bq", "bk", "bv", "qn", "kn"):
                 x = lw.get(k)
                 if x is None:
                     continue
@@ -124,6 +137,7 @@ class Engine:
         desc.eps = cfg.rms_norm_eps
         desc.attn_scale = cfg.attention_scale()
         desc.has_qkv_bias = 1 if with_bias else 0
+        desc.qk_norm = 1 if qk else 0
         desc.weights = _lib.RENG_WEIGHTS_BF16 if fp8 is None else _lib.RENG_WEIGHTS_FP8_E4M3
         desc.batch = batch
         desc.capacity = capacity

@@ -284,3 +284,24 @@ def test_the_engine_scales_its_embedding_table_like_the_gather():
     t = torch.from_numpy(e.view(np.int16).copy())
     got = _scaled_table(t, 12.0)
     assert got.dtype == torch.int16 and np.array_equal(got.numpy().view(np.uint16), want)
+
+
+def test_qk_norm_runs_only_behind_its_gate(monkeypatch):
+    """Qwen3's per-head q/k norm reaches the library only with
+    RENG_QK_NORM=1 (until its GPU parity run); the whole-row form (OLMo-2)
+    is refused either way.  Both refusals come before any device work."""
+    from reng.config import LlamaConfig
+    from reng.model import Engine
+    base = {"hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 1,
+            "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 16, "vocab_size": 32,
+            "model_type": "qwen3"}
+    cfg = LlamaConfig.from_dict(base)
+    head = {"qn": np.ones(16, np.float32), "kn": np.ones(16, np.float32)}
+    wide = {"qn": np.ones(64, np.float32), "kn": np.ones(32, np.float32)}
+    monkeypatch.delenv("RENG_QK_NORM", raising=False)
+    with pytest.raises(ValueError, match="q/k RMSNorm"):
+        Engine(cfg, {"layers": [head], "embed": np.zeros((1, 1), np.uint16)}, capacity=64)
+    monkeypatch.setenv("RENG_QK_NORM", "1")
+    with pytest.raises(ValueError, match="whole-row q/k norm"):
+        Engine(cfg, {"layers": [wide], "embed": np.zeros((1, 1), np.uint16)}, capacity=64)
+    assert "model_type qwen3" in cfg.unsupported(capacity=64)   # the config rule itself is unchanged
