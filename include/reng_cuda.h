@@ -171,6 +171,8 @@ typedef struct reng_layer_weights {
     const float *g1, *g2;              /* input_layernorm, post_attention_layernorm [h] */
     const float *bq, *bk, *bv;         /* [q_dim] [kv_dim] [kv_dim] or NULL */
     const float *qn, *kn;              /* [head_dim] q / k norm gains with qk_norm, else NULL */
+    int32_t no_rope;                   /* 1: the layer rotates nothing (SmolLM3's NoPE layers,
+                                          reng-model use_rope), else 0 */
 } reng_layer_weights;
 
 /*

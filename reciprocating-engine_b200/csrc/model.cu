@@ -31,6 +31,7 @@ struct LayerDev {
     uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
     float *g1 = nullptr, *g2 = nullptr, *bqkv = nullptr;
     float *qn = nullptr, *kn = nullptr;  // q/k norm gains [hd] (qk_norm; qn carries the attention scale)
+    bool no_rope = false;                // NoPE layer: the q/k/v launch rotates with the identity table
     // FP8 weights: per packed row scales (null for bf16)
     float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sd = nullptr;
 };
@@ -51,6 +52,7 @@ struct reng_model {
     // q/k norm (Qwen3): the q/k/v launch rotates with the identity table and
     // k_qk_norm normalises and rotates with the real one
     bool qk_norm = false;
+    bool any_no_rope = false;  // some layer rotates nothing (NoPE)
     float *rope_cos_id = nullptr, *rope_sin_id = nullptr;
     uint16_t *kcache = nullptr, *vcache = nullptr;
     size_t layer_kv = 0;  // elements per layer
@@ -427,8 +429,10 @@ GemvArgs qkv_args(reng_model* m, int l, int M) {
     g.q_tiles = m->q_tiles;
     g.k_tiles = m->k_tiles;
     g.n_kv = m->nkv;
-    g.rope_cos = m->qk_norm ? m->rope_cos_id : m->rope_cos;  // q/k norm: raw q/k, rotated after the norm
-    g.rope_sin = m->qk_norm ? m->rope_sin_id : m->rope_sin;
+    // q/k norm: raw q/k, rotated after the norm; NoPE: never rotated
+    const bool id = m->qk_norm || w.no_rope;
+    g.rope_cos = id ? m->rope_cos_id : m->rope_cos;
+    g.rope_sin = id ? m->rope_sin_id : m->rope_sin;
     g.kcache = m->kcache + (size_t)l * m->layer_kv;
     g.vcache = m->vcache + (size_t)l * m->layer_kv;
     g.cap = m->cap;
@@ -443,8 +447,8 @@ int k_qkv_launch(reng_model* m, int l, int M, cudaStream_t st) {
         a.kcache = m->kcache + (size_t)l * m->layer_kv;
         a.qn = m->layers[l].qn;
         a.kn = m->layers[l].kn;
-        a.rope_cos = m->rope_cos;
-        a.rope_sin = m->rope_sin;
+        a.rope_cos = m->layers[l].no_rope ? m->rope_cos_id : m->rope_cos;
+        a.rope_sin = m->layers[l].no_rope ? m->rope_sin_id : m->rope_sin;
         a.row_slot = m->row_slot;
         a.row_pos = m->row_pos;
         a.M = M;
@@ -617,7 +621,9 @@ int build_step(reng_model* m) {
     m->step_on = false;
     const char* env = getenv("RENG_STEP_KERNEL");
     if (!env || atoi(env) != 1) return RENG_OK;
-    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep || m->qk_norm) return RENG_OK;
+    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep || m->qk_norm ||
+        m->any_no_rope)
+        return RENG_OK;
     const int M = m->B;
     std::vector<StepPhase> ph;
     StepPhase pe{};
@@ -849,6 +855,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
         LayerDev& w = m->layers[l];
         if (m->qk_norm)
             RENG_CHECK_ARG(s.qn && s.kn, "reng_model_create: layer " + std::to_string(l) + " lacks q/k norm gains");
+        RENG_CHECK_ARG(s.no_rope == 0 || s.no_rope == 1, "reng_model_create: layer " + std::to_string(l) +
+                                                             " no_rope must be 0 or 1");
+        w.no_rope = s.no_rope == 1;
+        m->any_no_rope = m->any_no_rope || w.no_rope;
         // q, k, v row blocks of this rank
         TRY(copy_matrix(stage, s.wq + (size_t)R * m->q_dim * H, m->q_dim, H, H, mem, m->st));
         TRY(copy_matrix(stage + (size_t)m->q_dim * H, s.wk + (size_t)R * m->kv_dim * H, m->kv_dim, H, H, mem, m->st));
@@ -918,7 +928,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(upload_f32(m, &m->final_gamma, final_gamma, H, mem));
     TRY(upload_f32(m, &m->rope_cos, rope_cos, (size_t)m->cap * m->hd, mem));
     TRY(upload_f32(m, &m->rope_sin, rope_sin, (size_t)m->cap * m->hd, mem));
-    if (m->qk_norm) {  // identity rotation for the q/k/v launch: cos 1, sin 0
+    if (m->qk_norm || m->any_no_rope) {  // identity rotation for the q/k/v launch: cos 1, sin 0
         const size_t n = (size_t)m->cap * m->hd;
         TRY(upload_f32(m, &m->rope_sin_id, nullptr, n, RENG_MEM_HOST));
         TRY(dalloc(m, &m->rope_cos_id, n));

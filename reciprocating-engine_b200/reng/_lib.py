@@ -50,7 +50,8 @@ class ModelDesc(C.Structure):
 
 class LayerWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in
-                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv", "qn", "kn")]
+                ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2", "bq", "bk", "bv", "qn", "kn")] + \
+               [("no_rope", C.c_int32)]
 
 
 class StepTimes(C.Structure):

@@ -311,8 +311,9 @@ class LlamaConfig:
     # the families whose layers are this engine's decoder as loaded: Granite
     # once load_weights has folded its multipliers into the weights (the
     # embedding one is applied at the gather), Phi-3 once its partial
-    # rotation is permuted into the kernels' pair order
-    ENGINE_TYPES = (None, "llama", "qwen2", "mistral", "granite", "phi3")
+    # rotation is permuted into the kernels' pair order, SmolLM3 with its
+    # NoPE layers rotating nothing
+    ENGINE_TYPES = (None, "llama", "qwen2", "mistral", "granite", "phi3", "smollm3")
 
     def unsupported(self, capacity=None):
         """What this engine's kernels do not compute for this config (empty
@@ -338,8 +339,6 @@ class LlamaConfig:
                 out.append(k)
         if raw.get("qk_norm") or raw.get("use_qk_norm"):
             out.append("q/k RMSNorm")
-        if any(not self.use_rope(li) for li in range(self.num_hidden_layers)):
-            out.append("NoPE layers")
         win = self.window()
         if win and capacity is not None and capacity > win:
             out.append("sliding window %d below the capacity %d" % (win, capacity))

@@ -118,6 +118,7 @@ class Engine:
         n = len(w["layers"])
         arr = (_lib.LayerWeights * n)()
         for i, lw in enumerate(w["layers"]):
+            arr[i].no_rope = 0 if cfg.use_rope(i) else 1  # NoPE layers rotate nothing
             for k in MATS + ("g1", "g2", "bq", "bk", "bv", "qn", "kn"):
                 x = lw.get(k)
                 if x is None:

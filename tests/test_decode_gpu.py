@@ -323,6 +323,9 @@ FAMILY_CASES = {
     # Phi-3 with half the head dims rotated: q/k head dims permuted into the
     # kernels' pair order, identity RoPE entries on the pass-through pairs
     "phi3": dict(model_type="phi3", partial_rotary_factor=0.5),
+    # SmolLM3: layer 1 applies no rotary embedding (the q/k/v launch
+    # rotates with the identity table there)
+    "smollm3": dict(model_type="smollm3", no_rope_layers=[1, 0], use_sliding_window=False),
 }
 
 

@@ -90,11 +90,12 @@ def test_family_rules_as_parsed(golden, tmp_path):
     assert got["mistral"].window() == 8 and got["phi3"].window() == 8
     assert got["phi3"].rotary_dim() == 8
     assert [got["smollm3"].use_rope(i) for i in range(2)] == [True, False]
-    # the engine runs Granite (multipliers folded by the loader) and partial
-    # rotation; it refuses the rest, and Phi-3 here for its window of 8
-    # below the capacity
+    # the engine runs Granite (multipliers folded by the loader), partial
+    # rotation and NoPE layers; it refuses the rest, and Phi-3 here for its
+    # window of 8 below the capacity
     for fam, c in got.items():
-        assert bool(c.unsupported(capacity=64)) == (fam != "granite"), (fam, c.unsupported(capacity=64))
+        assert bool(c.unsupported(capacity=64)) == (fam not in ("granite", "smollm3")), \
+            (fam, c.unsupported(capacity=64))
     assert got["phi3"].unsupported(capacity=8) == []
 
 
