@@ -47,7 +47,9 @@ extern "C" {
 /* Message of the last failure on this thread ("" if none). */
 const char *reng_last_error(void);
 
-/* ABI version: (major << 16) | minor. */
+/* ABI version: (major << 16) | minor.  Minor 2 added reng_model_desc.qk_norm
+ * and reng_layer_weights.qn / kn / no_rope; callers built against minor 1
+ * pass structs that are too short. */
 int reng_version(void);
 
 /* Number of CUDA devices (replaces reng-hal's Gaudi accel discovery,

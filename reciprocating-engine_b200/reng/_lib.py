@@ -59,6 +59,10 @@ class StepTimes(C.Structure):
                 ("steps", C.c_int32), ("kernels_per_step", C.c_int32)]
 
 
+# (major << 16) | minor of include/reng_cuda.h that the structs below mirror
+ABI_VERSION = (0 << 16) | 2
+
+
 class DeviceInfo(C.Structure):
     _fields_ = [("ordinal", C.c_int32), ("name", C.c_char * 96), ("pci_bus_id", C.c_char * 32),
                 ("total_bytes", C.c_uint64), ("sm_count", C.c_int32), ("cc_major", C.c_int32),
@@ -111,6 +115,11 @@ def lib():
             f = getattr(L, name)
             f.argtypes = args
             f.restype = res
+        if L.reng_version() != ABI_VERSION:
+            # the structs above mirror one header; another layout would be
+            # read with the wrong sizes
+            raise OSError("%s has ABI version %#x, these bindings %#x: rebuild the library"
+                          % (path, L.reng_version(), ABI_VERSION))
         _lib = L
     return _lib
 
