@@ -120,3 +120,15 @@ def test_device_discovery_agrees_with_torch(reng_lib):
         assert rec["sm_count"] == p.multi_processor_count
         assert rec["compute_capability"] == (p.major, p.minor)
         assert rec["total_bytes"] == p.total_memory
+
+
+def test_bindings_refuse_a_library_of_another_abi_version(monkeypatch):
+    """A library built from another header would be handed structs of the
+    wrong size: the bindings stop at load time instead."""
+    from reng import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "ABI_VERSION", _lib.ABI_VERSION + 1)
+    with pytest.raises(OSError, match="ABI version"):
+        _lib.lib()
+    monkeypatch.undo()
+    assert _lib.lib().reng_version() == _lib.ABI_VERSION
