@@ -132,3 +132,36 @@ def test_bindings_refuse_a_library_of_another_abi_version(monkeypatch):
         _lib.lib()
     monkeypatch.undo()
     assert _lib.lib().reng_version() == _lib.ABI_VERSION
+
+
+def _header_struct_fields(text, name):
+    """Field names, in order, of `typedef struct name { ... } name;` in C."""
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), text, re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        for part in decl.split(","):
+            part = re.sub(r"\[.*?\]", "", part).strip()
+            names.append(re.findall(r"[A-Za-z_][A-Za-z0-9_]*", part)[-1])
+    return names
+
+
+def _stub_struct_fields(text, name):
+    body = re.search(r"pub struct %s \{(.*?)\}" % name, text, re.S).group(1)
+    return re.findall(r"pub ([a-z_0-9]+):", body)
+
+
+def test_integration_ffi_stub_structs_match_the_header():
+    """Every struct of the header appears in the Rust stub with the same
+    fields in the same order (the layout a #[repr(C)] mirror needs)."""
+    with open(os.path.join(ROOT, "include", "reng_cuda.h")) as f:
+        header = f.read()
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        stub = f.read()
+    structs = re.findall(r"typedef struct (reng_[a-z_]+) \{", header)
+    assert {"reng_model_desc", "reng_layer_weights", "reng_step_times", "reng_device_info"} <= set(structs)
+    for name in structs:
+        assert _stub_struct_fields(stub, name) == _header_struct_fields(header, name), name
