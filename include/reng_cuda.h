@@ -313,6 +313,17 @@ int reng_tp_unique_id(uint8_t out[128]);
  * NCCL.  The reference exchanges through hcclAllReduce (hccl.rs:646-651). */
 int reng_model_tp_exchange(reng_model *m, int *kind);
 
+/* Diagnostic: mean device time (ms) of one partial exchange of the decode
+ * step (the kind reng_model_tp_exchange names, for the model's B rows),
+ * launched `iters` times back to back after a few untimed launches.  Every
+ * rank of the model must call it at the same time with the same iters (the
+ * exchange waits on its peers).  It adds the partial buffer into the
+ * residual stream, so every slot is reset (position 0) afterwards.
+ * RENG_E_STATE for a model of world 1.  The reference measures its
+ * all-reduce floor the same way, in isolation (hccl.rs:1330, 1363;
+ * reng-ceiling strategy.rs:114-150). */
+int reng_model_time_exchange(reng_model *m, int iters, float *ms_out);
+
 /* Check of the exchange's failure path on one GPU: the peer all-reduce
  * kernel as rank 0 of two whose rank 1 never answers.  Its waits give up
  * after their bound (2 s) and it reports RENG_E_TIMEOUT, which this call

@@ -1281,6 +1281,42 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
     return sync_pos(m);
 }
 
+extern "C" int reng_model_time_exchange(reng_model* m, int iters, float* ms_out) {
+    TRY(check_model(m));
+    RENG_CHECK_ARG(ms_out != nullptr && iters >= 1, "reng_model_time_exchange: bad arguments");
+    if (m->world < 2) return fail(RENG_E_STATE, "reng_model_time_exchange: the model is not tensor-parallel");
+    CU(cudaSetDevice(m->dev));
+    CU(cudaStreamSynchronize(m->st));
+    const int M = m->B;
+    EventSet evs;
+    CU(evs.create(2));
+    // the exchange of M rows exactly as a decode step issues it after
+    // o_proj / down_proj (the peer all-reduce for M <= kMaxRows, otherwise
+    // NCCL + the residual kernel), on whatever partials the buffer holds
+    auto one = [&]() -> int {
+        if (tp_p2p(m, M)) {
+            CU(launch_tp_ar_residual(m, m->part, M, m->st));
+        } else {
+            CU(tp_allreduce(m, m->part, (size_t)M * m->hidden, m->st));
+            CU(launch_tp_residual(m, m->part, M, false, m->st));
+        }
+        return RENG_OK;
+    };
+    for (int i = 0; i < std::min(iters, 4); i++) TRY(one());
+    CU(cudaEventRecord(evs.e[0], m->st));
+    for (int i = 0; i < iters; i++) TRY(one());
+    CU(cudaEventRecord(evs.e[1], m->st));
+    CU(cudaEventSynchronize(evs.e[1]));
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, evs.e[0], evs.e[1]));
+    *ms_out = ms / (float)iters;
+    TRY(check_device_error(m));
+    // the residual stream took the stale partials: the cached prefix is no
+    // longer the one the slots' positions describe
+    for (int b = 0; b < m->B; b++) m->host_pos[b] = 0;
+    return sync_pos(m);
+}
+
 extern "C" int reng_model_trace_step(reng_model* m, uint64_t* out, int max_phases, int* n_phases) {
     TRY(check_model(m));
     RENG_CHECK_ARG(out != nullptr && n_phases != nullptr && max_phases >= 1, "reng_model_trace_step: bad arguments");

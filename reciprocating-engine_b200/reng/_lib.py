@@ -95,6 +95,7 @@ SIGNATURES = {
     "reng_model_device_bytes": ([_P, _P], C.c_int),
     "reng_model_last_times": ([_P, _P], C.c_int),
     "reng_model_time_kernels": ([_P, C.c_int, _P], C.c_int),
+    "reng_model_time_exchange": ([_P, C.c_int, _P], C.c_int),
     "reng_tp_unique_id": ([_P], C.c_int),
     "reng_model_trace_step": ([_P, _P, C.c_int, _P], C.c_int),
     "reng_gemm_bf16": ([_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, C.c_int, _P, C.c_int], C.c_int),
@@ -111,15 +112,20 @@ def lib():
         if not os.path.exists(path):
             raise OSError("libreng_cuda.so is not built (%s); run reng.build.build()" % path)
         L = C.CDLL(path, mode=C.RTLD_GLOBAL)
-        for name, (args, res) in SIGNATURES.items():
-            f = getattr(L, name)
-            f.argtypes = args
-            f.restype = res
+        # the version first: a library of another version may lack symbols
+        # these bindings name, and its structs may have another layout
+        L.reng_version.argtypes = []
+        L.reng_version.restype = C.c_int
         if L.reng_version() != ABI_VERSION:
-            # the structs above mirror one header; another layout would be
-            # read with the wrong sizes
             raise OSError("%s has ABI version %#x, these bindings %#x: rebuild the library"
                           % (path, L.reng_version(), ABI_VERSION))
+        for name, (args, res) in SIGNATURES.items():
+            try:
+                f = getattr(L, name)
+            except AttributeError:
+                raise OSError("%s does not export %s: rebuild the library" % (path, name)) from None
+            f.argtypes = args
+            f.restype = res
         _lib = L
     return _lib
 

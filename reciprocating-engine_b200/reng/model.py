@@ -249,6 +249,13 @@ class Engine:
         return dict(zip(("qkv", "attn", "o_proj", "gate_up", "down", "lm_head"),
                         (float(x) for x in out)))
 
+    def time_exchange(self, iters=64):
+        """Mean ms of one partial exchange (tensor-parallel models; every
+        rank calls it at the same time); resets every slot afterwards."""
+        out = C.c_float(0.0)
+        _lib.call("reng_model_time_exchange", self.h, iters, C.byref(out))
+        return float(out.value)
+
     def trace_step(self):
         """Phase timeline of one decode step of the persistent step kernel:
         a list of (name, start_us, first_done_us, last_done_us, staged_us,

@@ -52,12 +52,12 @@ def check_agreement(ids, dist, group=None):
 class TpGenerator:
     """B sequences decoded tensor-parallel (reng-model TpGenerator)."""
 
-    def __init__(self, w, cfg, rank, world, nccl_id, batch=1, capacity=1024, device=None):
+    def __init__(self, w, cfg, rank, world, nccl_id, batch=1, capacity=1024, device=None, fp8=None):
         cfg.shard(rank, world)  # the reference's divisibility rule, as a ValueError
         self.rank, self.world = rank, world
         self.engine = Engine(cfg, w, batch=batch, capacity=capacity,
                              device=rank if device is None else device,
-                             tp_rank=rank, tp_world=world, nccl_id=nccl_id)
+                             tp_rank=rank, tp_world=world, nccl_id=nccl_id, fp8=fp8)
 
     def batch(self):
         return self.engine.batch

@@ -25,10 +25,14 @@ def test_header_declares_the_boundary():
         assert must in names
 
 
+FFI_STUB = os.path.join(ROOT, "include", "reng_cuda_ffi.rs")
+
+
 def test_integration_ffi_stub_declares_every_function():
-    """The Rust FFI stub a maintainer would add binds
-    exactly the functions the header declares."""
-    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+    """The Rust FFI binding a maintainer adds to the reference
+    (include/reng_cuda_ffi.rs) binds exactly the functions the header
+    declares."""
+    with open(FFI_STUB) as f:
         stub = set(re.findall(r"pub fn (reng_[a-z0-9_]+)\(", f.read()))
     assert stub == set(declared_functions()), sorted(stub ^ set(declared_functions()))
 
@@ -159,7 +163,7 @@ def test_integration_ffi_stub_structs_match_the_header():
     fields in the same order (the layout a #[repr(C)] mirror needs)."""
     with open(os.path.join(ROOT, "include", "reng_cuda.h")) as f:
         header = f.read()
-    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+    with open(FFI_STUB) as f:
         stub = f.read()
     structs = re.findall(r"typedef struct (reng_[a-z_]+) \{", header)
     assert {"reng_model_desc", "reng_layer_weights", "reng_step_times", "reng_device_info"} <= set(structs)

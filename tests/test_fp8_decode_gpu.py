@@ -17,9 +17,12 @@ from test_decode_gpu import check_greedy, check_rows, cosine, oracle_for, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-def dequantized(w):
+def dequantized(w, windows=1):
     """The weights dict with every projection replaced by its E4M3 per-channel
-    round trip in bf16, as the oracle quantizer computes it."""
+    round trip in bf16, as the oracle quantizer computes it.  windows > 1:
+    o_proj and down_proj are quantized per column window, as each rank of a
+    tensor-parallel model quantizes its own window (one scale per row and
+    window); the row-split matrices keep whole-row scales."""
     import oracle
     from reng.synth import f32_to_bf16_bits
     from reng.weights import to_host
@@ -28,9 +31,14 @@ def dequantized(w):
     for lw in h["layers"]:
         d = dict(lw)
         for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
-            rows, cols = lw[k].shape
-            codes, scales, _ = oracle.quantize(lw[k], rows, cols, oracle.E4M3, oracle.PCS)
-            d[k] = f32_to_bf16_bits(oracle.dequantize(codes, scales, rows, cols, oracle.E4M3)).reshape(rows, cols)
+            parts = []
+            for win in np.split(lw[k], windows if k in ("wo", "wd") else 1, axis=1):
+                win = np.ascontiguousarray(win)
+                rows, cols = win.shape
+                codes, scales, _ = oracle.quantize(win, rows, cols, oracle.E4M3, oracle.PCS)
+                parts.append(f32_to_bf16_bits(oracle.dequantize(codes, scales, rows, cols, oracle.E4M3))
+                             .reshape(rows, cols))
+            d[k] = np.concatenate(parts, axis=1)
         out["layers"].append(d)
     return out
 
