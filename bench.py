@@ -595,6 +595,81 @@ def fp8_quant_bench(dev, iters=4):
             "gbs": b / (ms / 1e3) / 1e9, "frac": b / (ms / 1e3) / 1e9 / peak, "peak_kind": kind}
 
 
+def trace_summary(rows):
+    """Mean per phase kind of (duration, arrival spread, barrier, first and
+    last arrival), microseconds, of one persistent-step timeline."""
+    import numpy as np
+    kinds = {}
+    for i, (name, start, first, last, staged, loop) in enumerate(rows):
+        k = "".join(ch for ch in name if not ch.isdigit())
+        nxt = rows[i + 1][1] if i + 1 < len(rows) else last
+        kinds.setdefault(k, []).append((nxt - start, last - first, nxt - last, first - start, last - start,
+                                        staged - start if staged else 0.0, loop - start if loop else 0.0))
+    out = {}
+    for k, v in kinds.items():
+        a = np.array(v).mean(0)
+        out[k] = {"n": len(v), "us": round(a[0], 2), "spread_us": round(a[1], 2), "barrier_us": round(a[2], 2),
+                  "first_done_us": round(a[3], 2), "last_done_us": round(a[4], 2),
+                  "cta0_staged_us": round(a[5], 2), "cta0_loop_done_us": round(a[6], 2)}
+    return out
+
+
+def run_profile(args, cfg):
+    """The small case of the ncu captures (one GPU, a few GB on the device):
+    a layer-truncated model of the workload's widths (`--layers`), then
+      * each kernel kind alone on the model's stream `--iters` times,
+        cycling over the layers (reng_model_time_kernels; not with
+        --no-kinds),
+      * with --decode-steps N: a 16-token prompt in every slot and N greedy
+        steps through the step graph (device ms per step),
+      * with --trace: the persistent step kernel's phase timeline,
+      * with --quant N: N config-0 FP8 quantizations (bf16 [4096, 4096] ->
+        E4M3 per-channel) on device buffers.
+    Prints one JSON line of device times; no bench line."""
+    import torch
+    from reng import fp8 as f
+    from reng.model import Engine
+    from reng.synth import fp8_config0_matrix, prompt_ids
+    from reng.weights import random_weights
+    torch.cuda.set_device(0)
+    rep = {"model": args.model, "layers": args.layers, "batch": args.batch, "weights": args.weights}
+    if args.quant > 0:
+        import numpy as np
+        w = torch.from_numpy(fp8_config0_matrix(4096, 4096, seed=0).view(np.int16)).cuda()
+        codes = torch.empty((4096, 4096), dtype=torch.uint8, device="cuda")
+        scales = torch.empty(4096, dtype=torch.float32, device="cuda")
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        f.quantize_device(w, 4096, 4096, 0, 0, codes=codes, scales=scales)
+        e0.record()
+        for _ in range(args.quant):
+            f.quantize_device(w, 4096, 4096, 0, 0, codes=codes, scales=scales)
+        e1.record()
+        torch.cuda.synchronize()
+        rep["quant_us"] = round(e0.elapsed_time(e1) * 1e3 / args.quant, 2)
+        print(json.dumps(rep))
+        return
+    cfg.num_hidden_layers = args.layers
+    w = random_weights(cfg, seed=0, device="cuda", layers=args.layers)
+    fp8 = ("e4m3", "pcs") if args.weights == "fp8" else None
+    e = Engine(cfg, w, batch=args.batch, capacity=args.capacity, fp8=fp8)
+    del w
+    if args.kinds:
+        rep["kernel_us"] = {k: round(v * 1e3, 2) for k, v in e.time_kernels(args.iters).items()}
+    if args.decode_steps > 0 or args.trace:
+        p = prompt_ids(16, cfg.vocab_size, seed=1)
+        seeds = [e.prefill(b, p)[0] for b in range(args.batch)]
+        e.decode(seeds, max(1, args.decode_steps))
+        t = e.last_times()
+        rep["decode"] = {"steps": t.steps, "ms_per_step": round(t.device_ms / t.steps, 4),
+                         "kernels_per_step": t.kernels_per_step}
+        if args.trace:
+            rows = e.trace_step()
+            rep["trace"] = {"step_us": round(rows[-1][3], 1), "phases": trace_summary(rows)}
+    print(json.dumps(rep))
+    e.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -617,13 +692,24 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-fp8", dest="fp8", action="store_false",
                     help="skip the FP8 quantizer line")
+    pg = ap.add_argument_group("profiling (--profile: the small case of the ncu captures, no bench line)")
+    pg.add_argument("--profile", action="store_true")
+    pg.add_argument("--layers", type=int, default=2, help="depth of the profiled model")
+    pg.add_argument("--iters", type=int, default=4, help="launches per kernel kind")
+    pg.add_argument("--capacity", type=int, default=256)
+    pg.add_argument("--decode-steps", type=int, default=0)
+    pg.add_argument("--trace", action="store_true")
+    pg.add_argument("--no-kinds", dest="kinds", action="store_false")
+    pg.add_argument("--quant", type=int, default=0, help="FP8 quantizations of the config-0 matrix")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.extras is None:
         args.extras = "b8,b64,fp8" if args.model == "llama-3.1-8b" and args.batch == 1 else ""
     from reng.config import SHAPES
     cfg = SHAPES[args.model]()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args, cfg)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_ours(args, cfg)

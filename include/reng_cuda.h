@@ -106,7 +106,11 @@ int reng_fp8_quantize(const uint16_t *w, int64_t rows, int64_t cols, int fmt, in
  * Limits: rows <= 65,536 and rows * cols <= 2,097,152; larger matrices are
  * refused with RENG_E_INVAL.  Every GPU that loads the library holds the
  * 6.25 MiB array until exit.  The first call on a device looks up the
- * array's device address; make that first call before any stream capture.
+ * array's device address and keeps it for the process; make that first call
+ * before any stream capture.  The kept address belongs to the device's
+ * primary context: after cudaDeviceReset on that device, or when calling
+ * from another context on it, the array may have moved and this entry must
+ * not be used.
  * All calls on a device share the array: calls that overlap on the GPU (two
  * streams, two host threads) race and must be serialised by the caller.
  * The call returns after its copies back to the host are complete.
@@ -314,8 +318,9 @@ int reng_tp_unique_id(uint8_t out[128]);
 int reng_model_tp_exchange(reng_model *m, int *kind);
 
 /* Diagnostic: mean device time (ms) of one partial exchange of the decode
- * step (the kind reng_model_tp_exchange names, for the model's B rows),
- * launched `iters` times back to back after a few untimed launches.  Every
+ * step (the kind reng_model_tp_exchange names, for the model's B rows):
+ * `iters` exchanges captured back to back in one CUDA graph, as the step
+ * graph holds them, replayed once untimed and once under CUDA events.  Every
  * rank of the model must call it at the same time with the same iters (the
  * exchange waits on its peers).  It adds the partial buffer into the
  * residual stream, so every slot is reset (position 0) afterwards.

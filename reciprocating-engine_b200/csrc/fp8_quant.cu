@@ -343,29 +343,29 @@ int fp8_quantize_device(const uint16_t* w, int64_t rows, int64_t cols, int fmt, 
 
 using namespace reng;
 
-static int check_quant_args(const uint16_t* w, int64_t rows, int64_t cols, int fmt, int scaling,
-                            float backoff, uint8_t* codes, float* scales, uint32_t* exp_bias,
+// The argument checks of both quantize entry points; `who` names the entry
+// the caller used, so reng_last_error() reports that one.
+static int check_quant_args(const char* who, const uint16_t* w, int64_t rows, int64_t cols, int fmt,
+                            int scaling, float backoff, uint8_t* codes, float* scales, uint32_t* exp_bias,
                             int mem) {
-    RENG_CHECK_ARG(rows > 0 && cols > 0, "reng_fp8_quantize: empty shape " + std::to_string(rows) +
-                                             " x " + std::to_string(cols));
+    const std::string f = std::string(who) + ": ";
+    RENG_CHECK_ARG(rows > 0 && cols > 0, f + "empty shape " + std::to_string(rows) + " x " + std::to_string(cols));
     RENG_CHECK_ARG(backoff > 0.0f && std::isfinite(backoff),
-                   "reng_fp8_quantize: backoff " + std::to_string(backoff) +
-                       " is not positive and finite");
-    RENG_CHECK_ARG(fmt == RENG_FP8_E4M3 || fmt == RENG_FP8_E5M2, "reng_fp8_quantize: unknown format");
-    RENG_CHECK_ARG(scaling >= RENG_SCALING_PCS && scaling <= RENG_SCALING_UNIT,
-                   "reng_fp8_quantize: unknown scaling");
-    RENG_CHECK_ARG(w && codes && scales && exp_bias, "reng_fp8_quantize: NULL buffer");
-    RENG_CHECK_ARG(mem == RENG_MEM_DEVICE || mem == RENG_MEM_HOST, "reng_fp8_quantize: bad mem");
-    RENG_CHECK_ARG(rows <= (int64_t)1 << 40 && cols <= (int64_t)1 << 40 &&
-                       rows <= ((int64_t)1 << 62) / cols,
-                   "reng_fp8_quantize: shape overflows");
+                   f + "backoff " + std::to_string(backoff) + " is not positive and finite");
+    RENG_CHECK_ARG(fmt == RENG_FP8_E4M3 || fmt == RENG_FP8_E5M2, f + "unknown format");
+    RENG_CHECK_ARG(scaling >= RENG_SCALING_PCS && scaling <= RENG_SCALING_UNIT, f + "unknown scaling");
+    RENG_CHECK_ARG(w && codes && scales && exp_bias, f + "NULL buffer");
+    RENG_CHECK_ARG(mem == RENG_MEM_DEVICE || mem == RENG_MEM_HOST, f + "bad mem");
+    RENG_CHECK_ARG(rows <= (int64_t)1 << 40 && cols <= (int64_t)1 << 40 && rows <= ((int64_t)1 << 62) / cols,
+                   f + "shape overflows");
     return RENG_OK;
 }
 
 extern "C" int reng_fp8_quantize(const uint16_t* w, int64_t rows, int64_t cols, int fmt,
                                  int scaling, float backoff, uint8_t* codes, float* scales,
                                  uint32_t* exp_bias, int mem, void* stream) {
-    int rc = check_quant_args(w, rows, cols, fmt, scaling, backoff, codes, scales, exp_bias, mem);
+    int rc = check_quant_args("reng_fp8_quantize", w, rows, cols, fmt, scaling, backoff, codes, scales,
+                              exp_bias, mem);
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t nel = (size_t)rows * (size_t)cols;
@@ -480,7 +480,8 @@ int noalloc_scratch(int device, unsigned char** out) {
 extern "C" int reng_fp8_quantize_noalloc(const uint16_t* w, int64_t rows, int64_t cols, int fmt,
                                          int scaling, float backoff, uint8_t* codes, float* scales,
                                          uint32_t* exp_bias, void* stream) {
-    int rc = check_quant_args(w, rows, cols, fmt, scaling, backoff, codes, scales, exp_bias, RENG_MEM_HOST);
+    int rc = check_quant_args("reng_fp8_quantize_noalloc", w, rows, cols, fmt, scaling, backoff, codes,
+                              scales, exp_bias, RENG_MEM_HOST);
     if (rc) return rc;
     if (rows > kNoAllocMaxRows || rows * cols > kNoAllocMaxElems)
         return fail(RENG_E_INVAL, "reng_fp8_quantize_noalloc: " + std::to_string(rows) + " x " +

@@ -1288,11 +1288,11 @@ extern "C" int reng_model_time_exchange(reng_model* m, int iters, float* ms_out)
     CU(cudaSetDevice(m->dev));
     CU(cudaStreamSynchronize(m->st));
     const int M = m->B;
-    EventSet evs;
-    CU(evs.create(2));
     // the exchange of M rows exactly as a decode step issues it after
     // o_proj / down_proj (the peer all-reduce for M <= kMaxRows, otherwise
-    // NCCL + the residual kernel), on whatever partials the buffer holds
+    // NCCL + the residual kernel), on whatever partials the buffer holds;
+    // `iters` of them captured in one graph as the step graph holds them,
+    // so the time is the device's, not the host's launch rate
     auto one = [&]() -> int {
         if (tp_p2p(m, M)) {
             CU(launch_tp_ar_residual(m, m->part, M, m->st));
@@ -1302,9 +1302,29 @@ extern "C" int reng_model_time_exchange(reng_model* m, int iters, float* ms_out)
         }
         return RENG_OK;
     };
-    for (int i = 0; i < std::min(iters, 4); i++) TRY(one());
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = RENG_OK;
+    for (int i = 0; i < iters && rc == RENG_OK; i++) rc = one();
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("exchange capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(RENG_E_CUDA, std::string("exchange instantiate: ") + cudaGetErrorString(e));
+    struct Exec {
+        cudaGraphExec_t x;
+        ~Exec() { cudaGraphExecDestroy(x); }
+    } hold{ge};
+    EventSet evs;
+    CU(evs.create(2));
+    CU(cudaGraphLaunch(ge, m->st));  // untimed: every rank's first replay meets the others
     CU(cudaEventRecord(evs.e[0], m->st));
-    for (int i = 0; i < iters; i++) TRY(one());
+    CU(cudaGraphLaunch(ge, m->st));
     CU(cudaEventRecord(evs.e[1], m->st));
     CU(cudaEventSynchronize(evs.e[1]));
     float ms = 0.f;

@@ -178,7 +178,7 @@ def row_errors(w, q):
     (row_errors, lib.rs:347-386); an all-zero row reports 0.0 for both."""
     w = np.asarray(w, np.uint16).reshape(-1)
     if w.size != q.rows * q.cols:
-        raise ValueError("weight length against the shape")
+        raise ValueError("the weights hold %d values, not rows x cols" % w.size)
     codes = np.asarray(q.codes, np.uint8).reshape(q.rows, q.cols)
     w = w.reshape(q.rows, q.cols)
     return [_row_error(w[r], codes[r], q.scales[r], q.format) for r in range(q.rows)]
@@ -189,7 +189,7 @@ def sample_row_errors(w, q, max_rows):
     ceil(rows / n)-th from row 0 (sample_row_errors, lib.rs:388-430)."""
     w = np.asarray(w, np.uint16).reshape(-1)
     if w.size != q.rows * q.cols:
-        raise ValueError("weight length against the shape")
+        raise ValueError("the weights hold %d values, not rows x cols" % w.size)
     if max_rows <= 0:
         raise ValueError("max_rows must be positive")
     n = min(max_rows, q.rows)
@@ -205,7 +205,7 @@ def row_absmax(w, rows, cols):
     from .synth import bf16_bits_to_f32
     w = np.asarray(w, np.uint16).reshape(-1)
     if w.size != rows * cols:
-        raise ValueError("weight length against the shape")
+        raise ValueError("the weights hold %d values, not rows x cols" % w.size)
     a = np.abs(bf16_bits_to_f32(w).reshape(rows, cols))
     a = np.where(np.isnan(a), np.float32(0.0), a)
     return a.max(axis=1).astype(np.float32)
@@ -227,7 +227,7 @@ def _check(w_size, rows, cols, backoff):
     if rows <= 0 or cols <= 0:
         raise ValueError("empty shape %d x %d" % (rows, cols))
     if w_size != rows * cols:
-        raise ValueError("weight length %d against the shape %d x %d" % (w_size, rows, cols))
+        raise ValueError("the weights hold %d values, not %d x %d" % (w_size, rows, cols))
     if not (backoff > 0.0 and np.isfinite(backoff)):
         raise ValueError("backoff %r is not positive and finite" % (backoff,))
 
@@ -256,7 +256,7 @@ def quantize_device(w, rows, cols, fmt, scaling, backoff=DEFAULT_BACKOFF, codes=
     Returns (codes uint8 [rows, cols], scales f32 [rows], exp_bias)."""
     import torch
     if w.numel() != rows * cols:
-        raise ValueError("weight length against the shape")
+        raise ValueError("the weights hold %d values, not rows x cols" % w.numel())
     _check(w.numel(), rows, cols, backoff)
     dev = w.device
     if codes is None:

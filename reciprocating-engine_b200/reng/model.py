@@ -36,25 +36,57 @@ def _is_device(w):
     return not isinstance(x, np.ndarray)
 
 
+class Fp8Config(tuple):
+    """(format, scheme) of the FP8 switch, with its backoff as an attribute
+    (reng-model's Fp8Config, lib.rs:1693-1721); equal to the plain pair."""
+
+    def __new__(cls, fmt="e4m3", scheme="pcs", backoff=1.0):
+        t = super().__new__(cls, (fmt, scheme))
+        t.backoff = backoff
+        return t
+
+    def __str__(self):
+        return "%s/%s backoff %s" % (self[0], self[1], self.backoff)
+
+
 def fp8_switch(value, flag=False):
-    """RENG_FP8 / --fp8 grammar of reng-model (lib.rs:1693-1782): unset/""/"0"/
-    "off" -> None; "1"/"on"/"e4m3" -> (E4M3, pcs); "<fmt>:<scheme>" otherwise.
-    A bad value raises ValueError, never a silent bf16 run."""
+    """The FP8 switch of reng-model (fp8_switch, lib.rs:1723-1782): `value` is
+    RENG_FP8 (None when unset) and `flag` whether --fp8 was given.  Unset:
+    the flag decides (the defaults, E4M3 per-channel, backoff 1).  An empty
+    value, 0, off, false or no turns it off even with the flag; 1, on, true,
+    yes mean the defaults; anything else is a list of settings separated by
+    ':' or ',', each a format (e4m3, e5m2), a scale scheme (pcs, hw, unit)
+    or backoff=<f32> in (0, 1].  A word that is none of these raises
+    ValueError, so a typo never runs as bf16."""
+    import re
     from .fp8 import Fp8Format, Scaling
     if value is None:
-        return ("e4m3", "pcs") if flag else None
+        return Fp8Config() if flag else None
     v = value.strip().lower()
     if v in ("", "0", "off", "false", "no"):
-        return ("e4m3", "pcs") if flag else None
+        return None
     if v in ("1", "on", "true", "yes"):
-        return ("e4m3", "pcs")
-    fmt, _, sch = v.partition(":")
-    if Fp8Format.from_name(fmt) is None:
-        raise ValueError("RENG_FP8=%r: unknown format %r" % (value, fmt))
-    if sch and Scaling.from_name(sch) is None:
-        raise ValueError("RENG_FP8=%r: unknown scheme %r" % (value, sch))
-    return (Fp8Format.from_name(fmt).short_name,
-            Scaling.from_name(sch).short_name if sch else "pcs")
+        return Fp8Config()
+    fmt, sch, backoff = "e4m3", "pcs", 1.0
+    for word in re.split("[:,]", v):
+        word = word.strip()
+        if not word:
+            continue
+        if Fp8Format.from_name(word) is not None:
+            fmt = Fp8Format.from_name(word).short_name
+        elif Scaling.from_name(word) is not None:
+            sch = Scaling.from_name(word).short_name
+        elif word.startswith("backoff="):
+            try:
+                backoff = float(np.float32(word[len("backoff="):]))
+            except ValueError:
+                raise ValueError("RENG_FP8: %r is not a number" % word) from None
+            if not 0.0 < backoff <= 1.0:
+                raise ValueError("RENG_FP8: backoff %s must lie in (0, 1]" % backoff)
+        else:
+            raise ValueError("RENG_FP8: %r is neither a format (e4m3, e5m2), a scale scheme "
+                             "(pcs, hw, unit) nor backoff=<f32>" % word)
+    return Fp8Config(fmt, sch, backoff)
 
 
 def _scaled_table(t, s):

@@ -25,7 +25,7 @@ def rope_spec(rotary_dim, theta, scaling=None, seq_len=0):
 
     def orig():
         if scaling.original_max_position_embeddings is None:
-            raise ValueError("rope_scaling.original_max_position_embeddings")
+            raise ValueError("this rope scaling needs original_max_position_embeddings in rope_scaling")
         return F(scaling.original_max_position_embeddings)
 
     def factor_or_ratio():
@@ -82,7 +82,7 @@ def rope_spec(rotary_dim, theta, scaling=None, seq_len=0):
             inv[i] = F(F(F(f / factor) * ramp) + F(f * F(F(1.0) - ramp)))
     elif rtype == "longrope":
         if scaling.original_max_position_embeddings is None:
-            raise ValueError("rope_scaling.original_max_position_embeddings")
+            raise ValueError("this rope scaling needs original_max_position_embeddings in rope_scaling")
         olen = int(scaling.original_max_position_embeddings)
         factor = factor_or_ratio()
         if scaling.attention_factor is not None:
@@ -93,7 +93,7 @@ def rope_spec(rotary_dim, theta, scaling=None, seq_len=0):
             af = F(np.sqrt(F(F(1.0) + F(F(np.log(factor)) / F(np.log(F(olen)))))))
         ext = scaling.long_factor if seq_len > olen else scaling.short_factor
         if ext is None or len(ext) != half:
-            raise ValueError("rope_scaling factors: %s entries for %d rotary pairs"
+            raise ValueError("longrope: the factor list has %s values but the head rotates %d pairs"
                              % (None if ext is None else len(ext), half))
         inv = np.array([F(inv[i] / F(ext[i])) for i in range(half)], F)
     return inv, float(af)

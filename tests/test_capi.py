@@ -68,6 +68,10 @@ def test_quantize_refuses_bad_shapes_without_a_device(reng_lib):
     assert rc == reng_lib.RENG_E_INVAL
     with pytest.raises(reng_lib.RengError):
         reng_lib.check(rc)
+    # the allocation-free entry runs the same checks and names itself
+    rc = L.reng_fp8_quantize_noalloc(p(w), 0, 4, 0, 0, 1.0, p(codes), p(scales), C.byref(bias), None)
+    assert rc == reng_lib.RENG_E_INVAL
+    assert L.reng_last_error().startswith(b"reng_fp8_quantize_noalloc: empty shape")
 
 
 def test_model_create_refuses_bad_descriptors_without_a_device(reng_lib):

@@ -150,7 +150,15 @@ def test_fp8_switch_grammar():
     assert fp8_switch("e5m2:hw") == ("e5m2", "hw")
     assert fp8_switch("E4M3:unit") == ("e4m3", "unit")
     assert fp8_switch(None, flag=True) == ("e4m3", "pcs")
-    for bad in ("fp4", "e4m3:bogus", "e4m3:pcs:x"):
+    # an explicit off value wins over the flag (a wrapper's --fp8 can be
+    # turned off from the environment)
+    assert fp8_switch("off", flag=True) is None and fp8_switch("", flag=True) is None
+    # settings in any order, ':' or ',' separated, with a backoff in (0, 1]
+    c = fp8_switch("hw,e5m2")
+    assert c == ("e5m2", "hw") and c.backoff == 1.0
+    c = fp8_switch("pcs,backoff=0.5")
+    assert c == ("e4m3", "pcs") and c.backoff == 0.5
+    for bad in ("fp4", "e4m3:bogus", "e4m3:pcs:x", "backoff=2", "backoff=0", "backoff=x"):
         with pytest.raises(ValueError):
             fp8_switch(bad)
 
