@@ -363,9 +363,11 @@ def decode_measure(eng, args, B, prompt, dev, ws, rank, local, with_e2e=True, wi
     if clocks:
         clocks.start()
     with torch.cuda.stream(st):
+        torch.cuda.nvtx.range_push("decode_timed")  # the range launch-list captures select
         e0.record(st)
         eng.decode_device(seeds_d, args.steps, out_d, st.cuda_stream)
         e1.record(st)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop() if clocks else None
     if ws > 1:
