@@ -7,38 +7,35 @@
 
 namespace reng {
 
-constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
-constexpr int kGemmMaxSplits = 8;     // K splits of a super-tile (a portable cluster)
-constexpr int kGemmCntMax = 1024;     // super-tiles of a split launch (arrival counts)
+constexpr int kGemmRowsPerCta = 128;  // weight rows per MMA tile (the MMA's M)
+constexpr int kGemmCntMax = 4096;     // super-tiles of a launch (arrival counts)
 
 struct GemmArgs {
     GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
     const uint8_t* w;         // packed bf16 blocks [tiles16][kc]
     int tiles16;              // 16-row tiles of the matrix
     int kc;                   // 64-k chunks
-    int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
-    int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
+    int super_tiles;          // ceil(tiles16 / 8): 128-row MMA tiles
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
     int stages;               // pipeline stages (2..8)
-    // ks > 1 without a cluster: f32 partials [super_tiles][ks][128][N] and
-    // one arrival count per super-tile (0 between launches); null: the
-    // splits form a cluster and add their partials over shared memory
-    float* gpart;
-    int* gcnt;
+    int grid;                 // persistent CTAs, each an equal share of the super_tiles x kc chunks
+    float* gpart;             // split super-tiles' f32 partials [2 * grid][N / 16][128][16]
+    int* gcnt;                // arrivals per super-tile (0 between launches)
 };
 
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as
 // {64 k, n rows} boxes with the 128-byte swizzle; k >= K reads zeros.
 int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out);
 size_t gemm_smem_bytes(int n, int stages);
-// Pipeline stages for MMA width n: 4 with two CTAs per SM, else as many as
-// fit in about 200 KB.
-int gemm_pick_stages(int n, bool one_per_sm, int epi);
+// Pipeline stages for MMA width n: as many as fit about 200 KB.
+int gemm_pick_stages(int n);
 // Raise the dynamic shared-memory limit of every GEMM instantiation (call
 // once per device before capture).
 cudaError_t gemm_prepare();
-// K splits and pipeline stages of a launch over super_tiles x kc blocks.
-void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks, int* stages, bool* gsplit);
+// Persistent grid (one CTA per SM, at most one per chunk) and stages.
+void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages);
+// Floats of split-tile scratch a launch of `grid` CTAs at width n needs.
+size_t gemm_scratch_floats(int grid, int n);
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps,

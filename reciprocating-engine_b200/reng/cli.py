@@ -663,7 +663,7 @@ def bench_main(argv=None):
            entry("prefill % of ceiling (b1)", "%", pre_pct, "%s bound" % c_pre.bottleneck),
            entry("decode tok/s (b%d)" % B, "tok/s", decode_tps,
                  "ctx ~%d; mean step %.2f ms; ceiling %.0f tok/s" % (ctx, step_ms, c_dec.tokens_per_s)),
-           entry("decode % of ceiling (b%d)" % B, "%", dec_pct, "%s bound" % c_dec.bottleneck)]
+           entry("decode %% of ceiling (b%d)" % B, "%", dec_pct, "%s bound" % c_dec.bottleneck)]
     write_json(a["out"], doc, pretty=True)
     print("wrote %s" % a["out"])
     return 0
