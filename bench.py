@@ -621,7 +621,7 @@ def run_profile(args, cfg):
     a layer-truncated model of the workload's widths (`--layers`), then
       * each kernel kind alone on the model's stream `--iters` times,
         cycling over the layers (reng_model_time_kernels; not with
-        --no-kinds),
+        --no-kinds), after `--ctx` prompt tokens in every slot,
       * with --decode-steps N: a 16-token prompt in every slot and N greedy
         steps through the step graph (device ms per step),
       * with --trace: the persistent step kernel's phase timeline,
@@ -656,6 +656,11 @@ def run_profile(args, cfg):
     fp8 = ("e4m3", "pcs") if args.weights == "fp8" else None
     e = Engine(cfg, w, batch=args.batch, capacity=args.capacity, fp8=fp8)
     del w
+    if args.ctx > 0:  # every slot holds a prompt, so attention reads a real context
+        p = prompt_ids(args.ctx, cfg.vocab_size, seed=2)
+        for b in range(args.batch):
+            e.prefill(b, p)
+        rep["ctx"] = args.ctx
     if args.kinds:
         rep["kernel_us"] = {k: round(v * 1e3, 2) for k, v in e.time_kernels(args.iters).items()}
     if args.decode_steps > 0 or args.trace:
@@ -699,6 +704,7 @@ def main():
     pg.add_argument("--layers", type=int, default=2, help="depth of the profiled model")
     pg.add_argument("--iters", type=int, default=4, help="launches per kernel kind")
     pg.add_argument("--capacity", type=int, default=256)
+    pg.add_argument("--ctx", type=int, default=0, help="prompt tokens prefilled in every slot before the kernel timing")
     pg.add_argument("--decode-steps", type=int, default=0)
     pg.add_argument("--trace", action="store_true")
     pg.add_argument("--no-kinds", dest="kinds", action="store_false")
