@@ -604,9 +604,16 @@ size_t gemm_smem_bytes(int n, int stages) { return (size_t)stages * (kStageA + (
 
 int gemm_pick_stages(int n) {
     // One CTA per SM: as many stages as fit the ~200 KB budget (8 at N <= 64:
-    // 128 KB of weights in flight per SM; 4 at N = 256).
-    const int s = (int)((unsigned)kGemmStageBudget / (kStageA + (unsigned)n * 128u));
-    return s < 2 ? 2 : (s > kGemmMaxStages ? kGemmMaxStages : s);
+    // 128 KB of weights in flight per SM; 4 at N = 256).  RENG_GEMM_STAGES
+    // caps it (a tuning knob).
+    static const int cap = [] {
+        const char* v = getenv("RENG_GEMM_STAGES");
+        const int x = v ? atoi(v) : 0;
+        return x >= 2 && x <= kGemmMaxStages ? x : kGemmMaxStages;
+    }();
+    int s = (int)((unsigned)kGemmStageBudget / (kStageA + (unsigned)n * 128u));
+    if (s > cap) s = cap;
+    return s < 2 ? 2 : s;
 }
 
 void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages) {
