@@ -86,6 +86,22 @@ __device__ __forceinline__ void tensor_g2s(uint32_t dst, const CUtensorMap* map,
         "l"(map), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+__device__ __forceinline__ void tensor_g2s_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                              uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tensor_g2s_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                              uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+        : "memory");
+}
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, SBO 1024 B.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
     uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
@@ -283,6 +299,25 @@ __device__ __forceinline__ int sk_slot(int c, int S, int kc, long long T, long l
     return (int)(sk_start(c, T, G) / kc) == S ? 2 * c : 2 * c + 1;
 }
 
+// The copy units of a CTA's share: runs of up to C consecutive chunks of
+// one segment (one super-tile), each fetched by one weight copy and one
+// activation copy into one pipeline stage.
+struct SkUnits {
+    long long x, x0, x1;
+    int kc, C;
+    __device__ bool next(int& S, int& c0, int& cnt, bool& first, bool& last) {
+        if (x >= x1) return false;
+        S = (int)(x / kc);
+        c0 = (int)(x % kc);
+        const long long seg0 = max(x0, (long long)S * kc), seg1 = min(x1, (long long)(S + 1) * kc);
+        cnt = (int)min((long long)C, seg1 - x);
+        first = x == seg0;
+        last = x + cnt == seg1;
+        x += cnt;
+        return true;
+    }
+};
+
 // LM-head argmax of one finished super-tile: the 4 epilogue warps' best per
 // row into the rows' running maxima; the CTA that finishes the launch's last
 // super-tile reads the keys, swaps them with the other ranks (vocabulary
@@ -339,7 +374,8 @@ __device__ __forceinline__ void sk_logits_tile_done(const GemmArgs& g, float* am
 // CTAs to arrive adds them in K order (deterministic: the same sum whoever
 // arrives last) and runs the epilogue.  Every mbarrier wait is bounded.
 template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_constant__ CUtensorMap tmap_x, GemmArgs g) {
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_constant__ CUtensorMap tmap_x,
+                                                             const __grid_constant__ CUtensorMap tmap_w, GemmArgs g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], acc_full[2],
         acc_empty[2], drain;
@@ -352,8 +388,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
     const int c = blockIdx.x;
     const long long G = gridDim.x, T = (long long)g.super_tiles * g.kc;
     const long long x0 = sk_start(c, T, G), x1 = sk_start(c + 1, T, G);
-    const int kc = g.kc, N = g.N, SG = g.stages;
-    const uint32_t stage_bytes = kStageA + (uint32_t)N * 128u;
+    const int kc = g.kc, N = g.N, SG = g.stages, C = g.C;
+    const uint32_t stage_bytes = (uint32_t)C * (kStageA + (uint32_t)N * 128u);
+    const uint32_t b_off = (uint32_t)C * kStageA;  // the stage's activation tiles follow its C weight tiles
     const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem_raw) + 1023u) & ~1023u;
     const uint32_t bar_full = (uint32_t)__cvta_generic_to_shared(&full[0]);
     const uint32_t bar_empty = (uint32_t)__cvta_generic_to_shared(&empty[0]);
@@ -391,50 +428,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
 
     if (warp == 0) {
         if (lane == 0) {
-            const int n = (int)(x1 - x0);
-            auto tx_of = [&](long long x) {
-                const int S = (int)(x / kc), nt = min(8, g.tiles16 - 8 * S);
-                return (uint32_t)nt * kBlockBytesBf16 + (uint32_t)N * 128u;
+            // one weight copy (C chunks x 8 tiles x 2 KB, rows past the
+            // matrix and chunks past K read as zeros) and one activation copy
+            // (or one per chunk when K is ragged) per unit
+            const uint32_t tx_b = (uint32_t)N * 128u;
+            auto issue_a = [&](int i, int S, int c0) {
+                tensor_g2s_4d(smem0 + (uint32_t)(i % SG) * stage_bytes, &tmap_w, 0, 0, 8 * S, c0,
+                              bar_full + 8 * (i % SG));
             };
-            auto issue_a = [&](int i) {
-                const long long x = x0 + i;
-                const int S = (int)(x / kc), ck = (int)(x % kc), s = i % SG;
-                const uint32_t dst = smem0 + (uint32_t)s * stage_bytes;
-                for (int t = 0; t < 8; t++) {
-                    const int tile = 8 * S + t;
-                    if (tile < g.tiles16)
-                        bulk_g2s(dst + t * kBlockBytesBf16, g.w + ((size_t)tile * kc + ck) * kBlockBytesBf16,
-                                 kBlockBytesBf16, bar_full + 8 * s);
+            auto issue_b = [&](int i, int c0, int cnt) {
+                const uint32_t dst = smem0 + (uint32_t)(i % SG) * stage_bytes + b_off;
+                if (g.b3d) {
+                    tensor_g2s_3d(dst, &tmap_x, 0, 0, c0, bar_full + 8 * (i % SG));
+                } else {
+                    for (int q = 0; q < cnt; q++)
+                        tensor_g2s(dst + (uint32_t)q * tx_b, &tmap_x, (c0 + q) * kChunkK, 0, bar_full + 8 * (i % SG));
                 }
             };
-            auto issue_b = [&](int i) {
-                const int ck = (int)((x0 + i) % kc), s = i % SG;
-                tensor_g2s(smem0 + (uint32_t)s * stage_bytes + kStageA, &tmap_x, ck * kChunkK, 0, bar_full + 8 * s);
-            };
-            const int pre = min(SG, n);
+            auto tx_of = [&](int cnt) { return (uint32_t)C * kStageA + (uint32_t)(g.b3d ? C : cnt) * tx_b; };
+            SkUnits ua{x0, x0, x1, kc, C}, ub{x0, x0, x1, kc, C};
+            int S, c0, cnt, i = 0;
+            bool first, last;
             // the weights do not depend on the previous kernel
-            for (int i = 0; i < pre; i++) {
-                bar_expect_tx(bar_full + 8 * (i % SG), tx_of(x0 + i));
-                issue_a(i);
+            while (i < SG && ua.next(S, c0, cnt, first, last)) {
+                bar_expect_tx(bar_full + 8 * i, tx_of(cnt));
+                issue_a(i, S, c0);
+                i++;
             }
+            const int pre = i;
             pdl_wait();
-            for (int i = 0; i < pre; i++) issue_b(i);
+            for (int k = 0; k < pre && ub.next(S, c0, cnt, first, last); k++) issue_b(k, c0, cnt);
             int issued = pre;
-            for (int i = pre; i < n; i++) {
+            while (ua.next(S, c0, cnt, first, last)) {
                 const int s = i % SG;
                 if (!bar_wait(bar_empty + 8 * s, (uint32_t)(((i / SG) - 1) & 1))) {
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
                     break;
                 }
-                bar_expect_tx(bar_full + 8 * s, tx_of(x0 + i));
-                issue_a(i);
-                issue_b(i);
-                issued = i + 1;
+                bar_expect_tx(bar_full + 8 * s, tx_of(cnt));
+                issue_a(i, S, c0);
+                issue_b(i, c0, cnt);
+                issued = ++i;
             }
             // the last copy into each stage has landed before the CTA may
             // exit (already true unless a wait gave up; bounded)
-            for (int i = max(0, issued - SG); i < issued; i++)
-                if (!bar_wait(bar_full + 8 * (i % SG), (uint32_t)((i / SG) & 1))) atomicExch(g.e.err, RENG_E_TIMEOUT);
+            for (int k = max(0, issued - SG); k < issued; k++)
+                if (!bar_wait(bar_full + 8 * (k % SG), (uint32_t)((k / SG) & 1))) atomicExch(g.e.err, RENG_E_TIMEOUT);
         } else {
             pdl_wait();
         }
@@ -444,36 +483,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
         pdl_launch();
         if (lane == 0) {
             const uint32_t idesc = umma_idesc(N);
-            int i = 0, j = 0;
-            bool ok = true;
-            for (long long x = x0; x < x1 && ok; j++) {
-                const int kb = (int)(x % kc), ke = (int)min((long long)kc, kb + (x1 - x));
-                const int b = j & 1;
-                if (j >= 2 && !bar_wait(bar_acce + 8 * b, (uint32_t)(((j / 2) - 1) & 1))) {
-                    atomicExch(g.e.err, RENG_E_TIMEOUT);
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t acc = tmem + (uint32_t)b * half;
-                for (int k = kb; k < ke; k++, i++) {
-                    const int s = i % SG;
-                    if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
+            SkUnits u{x0, x0, x1, kc, C};
+            int S, c0, cnt, i = 0, j = -1, b = 0;
+            bool first, last;
+            uint32_t acc = tmem;
+            while (u.next(S, c0, cnt, first, last)) {
+                if (first) {
+                    b = ++j & 1;
+                    if (j >= 2 && !bar_wait(bar_acce + 8 * b, (uint32_t)(((j / 2) - 1) & 1))) {
                         atomicExch(g.e.err, RENG_E_TIMEOUT);
-                        ok = false;
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t a0 = smem0 + (uint32_t)s * stage_bytes, b0 = a0 + kStageA;
+                    acc = tmem + (uint32_t)b * half;
+                }
+                const int s = i % SG;
+                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
+                    atomicExch(g.e.err, RENG_E_TIMEOUT);
+                    umma_commit(bar_accf + 8 * b);  // the epilogue then sees the error word
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t st0 = smem0 + (uint32_t)s * stage_bytes;
+                for (int q = 0; q < cnt; q++) {
+                    const uint32_t a0 = st0 + (uint32_t)q * kStageA, b0 = st0 + b_off + (uint32_t)q * (uint32_t)N * 128u;
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
                         umma(acc, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32), idesc,
-                             (k > kb || kk > 0) ? 1u : 0u);
-                    umma_commit(bar_empty + 8 * s);
+                             (first && q == 0 && kk == 0) ? 0u : 1u);
                 }
-                // fires when this segment's MMAs have finished (also after a
-                // wait gave up: the epilogue then sees the error word)
-                umma_commit(bar_accf + 8 * b);
-                x += ke - kb;
+                umma_commit(bar_empty + 8 * s);
+                i++;
+                if (last) umma_commit(bar_accf + 8 * b);  // fires when this segment's MMAs have finished
             }
             // every MMA this thread issued has completed before TMEM is freed
             umma_commit(bar_drain);
@@ -600,9 +641,52 @@ int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out)
     return RENG_OK;
 }
 
-size_t gemm_smem_bytes(int n, int stages) { return (size_t)stages * (kStageA + (size_t)n * 128) + 1024; }
+// Activations as {64 k, n rows, c chunks} boxes (128-byte swizzle): one copy
+// fetches the x tiles of c consecutive 64-k chunks.  K must be a multiple of
+// 64 (the chunk dimension would otherwise run into the next row).
+int gemm_tensor_map3(const uint16_t* x, int rows, int K, int n, int c, CUtensorMap* out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (K % kChunkK || n % 16 || n < 16 || n > kRowsCap || n > rows || c < 1 || c > 4 || ((uintptr_t)x & 15))
+        return fail(RENG_E_INVAL, "gemm_tensor_map3: bad shape");
+    cuuint64_t dims[3] = {(cuuint64_t)kChunkK, (cuuint64_t)rows, (cuuint64_t)(K / kChunkK)};
+    cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)kChunkK * 2};
+    cuuint32_t box[3] = {(cuuint32_t)kChunkK, (cuuint32_t)n, (cuuint32_t)c};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void*)x, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled (x, 3-D) failed (" + std::to_string((int)r) + ")");
+    return RENG_OK;
+}
 
-int gemm_pick_stages(int n) {
+// The packed weights [tiles16][kc][2 KB block] as a 4-D tensor {64 elements,
+// 16 rows, tiles16, kc} read in {64, 16, 8, c} boxes: one copy lands c
+// chunks of a 128-row super-tile as [c][8 tiles][2 KB], each chunk the
+// UMMA A operand as packed (the blocks are stored pre-swizzled, so the copy
+// itself does not swizzle).  Tiles past the matrix and chunks past kc read
+// as zeros.
+int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (tiles16 < 1 || kc < 1 || c < 1 || c > 4 || ((uintptr_t)w & 15))
+        return fail(RENG_E_INVAL, "gemm_weight_map: bad shape");
+    cuuint64_t dims[4] = {64, (cuuint64_t)kTileRows, (cuuint64_t)tiles16, (cuuint64_t)kc};
+    cuuint64_t strides[3] = {128, (cuuint64_t)kc * kBlockBytesBf16, (cuuint64_t)kBlockBytesBf16};
+    cuuint32_t box[4] = {64, (cuuint32_t)kTileRows, 8, (cuuint32_t)c};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, (void*)w, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled (weights) failed (" + std::to_string((int)r) + ")");
+    return RENG_OK;
+}
+
+size_t gemm_smem_bytes(int n, int stages, int c) { return (size_t)stages * c * (kStageA + (size_t)n * 128) + 1024; }
+
+int gemm_chunks_per_stage(int n) { return n <= 128 ? 2 : 1; }
+
+int gemm_pick_stages(int n, int c) {
     // One CTA per SM: as many stages as fit the ~200 KB budget (8 at N <= 64:
     // 128 KB of weights in flight per SM; 4 at N = 256).  RENG_GEMM_STAGES
     // caps it (a tuning knob).
@@ -611,32 +695,34 @@ int gemm_pick_stages(int n) {
         const int x = v ? atoi(v) : 0;
         return x >= 2 && x <= kGemmMaxStages ? x : kGemmMaxStages;
     }();
-    int s = (int)((unsigned)kGemmStageBudget / (kStageA + (unsigned)n * 128u));
+    int s = (int)((unsigned)kGemmStageBudget / ((unsigned)c * (kStageA + (unsigned)n * 128u)));
     if (s > cap) s = cap;
     return s < 2 ? 2 : s;
 }
 
-void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages) {
+void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, int* c) {
     const long long T = (long long)super_tiles * kc;
     *grid = (int)(T < sms ? T : sms);
-    *stages = gemm_pick_stages(n);
+    *c = gemm_chunks_per_stage(n);
+    *stages = gemm_pick_stages(n, *c);
 }
 
 size_t gemm_scratch_floats(int grid, int n) { return (size_t)2 * grid * n * 128; }
 
 template <int EPI>
-static cudaError_t launch_tc_t(const CUtensorMap& map, const GemmArgs& g, bool pdl, cudaStream_t st) {
+static cudaError_t launch_tc_t(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, bool pdl,
+                               cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.gridDim = dim3(g.grid);
     cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C);
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemm_sk<EPI>, map, g);
+    return cudaLaunchKernelEx(&cfg, k_gemm_sk<EPI>, map, wmap, g);
 }
 
 template <int EPI>
@@ -653,18 +739,20 @@ cudaError_t gemm_prepare() {
     return e;
 }
 
-cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st) {
+cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
+                           cudaStream_t st) {
     const long long T = (long long)g.super_tiles * g.kc;
     if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.grid < 1 || g.grid > T ||
-        g.stages < 2 || g.stages > kGemmMaxStages || gemm_smem_bytes(g.N, g.stages) > (size_t)kGemmMaxDynSmem ||
-        g.gpart == nullptr || g.gcnt == nullptr || g.super_tiles > kGemmCntMax)
+        g.C < 1 || g.C > 4 || g.stages < 2 || g.stages > kGemmMaxStages ||
+        gemm_smem_bytes(g.N, g.stages, g.C) > (size_t)kGemmMaxDynSmem || g.gpart == nullptr || g.gcnt == nullptr ||
+        g.super_tiles > kGemmCntMax || (g.b3d && g.kc * kChunkK != g.e.K))
         return cudaErrorInvalidValue;
     switch (epi) {
-        case EPI_QKV: return launch_tc_t<EPI_QKV>(map, g, pdl, st);
-        case EPI_RESID: return launch_tc_t<EPI_RESID>(map, g, pdl, st);
-        case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(map, g, pdl, st);
-        case EPI_LOGITS: return launch_tc_t<EPI_LOGITS>(map, g, pdl, st);
-        case EPI_F32: return launch_tc_t<EPI_F32>(map, g, pdl, st);
+        case EPI_QKV: return launch_tc_t<EPI_QKV>(map, wmap, g, pdl, st);
+        case EPI_RESID: return launch_tc_t<EPI_RESID>(map, wmap, g, pdl, st);
+        case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(map, wmap, g, pdl, st);
+        case EPI_LOGITS: return launch_tc_t<EPI_LOGITS>(map, wmap, g, pdl, st);
+        case EPI_F32: return launch_tc_t<EPI_F32>(map, wmap, g, pdl, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -801,7 +889,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
-    gemm_plan(g.super_tiles, kc, N, num_sms(dev), &g.grid, &g.stages);
+    gemm_plan(g.super_tiles, kc, N, num_sms(dev), &g.grid, &g.stages, &g.C);
     if (splits != 0) {
         // that many CTAs per super-tile (capped by the chunks and the SMs):
         // shares that split super-tiles in several ways, for checks
@@ -814,17 +902,20 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     GEMM_CU(f.alloc(&g.gpart, gemm_scratch_floats(g.grid, N) * 4));
     GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * 4));
     GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * 4));
-    CUtensorMap tmap;
-    const int rc = gemm_tensor_map(xd, kRowsCap, K, N, &tmap);
+    CUtensorMap tmap, wmap;
+    g.b3d = K % kChunkK == 0;
+    int rc = g.b3d ? gemm_tensor_map3(xd, kRowsCap, K, N, g.C, &tmap) : gemm_tensor_map(xd, kRowsCap, K, N, &tmap);
     if (rc) return rc;
-    GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
+    rc = gemm_weight_map(packed, tiles, kc, g.C, &wmap);
+    if (rc) return rc;
+    GEMM_CU(launch_gemm_tc(tmap, wmap, g, EPI_F32, false, 0));
     GEMM_CU(cudaDeviceSynchronize());
     if (iters > 0) {
         EventSet evs;
         GEMM_CU(evs.create(2));
         cudaEvent_t e0 = evs.e[0], e1 = evs.e[1];
         GEMM_CU(cudaEventRecord(e0, 0));
-        for (int i = 0; i < iters; i++) GEMM_CU(launch_gemm_tc(tmap, g, EPI_F32, false, 0));
+        for (int i = 0; i < iters; i++) GEMM_CU(launch_gemm_tc(tmap, wmap, g, EPI_F32, false, 0));
         GEMM_CU(cudaEventRecord(e1, 0));
         GEMM_CU(cudaEventSynchronize(e1));
         float ms = 0.f;

@@ -18,6 +18,8 @@ struct GemmArgs {
     int super_tiles;          // ceil(tiles16 / 8): 128-row MMA tiles
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
     int stages;               // pipeline stages (2..8)
+    int C;                    // 64-k chunks per stage (one weight copy, one activation copy)
+    int b3d;                  // the activation map is 3-D ({64, N, C} boxes; K % 64 == 0), else 2-D per chunk
     int grid;                 // persistent CTAs, each an equal share of the super_tiles x kc chunks
     float* gpart;             // split super-tiles' f32 partials [2 * grid][N / 16][128][16]
     int* gcnt;                // arrivals per super-tile (0 between launches)
@@ -26,17 +28,25 @@ struct GemmArgs {
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as
 // {64 k, n rows} boxes with the 128-byte swizzle; k >= K reads zeros.
 int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out);
-size_t gemm_smem_bytes(int n, int stages);
-// Pipeline stages for MMA width n: as many as fit about 200 KB.
-int gemm_pick_stages(int n);
+// The same buffer as {64 k, n rows, c chunks} boxes (K % 64 == 0).
+int gemm_tensor_map3(const uint16_t* x, int rows, int K, int n, int c, CUtensorMap* out);
+// Packed bf16 weights [tiles16][kc][2 KB] as {64, 16, 8 tiles, c chunks} boxes.
+int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out);
+size_t gemm_smem_bytes(int n, int stages, int c);
+// 64-k chunks per pipeline stage for MMA width n.
+int gemm_chunks_per_stage(int n);
+// Pipeline stages of c chunks at MMA width n: as many as fit about 200 KB.
+int gemm_pick_stages(int n, int c);
 // Raise the dynamic shared-memory limit of every GEMM instantiation (call
 // once per device before capture).
 cudaError_t gemm_prepare();
-// Persistent grid (one CTA per SM, at most one per chunk) and stages.
-void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages);
+// Persistent grid (one CTA per SM, at most one per chunk), stages and
+// chunks per stage.
+void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, int* c);
 // Floats of split-tile scratch a launch of `grid` CTAs at width n needs.
 size_t gemm_scratch_floats(int grid, int n);
-cudaError_t launch_gemm_tc(const CUtensorMap& map, const GemmArgs& g, int epi, bool pdl, cudaStream_t st);
+cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
+                           cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.
 cudaError_t launch_rmsnorm_rows(const uint16_t* x, const float* ss, int ss_tiles, const float* gain, float eps,
                                 int H, uint16_t* xn, int M, bool pdl, cudaStream_t st);

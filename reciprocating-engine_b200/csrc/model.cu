@@ -390,8 +390,6 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
         x = m->xn;
     }
     const int N = (g.M + 15) / 16 * 16;
-    CUtensorMap map;
-    TRY(gemm_tensor_map(x, kRowsCap, g.K, N, &map));
     GemmArgs a{};
     a.e = g;
     a.w = g.w;
@@ -399,12 +397,19 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.kc = g.kc;
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
-    gemm_plan(a.super_tiles, g.kc, N, m->sms, &a.grid, &a.stages);
+    gemm_plan(a.super_tiles, g.kc, N, m->sms, &a.grid, &a.stages, &a.C);
+    a.b3d = g.K % kChunkK == 0;
+    CUtensorMap map, wmap;
+    if (a.b3d)
+        TRY(gemm_tensor_map3(x, kRowsCap, g.K, N, a.C, &map));
+    else
+        TRY(gemm_tensor_map(x, kRowsCap, g.K, N, &map));
+    TRY(gemm_weight_map(g.w, g.tiles, g.kc, a.C, &wmap));
     if (gemm_scratch_floats(a.grid, N) > m->gpart_floats || a.super_tiles > kGemmCntMax)
         return fail(RENG_E_STATE, "GEMM split-tile scratch too small");
     a.gpart = m->gpart;
     a.gcnt = m->gcnt;
-    CU(launch_gemm_tc(map, a, epi, true, st));
+    CU(launch_gemm_tc(map, wmap, a, epi, true, st));
     m->launches++;
     return RENG_OK;
 }
