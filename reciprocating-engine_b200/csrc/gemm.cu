@@ -572,22 +572,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
             if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + S, 1) == cl - cf;
             named_sync_epilogue();
             if (!s_flag) continue;
-            // the last CTA of this super-tile: every share's partial, in K order
+            // the last CTA of this super-tile: every share's partial, in K
+            // order; the loads of up to 4 shares go out together (one L2
+            // round trip per 4 shares and column group, not one per share)
             __threadfence();
             for (int cb = 0; cb < ncb; cb++) {
                 float v[16];
 #pragma unroll
                 for (int q = 0; q < 16; q++) v[q] = 0.f;
-                for (int cc = cf; cc <= cl; cc++) {
-                    const float4* src = reinterpret_cast<const float4*>(
-                        g.gpart + ((size_t)sk_slot(cc, S, kc, T, G) * ncb * 128 + (size_t)cb * 128 + lr) * 16);
+                for (int c4 = cf; c4 <= cl; c4 += 4) {
+                    float4 t4[4][4];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float4 w4 = __ldcg(src + q);
-                        v[4 * q] += w4.x;
-                        v[4 * q + 1] += w4.y;
-                        v[4 * q + 2] += w4.z;
-                        v[4 * q + 3] += w4.w;
+                    for (int u = 0; u < 4; u++) {
+                        const int cc = min(c4 + u, cl);
+                        const float4* src = reinterpret_cast<const float4*>(
+                            g.gpart + ((size_t)sk_slot(cc, S, kc, T, G) * ncb * 128 + (size_t)cb * 128 + lr) * 16);
+#pragma unroll
+                        for (int q = 0; q < 4; q++) t4[u][q] = __ldcg(src + q);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        if (c4 + u > cl) break;
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            v[4 * q] += t4[u][q].x;
+                            v[4 * q + 1] += t4[u][q].y;
+                            v[4 * q + 2] += t4[u][q].z;
+                            v[4 * q + 3] += t4[u][q].w;
+                        }
                     }
                 }
                 tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
@@ -701,8 +713,25 @@ int gemm_pick_stages(int n, int c) {
 }
 
 void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, int* c) {
+    // Fewer super-tiles than SMs (the 4096-row projections: 32): ks CTAs
+    // per super-tile, so each is split in ks shares (about kc / ks chunks)
+    // that finish together and whose partials the last CTA reads in one go;
+    // at N >= 128 at most 2 (a 128 x N partial is 64-128 KB, as large as 4-8
+    // chunks of weights).  Otherwise one CTA per SM, each super-tile split
+    // in at most 2-3 shares.
+    long long G;
+    if (super_tiles >= sms) {
+        G = sms;
+    } else {
+        int ks = sms / super_tiles;
+        const int cap = n >= 128 ? 2 : 4;
+        if (ks > cap) ks = cap;
+        if (ks > kc) ks = kc;
+        if (ks < 1) ks = 1;
+        G = (long long)super_tiles * ks;
+    }
     const long long T = (long long)super_tiles * kc;
-    *grid = (int)(T < sms ? T : sms);
+    *grid = (int)(T < G ? T : G);
     *c = gemm_chunks_per_stage(n);
     *stages = gemm_pick_stages(n, *c);
 }
