@@ -724,7 +724,12 @@ void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, 
         G = sms;
     } else {
         int ks = sms / super_tiles;
-        const int cap = n >= 128 ? 2 : 4;
+        static const int cap_env = [] {  // RENG_GEMM_KS: a tuning knob for the shares cap
+            const char* v = getenv("RENG_GEMM_KS");
+            const int x = v ? atoi(v) : 0;
+            return x >= 1 && x <= 8 ? x : 0;
+        }();
+        const int cap = cap_env ? cap_env : (n >= 128 ? 2 : 4);
         if (ks > cap) ks = cap;
         if (ks > kc) ks = kc;
         if (ks < 1) ks = 1;
