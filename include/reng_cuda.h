@@ -290,14 +290,12 @@ int reng_model_trace_step(reng_model *m, uint64_t *out, int max_phases, int *n_p
  * is packed into the engine's swizzled 16 x 64 blocks, x (bf16 [M][K]) is
  * read by the tensor-memory-accelerator copy, the accumulator lives in
  * tensor memory.  Host buffers (mem RENG_MEM_HOST) or device buffers
- * (RENG_MEM_DEVICE).  1 <= M <= 256, K % 8 == 0.  The kernel is
- * persistent: each CTA streams an equal share of the (128-row super-tile,
- * 64-k chunk) work and the last CTA of a split super-tile adds the
- * partials in K order.  splits = 0: the model's grid (one CTA per SM, at
- * most one per chunk); -8..8 otherwise: |splits| CTAs per super-tile
- * (capped by the chunks and the SMs), for checks of the split paths.
- * iters > 0: the kernel alone is also launched iters more times and
- * *ms_out gets its mean duration (CUDA events).  The
+ * (RENG_MEM_DEVICE).  1 <= M <= 256, K % 8 == 0.  splits = K splits (0:
+ * the model's choice; > 0: that many CTAs of one cluster adding their
+ * partials over shared memory; < 0: -splits plain CTAs adding theirs
+ * through global scratch, the last to arrive in split order).  iters > 0:
+ * the kernel alone is also launched iters more times and *ms_out gets its
+ * mean duration (CUDA events).  The
  * reference's projections are SynapseAI graph matmuls (reng-synapse
  * src/model.rs:2960-3040); this entry exists so the kernel can be checked
  * and timed on its own.

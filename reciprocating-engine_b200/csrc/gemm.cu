@@ -1,31 +1,37 @@
 // tcgen05 / TMEM GEMM for steps with many activation rows (batch > 8 decode
 // and prefill blocks): Y[m, row] = sum_k X[m, k] * W[row, k] with the
-// weights as the MMA's A operand (M = 128 weight rows per tile) and the
+// weights as the MMA's A operand (M = 128 weight rows per CTA) and the
 // activation rows as its N (16..256), so a wide batch is one N dimension and
 // the weights stream from HBM once per step.
 //
 // Operands in shared memory use the K-major 128-byte-swizzle atom of the
 // UMMA descriptors (8 rows x 128 B, 16-byte chunk j of row r at j ^ r):
-//  * A (weights): the packed blocks are already that atom, so a stage is
-//    eight 2 KB bulk copies (one per 16-row tile of the 128-row super-tile);
-//  * B (activations, row-major [rows][K] bf16): a 2-D tensor-map copy with
-//    128-byte swizzle of a {64 k, N rows} box.
+//  * A (weights): the packed blocks are already that atom; a 4-D tensor map
+//    over the packed matrix ({64, 16 rows, tiles, chunks}, no swizzle) lands
+//    C chunks x 8 tiles x 2 KB with one copy;
+//  * B (activations, row-major [rows][K] bf16): a 3-D tensor-map copy with
+//    128-byte swizzle of a {64 k, N rows, C chunks} box (a 2-D copy per
+//    chunk when K is not a multiple of 64).
 // Both give SBO = 1024 B (one 8-row atom), and the K=16 steps inside a
-// 64-k stage advance the descriptor start address by 32 B.
+// 64-k chunk advance the descriptor start address by 32 B.  A stage holds C
+// (2) chunks: two copies per 128 KB of weights instead of one per 2 KB
+// block, since a single issuing thread's copy count, not the bytes in
+// flight, bounded the weight stream (17 GB/s per SM with eight 2 KB copies
+// per chunk whatever the stage count, 40 GB/s with one copy per stage,
+// B200).
 //
-// Scheduling (k_gemm_sk): persistent stream-K.  One CTA per SM takes an
-// equal share of the (super-tile, 64-k chunk) work in super-tile-major
-// order, so every SM streams weights from its first chunk to its last
-// whatever the matrix shape (a 4096-row projection has 32 super-tiles, a
-// Llama LM head 1002).  Roles (192 threads): warp 0 lane 0 issues the
-// copies into an up-to-8-stage ring, warp 1 owns the TMEM accumulators (two
-// buffers of N f32 columns) and lane 0 issues tcgen05.mma.kind::f16 and
-// commits each stage back to the producer and each finished segment to the
-// epilogue, warps 2-5 read TMEM with tcgen05.ld (warp w: lanes 32*(w%4) ..
-// +32) and apply the same epilogues as the GEMV kernels while the next
-// segment accumulates in the other buffer.  Super-tiles split between two
-// or more shares are finished by the last of their CTAs to arrive, which
-// adds the f32 partials in K order.  Every mbarrier wait is bounded.
+// Roles (192 threads): warp 0 lane 0 issues the copies, warp 1 owns the TMEM
+// accumulator (128 lanes x N f32 columns) and lane 0 issues the MMAs and
+// commits each stage back to the producer; warps 2-5 read the accumulator
+// with tcgen05.ld (warp w reads TMEM lanes 32*(w%4) .. +32) and apply the
+// same epilogues as the GEMV kernels.  A weight matrix with few super-tiles
+// is split along K over up to 8 CTAs launched as one thread-block cluster:
+// each keeps its partial tile in its own shared memory, and after a cluster
+// barrier CTA r adds column blocks r, r + ks, ... of every split over
+// distributed shared memory in rank order (deterministic) and runs their
+// epilogue.  Every mbarrier wait is bounded.
+#include <cooperative_groups.h>
+
 #include <mutex>
 #include <string>
 #include <vector>
@@ -284,134 +290,47 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
     }
 }
 
-// The CTA's share of the launch's work: chunks [start, end) of the
-// super-tile-major chunk order (super-tile S owns chunks S*kc .. S*kc+kc-1),
-// start = floor(c * T / G) for CTA c of G and T chunks in all.
-__device__ __forceinline__ long long sk_start(long long c, long long T, long long G) { return c * T / G; }
-// The CTA whose share holds chunk x: the largest c with sk_start(c) <= x.
-__device__ __forceinline__ int sk_owner(long long x, long long T, long long G) {
-    return (int)(((x + 1) * G - 1) / T);
-}
-// Partial-tile slot of CTA c's segment of super-tile S: a share holds at
-// most two split super-tiles, the one it starts in (slot 2c) and the one it
-// ends in (slot 2c + 1).
-__device__ __forceinline__ int sk_slot(int c, int S, int kc, long long T, long long G) {
-    return (int)(sk_start(c, T, G) / kc) == S ? 2 * c : 2 * c + 1;
-}
-
-// The copy units of a CTA's share: runs of up to C consecutive chunks of
-// one segment (one super-tile), each fetched by one weight copy and one
-// activation copy into one pipeline stage.
-struct SkUnits {
-    long long x, x0, x1;
-    int kc, C;
-    __device__ bool next(int& S, int& c0, int& cnt, bool& first, bool& last) {
-        if (x >= x1) return false;
-        S = (int)(x / kc);
-        c0 = (int)(x % kc);
-        const long long seg0 = max(x0, (long long)S * kc), seg1 = min(x1, (long long)(S + 1) * kc);
-        cnt = (int)min((long long)C, seg1 - x);
-        first = x == seg0;
-        last = x + cnt == seg1;
-        x += cnt;
-        return true;
-    }
-};
-
-// LM-head argmax of one finished super-tile: the 4 epilogue warps' best per
-// row into the rows' running maxima; the CTA that finishes the launch's last
-// super-tile reads the keys, swaps them with the other ranks (vocabulary
-// shards) and writes the ids.
-__device__ __forceinline__ void sk_logits_tile_done(const GemmArgs& g, float* am_v, int* am_i, int* s_done) {
-    const GemvArgs& a = g.e;
-    named_sync_epilogue();
-    for (int m = threadIdx.x - 64; m < a.M; m += 128) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + m], am_i[w * kRowsCap + m]);
-        atomicMax(a.am_key + m, am_pack(bv, bi));
-    }
-    __threadfence();
-    named_sync_epilogue();
-    if (threadIdx.x == 64) *s_done = (atomicAdd(a.am_count, 1u) == (unsigned)g.super_tiles - 1);
-    named_sync_epilogue();
-    if (*s_done) {
-        __threadfence();
-        for (int m = threadIdx.x - 64; m < a.M; m += 128) {
-            unsigned long long k = atomicExch(a.am_key + m, 0ull);
-            if (a.hx) k = head_exchange(a.hx, m, k, a.err);  // vocabulary shards of the ranks
-            am_i[m] = am_unpack(k);
-        }
-        named_sync_epilogue();
-        if (a.hx && threadIdx.x == 64) *a.hx->epoch += 1;
-        if (threadIdx.x == 64) {
-            if (a.mode == 0) {
-                const int s = *a.step;
-                for (int m = 0; m < a.M; m++) {
-                    a.ids_ring[(size_t)(s + 1) * a.batch + m] = (uint32_t)am_i[m];
-                    a.pos[m] += 1;
-                }
-                *a.step = s + 1;
-            } else {
-                *a.next_id = (uint32_t)am_i[a.M - 1];
-            }
-            *a.am_count = 0u;
-            __threadfence();
-        }
-    }
-    named_sync_epilogue();  // am_v / am_i are free for the next super-tile
-}
-
-// Persistent stream-K GEMM: one CTA per SM, each streaming an equal share
-// of the launch's (super-tile, 64-k chunk) work in super-tile-major order,
-// so every SM keeps weights in flight from its first chunk to its last,
-// whatever the matrix's shape.  A share is a run of segments (one
-// super-tile's chunks each); a segment accumulates in one of two TMEM
-// buffers, so the epilogue warps finish segment j while the MMA warp fills
-// the other buffer with segment j + 1 and the producer streams on.  A
-// segment that covers its super-tile's whole K runs the epilogue from TMEM;
-// a split super-tile's segments store f32 partials, and the last of its
-// CTAs to arrive adds them in K order (deterministic: the same sum whoever
-// arrives last) and runs the epilogue.  Every mbarrier wait is bounded.
 template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmap_x,
                                                              const __grid_constant__ CUtensorMap tmap_w, GemmArgs g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], acc_full[2],
-        acc_empty[2], drain;
+    __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], accum;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int s_flag, s_done;
+    __shared__ int s_flag;
     __shared__ float am_v[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
     __shared__ int am_i[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c = blockIdx.x;
-    const long long G = gridDim.x, T = (long long)g.super_tiles * g.kc;
-    const long long x0 = sk_start(c, T, G), x1 = sk_start(c + 1, T, G);
-    const int kc = g.kc, N = g.N, SG = g.stages, C = g.C;
+    const int S = blockIdx.x / g.ks, ksi = blockIdx.x % g.ks;
+    const int kper = (g.kc + g.ks - 1) / g.ks;
+    const int kb = min(g.kc, ksi * kper), ke = min(g.kc, kb + kper), nk = ke - kb;
+    // each super-tile walks its k range from a different starting chunk, so
+    // the CTAs in flight read different activation chunks (all CTAs read the
+    // same x; in lock-step they would all hit the same L2 lines)
+    // the split's chunks go in units of up to C consecutive chunks (one
+    // weight copy and one activation copy each), walked from a per-super-
+    // tile starting unit so that the CTAs in flight read different
+    // activation chunks (all CTAs read the same x; in lock-step they would
+    // all hit the same L2 lines)
+    const int C = g.C, nu = (nk + C - 1) / C;
+    const int rot = nu > 0 ? (int)(((unsigned)S * 2654435761u) % (unsigned)nu) : 0;
+    const int N = g.N, SG = g.stages;
     const uint32_t stage_bytes = (uint32_t)C * (kStageA + (uint32_t)N * 128u);
-    const uint32_t b_off = (uint32_t)C * kStageA;  // the stage's activation tiles follow its C weight tiles
+    const uint32_t b_off = (uint32_t)C * kStageA;  // a stage's activation tiles follow its C weight tiles
+    // 1024-byte alignment of the stage buffers (the swizzle atoms)
     const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem_raw) + 1023u) & ~1023u;
     const uint32_t bar_full = (uint32_t)__cvta_generic_to_shared(&full[0]);
     const uint32_t bar_empty = (uint32_t)__cvta_generic_to_shared(&empty[0]);
-    const uint32_t bar_accf = (uint32_t)__cvta_generic_to_shared(&acc_full[0]);
-    const uint32_t bar_acce = (uint32_t)__cvta_generic_to_shared(&acc_empty[0]);
-    const uint32_t bar_drain = (uint32_t)__cvta_generic_to_shared(&drain);
-    // two accumulators of N columns, each at a power-of-two column offset
-    uint32_t half = 16;
-    while ((int)half < N) half <<= 1;
-    const uint32_t ncols = half < 16 ? 32 : 2 * half;
+    const uint32_t bar_acc = (uint32_t)__cvta_generic_to_shared(&accum);
+    uint32_t ncols = 32;
+    while ((int)ncols < N) ncols <<= 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SG; s++) {
             bar_init(bar_full + 8 * s, 1);
             bar_init(bar_empty + 8 * s, 1);
         }
-        for (int b = 0; b < 2; b++) {
-            bar_init(bar_accf + 8 * b, 1);
-            bar_init(bar_acce + 8 * b, 4);  // lane 0 of each epilogue warp
-        }
-        bar_init(bar_drain, 1);
+        bar_init(bar_acc, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -425,18 +344,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
+    bool failed = false;
 
     if (warp == 0) {
         if (lane == 0) {
-            // one weight copy (C chunks x 8 tiles x 2 KB, rows past the
-            // matrix and chunks past K read as zeros) and one activation copy
-            // (or one per chunk when K is ragged) per unit
-            const uint32_t tx_b = (uint32_t)N * 128u;
-            auto issue_a = [&](int i, int S, int c0) {
+            int issued = 0;
+            // unit i: chunks c0 .. c0 + cnt - 1 of this split
+            auto unit = [&](int i, int& c0, int& cnt) {
+                const int u = (i + rot) % nu;
+                c0 = kb + u * C;
+                cnt = min(C, ke - c0);
+            };
+            auto issue_a = [&](int i) {
+                int c0, cnt;
+                unit(i, c0, cnt);
+                // one copy of C chunks x 8 tiles (tiles past the matrix and
+                // chunks past kc land as zeros)
                 tensor_g2s_4d(smem0 + (uint32_t)(i % SG) * stage_bytes, &tmap_w, 0, 0, 8 * S, c0,
                               bar_full + 8 * (i % SG));
             };
-            auto issue_b = [&](int i, int c0, int cnt) {
+            const uint32_t tx_b = (uint32_t)N * 128u;
+            auto issue_b = [&](int i) {
+                int c0, cnt;
+                unit(i, c0, cnt);
                 const uint32_t dst = smem0 + (uint32_t)(i % SG) * stage_bytes + b_off;
                 if (g.b3d) {
                     tensor_g2s_3d(dst, &tmap_x, 0, 0, c0, bar_full + 8 * (i % SG));
@@ -445,35 +375,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
                         tensor_g2s(dst + (uint32_t)q * tx_b, &tmap_x, (c0 + q) * kChunkK, 0, bar_full + 8 * (i % SG));
                 }
             };
-            auto tx_of = [&](int cnt) { return (uint32_t)C * kStageA + (uint32_t)(g.b3d ? C : cnt) * tx_b; };
-            SkUnits ua{x0, x0, x1, kc, C}, ub{x0, x0, x1, kc, C};
-            int S, c0, cnt, i = 0;
-            bool first, last;
+            auto tx_of = [&](int i) {
+                int c0, cnt;
+                unit(i, c0, cnt);
+                return (uint32_t)C * kStageA + (uint32_t)(g.b3d ? C : cnt) * tx_b;
+            };
+            const int pre = min(SG, nu);
             // the weights do not depend on the previous kernel
-            while (i < SG && ua.next(S, c0, cnt, first, last)) {
-                bar_expect_tx(bar_full + 8 * i, tx_of(cnt));
-                issue_a(i, S, c0);
-                i++;
+            for (int i = 0; i < pre; i++) {
+                bar_expect_tx(bar_full + 8 * (i % SG), tx_of(i));
+                issue_a(i);
             }
-            const int pre = i;
             pdl_wait();
-            for (int k = 0; k < pre && ub.next(S, c0, cnt, first, last); k++) issue_b(k, c0, cnt);
-            int issued = pre;
-            while (ua.next(S, c0, cnt, first, last)) {
+            for (int i = 0; i < pre; i++) issue_b(i);
+            issued = pre;
+            for (int i = pre; i < nu; i++) {
                 const int s = i % SG;
                 if (!bar_wait(bar_empty + 8 * s, (uint32_t)(((i / SG) - 1) & 1))) {
+                    failed = true;
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
                     break;
                 }
-                bar_expect_tx(bar_full + 8 * s, tx_of(cnt));
-                issue_a(i, S, c0);
-                issue_b(i, c0, cnt);
-                issued = ++i;
+                bar_expect_tx(bar_full + 8 * s, tx_of(i));
+                issue_a(i);
+                issue_b(i);
+                issued = i + 1;
             }
-            // the last copy into each stage has landed before the CTA may
-            // exit (already true unless a wait gave up; bounded)
-            for (int k = max(0, issued - SG); k < issued; k++)
-                if (!bar_wait(bar_full + 8 * (k % SG), (uint32_t)((k / SG) & 1))) atomicExch(g.e.err, RENG_E_TIMEOUT);
+            // drain: the last copy into each stage has landed before the CTA
+            // may exit (already true unless a wait gave up; bounded)
+            for (int i = max(0, issued - SG); i < issued; i++)
+                if (!bar_wait(bar_full + 8 * (i % SG), (uint32_t)((i / SG) & 1)))
+                    atomicExch(g.e.err, RENG_E_TIMEOUT);
         } else {
             pdl_wait();
         }
@@ -483,130 +415,183 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_sk(const __grid_consta
         pdl_launch();
         if (lane == 0) {
             const uint32_t idesc = umma_idesc(N);
-            SkUnits u{x0, x0, x1, kc, C};
-            int S, c0, cnt, i = 0, j = -1, b = 0;
-            bool first, last;
-            uint32_t acc = tmem;
-            while (u.next(S, c0, cnt, first, last)) {
-                if (first) {
-                    b = ++j & 1;
-                    if (j >= 2 && !bar_wait(bar_acce + 8 * b, (uint32_t)(((j / 2) - 1) & 1))) {
-                        atomicExch(g.e.err, RENG_E_TIMEOUT);
-                        break;
-                    }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    acc = tmem + (uint32_t)b * half;
-                }
+            int done = 0;
+            for (int i = 0; i < nu; i++) {
                 const int s = i % SG;
                 if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
-                    umma_commit(bar_accf + 8 * b);  // the epilogue then sees the error word
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const int cnt = min(C, ke - (kb + ((i + rot) % nu) * C));
                 const uint32_t st0 = smem0 + (uint32_t)s * stage_bytes;
                 for (int q = 0; q < cnt; q++) {
                     const uint32_t a0 = st0 + (uint32_t)q * kStageA, b0 = st0 + b_off + (uint32_t)q * (uint32_t)N * 128u;
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        umma(acc, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32), idesc,
-                             (first && q == 0 && kk == 0) ? 0u : 1u);
+                        umma(tmem, umma_desc(a0 + kk * 32), umma_desc(b0 + kk * 32), idesc,
+                             (i > 0 || q > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(bar_empty + 8 * s);
-                i++;
-                if (last) umma_commit(bar_accf + 8 * b);  // fires when this segment's MMAs have finished
+                done = i + 1;
             }
-            // every MMA this thread issued has completed before TMEM is freed
-            umma_commit(bar_drain);
-            if (!bar_wait(bar_drain, 0)) atomicExch(g.e.err, RENG_E_TIMEOUT);
+            // the commit fires when every MMA issued so far has finished
+            // (also after a wait gave up, so none still reads shared memory)
+            if (done > 0) umma_commit(bar_acc);
+            else bar_arrive(bar_acc);
         }
     } else {
-        // ---- epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. +32 ----
+        // ---- epilogue warps 2..5 ----
         pdl_wait();
         pdl_launch();
         const int q4 = warp & 3, warp_e = warp - 2;
-        const int lr = 32 * q4 + lane;
-        const int ncb = N / 16;
-        int j = 0;
-        for (long long x = x0; x < x1; j++) {
-            const int S = (int)(x / kc), kb = (int)(x % kc), ke = (int)min((long long)kc, kb + (x1 - x));
-            x += ke - kb;
-            const int b = j & 1;
-            const int p = 128 * S + lr;  // packed row of the matrix
-            if (!bar_wait(bar_accf + 8 * b, (uint32_t)((j / 2) & 1))) {
-                if (lane == 0) atomicExch(g.e.err, RENG_E_TIMEOUT);
-                break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t trow = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)b * half;
-            if (kb == 0 && ke == kc) {
-                // the whole K of this super-tile: epilogue straight from TMEM
-                for (int cb = 0; cb < ncb; cb++) {
-                    float v[16];
-                    tmem_ld16(trow + cb * 16, v);
-                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
-                }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) bar_arrive(bar_acce + 8 * b);
-                if (EPI == EPI_LOGITS) sk_logits_tile_done(g, am_v, am_i, &s_done);
-                continue;
-            }
-            // a split super-tile: this share's partial to its slot,
-            // [slot][cb][128 rows][16] f32 (a warp stores 2 KB contiguous)
-            const int slot = sk_slot(c, S, kc, T, G);
-            float* mine = g.gpart + (size_t)slot * ncb * 128 * 16;
-            for (int cb = 0; cb < ncb; cb++) {
+        const int lr = 32 * q4 + lane;       // TMEM lane = row of the super-tile
+        const int p = 128 * S + lr;          // packed row of the matrix
+        if (!bar_wait(bar_acc, 0)) {
+            failed = true;
+            if (lane == 0) atomicExch(g.e.err, RENG_E_TIMEOUT);
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t trow = tmem + ((uint32_t)(32 * q4) << 16);
+        // no MMA ran (empty split, or a wait gave up and *err is set): the
+        // accumulator was never written
+        const bool zero = nk == 0 || failed;
+        if (g.ks == 1) {
+            for (int cb = 0; cb < N / 16; cb++) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
-                float4* dst = reinterpret_cast<float4*>(mine + ((size_t)cb * 128 + lr) * 16);
+                if (zero)
 #pragma unroll
-                for (int q = 0; q < 4; q++) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+                    for (int j = 0; j < 16; j++) v[j] = 0.f;
+                tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
             }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) bar_arrive(bar_acce + 8 * b);
-            const int cf = sk_owner((long long)S * kc, T, G), cl = sk_owner((long long)S * kc + kc - 1, T, G);
+        } else if (g.gpart != nullptr) {
+            // split K without a cluster: this split's partial to global
+            // scratch [super-tile][split][128][N]; the last split of the
+            // super-tile to arrive adds all of them in split order
+            // (deterministic) and runs the epilogue
+            float* mine = g.gpart + (((size_t)S * g.ks + ksi) * 128 + lr) * N;
+            for (int cb = 0; cb < N / 16; cb++) {
+                float v[16];
+                tmem_ld16(trow + cb * 16, v);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    __stcg(reinterpret_cast<float4*>(mine + cb * 16) + j,
+                           zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            }
             __threadfence();
             named_sync_epilogue();
-            if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + S, 1) == cl - cf;
+            if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + S, 1) == g.ks - 1;
             named_sync_epilogue();
-            if (!s_flag) continue;
-            // the last CTA of this super-tile: every share's partial, in K
-            // order; the loads of up to 4 shares go out together (one L2
-            // round trip per 4 shares and column group, not one per share)
+            if (s_flag) {
+                __threadfence();
+                for (int cb = 0; cb < N / 16; cb++) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = 0.f;
+                    for (int k = 0; k < g.ks; k++) {
+                        const float4* src =
+                            reinterpret_cast<const float4*>(g.gpart + (((size_t)S * g.ks + k) * 128 + lr) * N + cb * 16);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float4 x = __ldcg(src + j);
+                            v[4 * j] += x.x;
+                            v[4 * j + 1] += x.y;
+                            v[4 * j + 2] += x.z;
+                            v[4 * j + 3] += x.w;
+                        }
+                    }
+                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                }
+                if (threadIdx.x == 64) g.gcnt[S] = 0;
+            }
+        } else {
+            // split K: this split's partial into the (finished) stage buffers,
+            // row lr at lr * (N + 4) floats (conflict-free 16-byte stores)
+            float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
+            for (int cb = 0; cb < N / 16; cb++) {
+                float v[16];
+                tmem_ld16(trow + cb * 16, v);
+                float4* dst = reinterpret_cast<float4*>(part + (size_t)lr * (N + 4) + cb * 16);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    dst[j] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                  : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+        }
+        if (EPI == EPI_LOGITS) {
+            // CTA partials of every row: best over the 4 epilogue warps
+            named_sync_epilogue();
+            const GemvArgs& a = g.e;
+            // this CTA's best per row into the rows' running maxima
+            for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + m], am_i[w * kRowsCap + m]);
+                atomicMax(a.am_key + m, am_pack(bv, bi));
+            }
             __threadfence();
-            for (int cb = 0; cb < ncb; cb++) {
+            named_sync_epilogue();
+            if (threadIdx.x == 64) s_flag = (atomicAdd(a.am_count, 1u) == gridDim.x - 1);
+            named_sync_epilogue();
+            if (s_flag) {
+                __threadfence();
+                for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+                    unsigned long long k = atomicExch(a.am_key + m, 0ull);
+                    if (a.hx) k = head_exchange(a.hx, m, k, a.err);  // vocabulary shards of the ranks
+                    am_i[m] = am_unpack(k);
+                }
+                named_sync_epilogue();
+                if (a.hx && threadIdx.x == 64) *a.hx->epoch += 1;
+                if (threadIdx.x == 64) {
+                    if (a.mode == 0) {
+                        const int s = *a.step;
+                        for (int m = 0; m < a.M; m++) {
+                            a.ids_ring[(size_t)(s + 1) * a.batch + m] = (uint32_t)am_i[m];
+                            a.pos[m] += 1;
+                        }
+                        *a.step = s + 1;
+                    } else {
+                        *a.next_id = (uint32_t)am_i[a.M - 1];
+                    }
+                    *a.am_count = 0u;
+                    __threadfence();
+                }
+            }
+        }
+    }
+    if (g.ks > 1 && g.gpart == nullptr) {
+        // the K splits of this super-tile are one cluster: once every
+        // split's partial is in its shared memory, CTA r adds column blocks
+        // r, r + ks, ... over the cluster in rank order (deterministic) and
+        // runs their epilogue
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (warp >= 2) {
+            const int lr = 32 * (warp & 3) + lane, p = 128 * S + lr, warp_e = warp - 2;
+            float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
+            for (int cb = ksi; cb < N / 16; cb += g.ks) {
                 float v[16];
 #pragma unroll
-                for (int q = 0; q < 16; q++) v[q] = 0.f;
-                for (int c4 = cf; c4 <= cl; c4 += 4) {
-                    float4 t4[4][4];
+                for (int j = 0; j < 16; j++) v[j] = 0.f;
+                for (int k = 0; k < g.ks; k++) {
+                    const float4* src =
+                        reinterpret_cast<const float4*>(cluster.map_shared_rank(part, k) + (size_t)lr * (N + 4) + cb * 16);
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int cc = min(c4 + u, cl);
-                        const float4* src = reinterpret_cast<const float4*>(
-                            g.gpart + ((size_t)sk_slot(cc, S, kc, T, G) * ncb * 128 + (size_t)cb * 128 + lr) * 16);
-#pragma unroll
-                        for (int q = 0; q < 4; q++) t4[u][q] = __ldcg(src + q);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        if (c4 + u > cl) break;
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            v[4 * q] += t4[u][q].x;
-                            v[4 * q + 1] += t4[u][q].y;
-                            v[4 * q + 2] += t4[u][q].z;
-                            v[4 * q + 3] += t4[u][q].w;
-                        }
+                    for (int j = 0; j < 4; j++) {
+                        const float4 x = src[j];
+                        v[4 * j] += x.x;
+                        v[4 * j + 1] += x.y;
+                        v[4 * j + 2] += x.z;
+                        v[4 * j + 3] += x.w;
                     }
                 }
                 tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
             }
-            if (threadIdx.x == 64) g.gcnt[S] = 0;
-            if (EPI == EPI_LOGITS) sk_logits_tile_done(g, am_v, am_i, &s_done);
         }
+        cluster.sync();  // peers are done reading this CTA's partial
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -696,72 +681,75 @@ int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* o
 
 size_t gemm_smem_bytes(int n, int stages, int c) { return (size_t)stages * c * (kStageA + (size_t)n * 128) + 1024; }
 
-int gemm_chunks_per_stage(int n) { return n <= 128 ? 2 : 1; }
-
-int gemm_pick_stages(int n, int c) {
-    // One CTA per SM: as many stages as fit the ~200 KB budget (8 at N <= 64:
-    // 128 KB of weights in flight per SM; 4 at N = 256).  RENG_GEMM_STAGES
-    // caps it (a tuning knob).
-    static const int cap = [] {
-        const char* v = getenv("RENG_GEMM_STAGES");
+int gemm_chunks_per_stage(int n) {
+    static const int fixed = [] {  // RENG_GEMM_C: chunks per stage, 1 or 2 (a tuning knob)
+        const char* v = getenv("RENG_GEMM_C");
         const int x = v ? atoi(v) : 0;
-        return x >= 2 && x <= kGemmMaxStages ? x : kGemmMaxStages;
+        return x == 1 || x == 2 ? x : 0;
     }();
-    int s = (int)((unsigned)kGemmStageBudget / ((unsigned)c * (kStageA + (unsigned)n * 128u)));
-    if (s > cap) s = cap;
-    return s < 2 ? 2 : s;
+    return fixed ? fixed : 2;
+    (void)n;
 }
 
-void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, int* c) {
-    // Fewer super-tiles than SMs (the 4096-row projections: 32): ks CTAs
-    // per super-tile, so each is split in ks shares (about kc / ks chunks)
-    // that finish together and whose partials the last CTA reads in one go;
-    // at N >= 128 at most 2 (a 128 x N partial is 64-128 KB, as large as 4-8
-    // chunks of weights).  Otherwise one CTA per SM, each super-tile split
-    // in at most 2-3 shares.
-    long long G;
-    if (super_tiles >= sms) {
-        G = sms;
-    } else {
-        int ks = sms / super_tiles;
-        static const int cap_env = [] {  // RENG_GEMM_KS: a tuning knob for the shares cap
-            const char* v = getenv("RENG_GEMM_KS");
-            const int x = v ? atoi(v) : 0;
-            return x >= 1 && x <= 8 ? x : 0;
-        }();
-        const int cap = cap_env ? cap_env : (n >= 128 ? 2 : 4);
-        if (ks > cap) ks = cap;
-        if (ks > kc) ks = kc;
-        if (ks < 1) ks = 1;
-        G = (long long)super_tiles * ks;
-    }
-    const long long T = (long long)super_tiles * kc;
-    *grid = (int)(T < G ? T : G);
-    *c = gemm_chunks_per_stage(n);
-    *stages = gemm_pick_stages(n, *c);
+int gemm_pick_stages(int n, bool one_per_sm, int epi, int c) {
+    // Two CTAs per SM (no cluster): as many stages as fit in half the SM's
+    // 228 KB beside the kernel's static shared memory, the 1 KB alignment
+    // slack and the 1 KB per-CTA reservation (6 at N = 16, 5 at N = 32, 4 at
+    // N = 64; one fewer for the LM head's argmax scratch).  One CTA per SM:
+    // 4 stages; measured on B200 (Llama-8B widths, 64 rows), 8 stages at one
+    // CTA per SM were slower than 4 (q/k/v 55 against 33 us).
+    // stages of c chunks: the same bytes in flight as c x as many one-chunk stages
+    const unsigned stage = (unsigned)c * (kStageA + (unsigned)n * 128u);
+    const unsigned fixed = 2048u + (epi == EPI_LOGITS ? 9216u : 1024u);
+    static const int one_sm = [] {  // RENG_GEMM_STAGES1: stages at one CTA per SM (a tuning knob)
+        const char* v = getenv("RENG_GEMM_STAGES1");
+        const int x = v ? atoi(v) : 0;
+        return x >= 2 && x <= kGemmMaxStages ? x : 4;
+    }();
+    int s = one_per_sm ? (one_sm + c - 1) / c : (int)((114u * 1024u - fixed) / stage);
+    const int fit = (int)((unsigned)kGemmStageBudget / stage);
+    if (s > fit) s = fit;
+    return s < 2 ? 2 : (s > kGemmMaxStages ? kGemmMaxStages : s);
 }
-
-size_t gemm_scratch_floats(int grid, int n) { return (size_t)2 * grid * n * 128; }
 
 template <int EPI>
 static cudaError_t launch_tc_t(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, bool pdl,
                                cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    cfg.gridDim = dim3(g.grid);
+    cudaLaunchAttribute attr[2];
+    cfg.gridDim = dim3(g.super_tiles * g.ks);
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C);
     cfg.stream = st;
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 0;
+    if (g.ks > 1 && g.gpart == nullptr) {  // the K splits of a super-tile form one cluster
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = g.ks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemm_sk<EPI>, map, wmap, g);
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, map, wmap, g);
 }
 
+// The largest dynamic shared memory any launch uses, and the whole of the
+// SM's unified L1/shared storage as shared memory, so that two ~100 KB CTAs
+// (N <= 64) fit on one SM (the default carveout sizes the SM for one block).
 template <int EPI>
 static cudaError_t prepare_t() {
-    return cudaFuncSetAttribute(k_gemm_sk<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmMaxDynSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kGemmMaxDynSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    return e;
 }
 
 cudaError_t gemm_prepare() {
@@ -773,13 +761,43 @@ cudaError_t gemm_prepare() {
     return e;
 }
 
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks_out, int* stages_out,
+               bool* gsplit_out, int* c_out) {
+    // Enough super-tiles to occupy the SMs (or the LM head, whose argmax
+    // needs whole rows per CTA): one CTA per super-tile, two per SM at N <= 64.
+    // Else split K over up to 8 CTAs.  At N = 16 the splits are plain CTAs
+    // adding their partials through global scratch, two per SM with 6-stage
+    // pipelines; wider, they form a cluster adding over shared memory
+    // (clusters of these kernels are scheduled one CTA per SM).  Measured on
+    // B200 (Llama-8B): down_proj at 8 rows 47 -> 30 us with plain splits (a
+    // cluster of 4 per super-tile, 128 CTAs of 4 stages, kept about 72 KB in
+    // flight per SM); at 64 rows plain splits lost (the last split reading
+    // 8 partials of 32 KB: b64 step 6.98 -> 9.55 ms).
+    int ks = 1;
+    const bool gsplit = gsplit_ok && n <= 16;
+    const int slots = gsplit ? 2 * sms : sms;
+    if (epi != EPI_LOGITS && super_tiles < sms) {
+        ks = slots / super_tiles;
+        ks = ks < 1 ? 1 : (ks > kc ? kc : ks);
+        if (ks > kGemmMaxSplits) ks = kGemmMaxSplits;
+        const int kper = (kc + ks - 1) / ks;
+        ks = (kc + kper - 1) / kper;  // every split gets at least one chunk
+    }
+    *ks_out = ks;
+    *gsplit_out = ks > 1 && gsplit;
+    *c_out = gemm_chunks_per_stage(n);
+    *stages_out = gemm_pick_stages(n, (ks > 1 && !gsplit) || n > 64, epi, *c_out);
+}
+
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
                            cudaStream_t st) {
-    const long long T = (long long)g.super_tiles * g.kc;
-    if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.grid < 1 || g.grid > T ||
-        g.C < 1 || g.C > 4 || g.stages < 2 || g.stages > kGemmMaxStages ||
-        gemm_smem_bytes(g.N, g.stages, g.C) > (size_t)kGemmMaxDynSmem || g.gpart == nullptr || g.gcnt == nullptr ||
-        g.super_tiles > kGemmCntMax || (g.b3d && g.kc * kChunkK != g.e.K))
+    if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
+        g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1) || g.stages < 2 || g.stages > kGemmMaxStages ||
+        g.C < 1 || g.C > 4 || (g.b3d && g.kc * kChunkK != g.e.K) ||
+        gemm_smem_bytes(g.N, g.stages, g.C) > (size_t)kGemmMaxDynSmem ||
+        (g.ks > 1 && g.gpart == nullptr &&
+         (size_t)g.stages * g.C * (kStageA + (size_t)g.N * 128) < (size_t)128 * (g.N + 4) * 4) ||
+        (g.gpart != nullptr && g.gcnt == nullptr))
         return cudaErrorInvalidValue;
     switch (epi) {
         case EPI_QKV: return launch_tc_t<EPI_QKV>(map, wmap, g, pdl, st);
@@ -871,7 +889,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     RENG_CHECK_ARG(w && x && y, "reng_gemm_bf16: NULL buffer");
     RENG_CHECK_ARG(rows >= 1 && K >= 8 && K % 8 == 0, "reng_gemm_bf16: rows >= 1 and K a positive multiple of 8");
     RENG_CHECK_ARG(M >= 1 && M <= kRowsCap, "reng_gemm_bf16: M must be in [1, 256]");
-    RENG_CHECK_ARG(splits >= -8 && splits <= 8 && iters >= 0 && (iters == 0 || ms_out),
+    RENG_CHECK_ARG(splits >= -kGemmMaxSplits && splits <= kGemmMaxSplits && iters >= 0 && (iters == 0 || ms_out),
                    "reng_gemm_bf16: bad splits / iters");
     RENG_CHECK_ARG(mem == RENG_MEM_HOST || mem == RENG_MEM_DEVICE, "reng_gemm_bf16: bad mem");
     const cudaMemcpyKind h2d = mem == RENG_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
@@ -923,19 +941,22 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
-    gemm_plan(g.super_tiles, kc, N, num_sms(dev), &g.grid, &g.stages, &g.C);
-    if (splits != 0) {
-        // that many CTAs per super-tile (capped by the chunks and the SMs):
-        // shares that split super-tiles in several ways, for checks
-        const long long T = (long long)g.super_tiles * kc;
-        long long want = (long long)g.super_tiles * (splits > 0 ? splits : -splits);
-        if (want > T) want = T;
-        if (want > num_sms(dev)) want = num_sms(dev);
-        g.grid = (int)want;
+    bool gsplit = false;
+    gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), true, &g.ks, &g.stages, &gsplit, &g.C);
+    if (splits != 0) {  // > 0: a cluster of that many splits; < 0: plain CTAs
+        int s = splits > 0 ? splits : -splits;
+        s = s > kc ? kc : s;
+        if (s > kGemmMaxSplits) s = kGemmMaxSplits;
+        const int kper = (kc + s - 1) / s;
+        g.ks = (kc + kper - 1) / kper;
+        gsplit = splits < 0 && g.ks > 1;
+        g.stages = gemm_pick_stages(N, (g.ks > 1 && !gsplit) || N > 64, EPI_F32, g.C);
     }
-    GEMM_CU(f.alloc(&g.gpart, gemm_scratch_floats(g.grid, N) * 4));
-    GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * 4));
-    GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * 4));
+    if (gsplit) {
+        GEMM_CU(f.alloc(&g.gpart, (size_t)g.super_tiles * g.ks * 128 * N * 4));
+        GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * 4));
+        GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * 4));
+    }
     CUtensorMap tmap, wmap;
     g.b3d = K % kChunkK == 0;
     int rc = g.b3d ? gemm_tensor_map3(xd, kRowsCap, K, N, g.C, &tmap) : gemm_tensor_map(xd, kRowsCap, K, N, &tmap);

@@ -7,22 +7,26 @@
 
 namespace reng {
 
-constexpr int kGemmRowsPerCta = 128;  // weight rows per MMA tile (the MMA's M)
-constexpr int kGemmCntMax = 4096;     // super-tiles of a launch (arrival counts)
+constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
+constexpr int kGemmMaxSplits = 8;     // K splits of a super-tile (a portable cluster)
+constexpr int kGemmCntMax = 1024;     // super-tiles of a split launch (arrival counts)
 
 struct GemmArgs {
     GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
     const uint8_t* w;         // packed bf16 blocks [tiles16][kc]
     int tiles16;              // 16-row tiles of the matrix
     int kc;                   // 64-k chunks
-    int super_tiles;          // ceil(tiles16 / 8): 128-row MMA tiles
+    int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
+    int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
     int N;                    // MMA N: activation rows rounded up to 16 (16..256)
     int stages;               // pipeline stages (2..8)
     int C;                    // 64-k chunks per stage (one weight copy, one activation copy)
     int b3d;                  // the activation map is 3-D ({64, N, C} boxes; K % 64 == 0), else 2-D per chunk
-    int grid;                 // persistent CTAs, each an equal share of the super_tiles x kc chunks
-    float* gpart;             // split super-tiles' f32 partials [2 * grid][N / 16][128][16]
-    int* gcnt;                // arrivals per super-tile (0 between launches)
+    // ks > 1 without a cluster: f32 partials [super_tiles][ks][128][N] and
+    // one arrival count per super-tile (0 between launches); null: the
+    // splits form a cluster and add their partials over shared memory
+    float* gpart;
+    int* gcnt;
 };
 
 // Tensor map of a row-major bf16 activation buffer [rows][K] read as
@@ -33,18 +37,17 @@ int gemm_tensor_map3(const uint16_t* x, int rows, int K, int n, int c, CUtensorM
 // Packed bf16 weights [tiles16][kc][2 KB] as {64, 16, 8 tiles, c chunks} boxes.
 int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out);
 size_t gemm_smem_bytes(int n, int stages, int c);
-// 64-k chunks per pipeline stage for MMA width n.
+// 64-k chunks per pipeline stage.
 int gemm_chunks_per_stage(int n);
-// Pipeline stages of c chunks at MMA width n: as many as fit about 200 KB.
-int gemm_pick_stages(int n, int c);
+// Pipeline stages of c chunks for MMA width n: as many as fit two CTAs per
+// SM, or at one CTA per SM the bytes in flight of 4 one-chunk stages.
+int gemm_pick_stages(int n, bool one_per_sm, int epi, int c);
 // Raise the dynamic shared-memory limit of every GEMM instantiation (call
 // once per device before capture).
 cudaError_t gemm_prepare();
-// Persistent grid (one CTA per SM, at most one per chunk), stages and
-// chunks per stage.
-void gemm_plan(int super_tiles, int kc, int n, int sms, int* grid, int* stages, int* c);
-// Floats of split-tile scratch a launch of `grid` CTAs at width n needs.
-size_t gemm_scratch_floats(int grid, int n);
+// K splits and pipeline stages of a launch over super_tiles x kc blocks.
+void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks, int* stages, bool* gsplit,
+               int* c);
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
                            cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.

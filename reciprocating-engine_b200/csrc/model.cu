@@ -61,9 +61,9 @@ struct reng_model {
     uint16_t* xn = nullptr;          // RMS-normalised rows, the x operand of the tcgen05 GEMMs
     int launches = 0;                // kernels of this library enqueued so far
     bool gemv8 = true;               // 3..8-row projections on the register-fragment GEMV (RENG_GEMV8=0: off)
-    float* gpart = nullptr;          // GEMM split-tile partials (2 slots per persistent CTA)
+    float* gpart = nullptr;          // GEMM split-K partials (splits without a cluster)
     size_t gpart_floats = 0;
-    int* gcnt = nullptr;             // GEMM arrivals per split super-tile
+    int* gcnt = nullptr;             // GEMM split-K arrivals per super-tile
     // the persistent decode step (one cooperative launch per step) when the
     // shape allows it, else the per-projection kernels
     bool step_on = false;
@@ -397,7 +397,16 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.kc = g.kc;
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
-    gemm_plan(a.super_tiles, g.kc, N, m->sms, &a.grid, &a.stages, &a.C);
+    bool gsplit = false;
+    gemm_plan(a.super_tiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit, &a.C);
+    if (gsplit) {
+        if ((size_t)a.super_tiles * a.ks * 128 * N > m->gpart_floats || a.super_tiles > kGemmCntMax)
+            return fail(RENG_E_STATE, "GEMM split-K scratch too small");
+        a.gpart = m->gpart;
+        a.gcnt = m->gcnt;
+    }
+    if (epi == EPI_LOGITS && (size_t)a.super_tiles > (size_t)m->lm_grid)
+        return fail(RENG_E_STATE, "LM head argmax partials too small");
     a.b3d = g.K % kChunkK == 0;
     CUtensorMap map, wmap;
     if (a.b3d)
@@ -405,10 +414,6 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     else
         TRY(gemm_tensor_map(x, kRowsCap, g.K, N, &map));
     TRY(gemm_weight_map(g.w, g.tiles, g.kc, a.C, &wmap));
-    if (gemm_scratch_floats(a.grid, N) > m->gpart_floats || a.super_tiles > kGemmCntMax)
-        return fail(RENG_E_STATE, "GEMM split-tile scratch too small");
-    a.gpart = m->gpart;
-    a.gcnt = m->gcnt;
     CU(launch_gemm_tc(map, wmap, a, epi, true, st));
     m->launches++;
     return RENG_OK;
@@ -978,8 +983,8 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
-    // GEMM split-tile partials: two 128 x N slots per persistent CTA (N <= kRowsCap)
-    m->gpart_floats = gemm_scratch_floats(m->sms, kRowsCap);
+    // split-K partials: at most two CTAs per SM of 128 rows x N <= 64
+    m->gpart_floats = (size_t)2 * m->sms * 128 * 64;
     TRY(dalloc(m, &m->gpart, m->gpart_floats));
     TRY(dalloc(m, &m->gcnt, (size_t)kGemmCntMax));
     CU(cudaMemsetAsync(m->gcnt, 0, (size_t)kGemmCntMax * 4, m->st));

@@ -23,24 +23,24 @@ def bits_to_f64(b):
     return (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
 
 
-# splits: 0 = the engine's persistent grid (one CTA per SM, at most one per
-# 64-k chunk); s != 0 = |s| CTAs per 128-row super-tile, so the stream-K
-# shares split super-tiles in other places (partials finished by the last
-# CTA to arrive)
+# splits: 0 = the engine's plan; s > 0 = a cluster of s CTAs per 128-row
+# super-tile adding their partials over shared memory; s < 0 = -s plain CTAs
+# adding theirs through global scratch, the last to arrive in split order
 @pytest.mark.parametrize("rows,K,M,splits", [
     (128, 64, 16, 1),        # one CTA, one k chunk
     (256, 512, 9, 1),        # M padded to N = 16
     (200, 200, 33, 0),       # ragged rows (16-row tiles, 128-row super-tiles) and K (zero fill past K)
-    (384, 1024, 64, 3),      # 3 shares per super-tile
-    (384, 1024, 24, -3),
-    (300, 1000, 8, -5),      # ragged rows and K, 5 shares per super-tile
+    (384, 1024, 64, 3),      # split K, a cluster of 3 adding over shared memory
+    (384, 1024, 24, -3),     # split K, 3 plain CTAs adding through global scratch
+    (300, 1000, 8, -5),      # ragged rows and K, 5 plain splits
     (1000, 576, 256, 0),     # N = 256, the widest MMA
-    (4096, 4096, 64, 0),     # Llama-8B o_proj widths: 32 super-tiles over all SMs
-    (4096, 14336, 8, 0),     # Llama-8B down_proj at batch 8
-    (512, 2048, 40, -4),     # N = 48
-    (128, 4096, 32, 8),      # one super-tile in 8 shares (8 partials in K order)
-    (8192, 512, 24, 0),      # 64 super-tiles of 8 chunks over every SM: shares end mid-tile
-    (2048, 2048, 256, 0),    # N = 256 with split super-tiles (4 stages, 512 TMEM columns)
+    (4096, 4096, 64, 0),     # Llama-8B o_proj widths, automatic splits
+    (4096, 14336, 8, 0),     # Llama-8B down_proj at batch 8: plain splits
+    (512, 2048, 40, -4),     # plain splits at N = 48
+    (128, 4096, 32, 8),      # one super-tile split 8 ways in a cluster
+    (8192, 520, 24, 0),      # 64 super-tiles, ragged K: an odd chunk count (units of 2 chunks and of 1)
+    (2048, 2048, 256, 0),    # N = 256 with split K
+    (256, 1000, 48, 3),      # ragged K with a cluster: per-chunk activation copies
 ])
 def test_gemm_matches_exact_sums(reng_lib, rows, K, M, splits):
     from reng.gemm import gemm_bf16
