@@ -157,15 +157,17 @@ def test_decode_matches_the_oracle(reng_lib, oracle_lib):
         assert np.array_equal(got[~nan], want[~nan])
 
 
+@pytest.mark.parametrize("product", ["1", "0"])
 @pytest.mark.parametrize("fmt", [0, 1])
 @pytest.mark.parametrize("scaling", [0, 2])
-def test_division_free_quotient_is_bit_exact(fp8, oracle_lib, monkeypatch, fmt, scaling):
-    """RENG_FP8_PRODUCT=1 (Markstein's correction of x * RN(1/s) in place
-    of the division, csrc/fp8_product.h): the config-0 matrix and the rows
-    of special values, bit for bit against the oracle's x / s."""
+def test_both_quotient_paths_are_bit_exact(fp8, oracle_lib, monkeypatch, fmt, scaling, product):
+    """The default division-free quotient (Markstein's correction of
+    x * RN(1/s), csrc/fp8_product.h) and the IEEE division it replaces
+    (RENG_FP8_PRODUCT=0): the config-0 matrix and the rows of special
+    values, bit for bit against the oracle's x / s."""
     import torch
     from reng.synth import f32_to_bf16_bits, fp8_config0_matrix
-    monkeypatch.setenv("RENG_FP8_PRODUCT", "1")
+    monkeypatch.setenv("RENG_FP8_PRODUCT", product)
     rows = cols = 4096
     w = fp8_config0_matrix(rows, cols, seed=99)
     co, so, bo = oracle_lib.quantize(w, rows, cols, fmt, scaling)
