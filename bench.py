@@ -349,6 +349,12 @@ def decode_measure(eng, args, B, prompt, dev, ws, rank, local, with_e2e=True, wi
         return [eng.prefill(b, prompt)[0] for b in range(B)]
 
     st = torch.cuda.Stream(device=dev)
+    clocks = Clocks(local) if with_clocks else None
+    if clocks:
+        # sampled from before the warm-up to the end of the timed steps: a
+        # timed region of tens of ms would otherwise fall between samples
+        clocks.start()
+        time.sleep(0.3)
     seeds = fresh()
     eng.decode(seeds, args.warmup)
     seeds = fresh()
@@ -356,12 +362,9 @@ def decode_measure(eng, args, B, prompt, dev, ws, rank, local, with_e2e=True, wi
     out_d = torch.empty((args.steps, B), dtype=torch.int32, device=dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(local) if with_clocks else None
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
     with torch.cuda.stream(st):
         torch.cuda.nvtx.range_push("decode_timed")  # the range launch-list captures select
         e0.record(st)
@@ -370,6 +373,8 @@ def decode_measure(eng, args, B, prompt, dev, ws, rank, local, with_e2e=True, wi
         torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop() if clocks else None
+    if clk is not None:
+        clk["window"] = "warm-up and timed decode steps"
     if ws > 1:
         dist.barrier()
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -626,7 +631,9 @@ def run_profile(args, cfg):
         steps through the step graph (device ms per step),
       * with --trace: the persistent step kernel's phase timeline,
       * with --quant N: N config-0 FP8 quantizations (bf16 [4096, 4096] ->
-        E4M3 per-channel) on device buffers.
+        E4M3 per-channel) on device buffers,
+      * with --gemm shapes: the tcgen05 GEMM alone (reng_gemm_bf16) on
+        random bf16 of those shapes, --iters launches.
     Prints one JSON line of device times; no bench line."""
     import torch
     from reng import fp8 as f
@@ -635,6 +642,22 @@ def run_profile(args, cfg):
     from reng.weights import random_weights
     torch.cuda.set_device(0)
     rep = {"model": args.model, "layers": args.layers, "batch": args.batch, "weights": args.weights}
+    if args.gemm:
+        import numpy as np
+        from reng.gemm import gemm_bf16
+        out = []
+        for spec in args.gemm.split(";"):
+            rows, K, M = (int(v) for v in spec.split(","))
+            rng = np.random.default_rng(1)
+            w = rng.integers(0x3c00, 0x3c80, size=(rows, K), dtype=np.uint16)  # bf16 in [1, 2)
+            x = rng.integers(0x3c00, 0x3c80, size=(M, K), dtype=np.uint16)
+            _, ms = gemm_bf16(w, x, splits=0, iters=args.iters)
+            out.append({"rows": rows, "K": K, "M": M, "us": round(ms * 1e3, 2),
+                        "weight_gbs": round(rows * K * 2 / (ms / 1e3) / 1e9, 1)})
+        rep = {"gemm": out, "timing": "reng_gemm_bf16 alone, %d back-to-back launches after one (CUDA "
+                                      "events, launch overhead included, weights resident in L2 when they fit)" % args.iters}
+        print(json.dumps(rep))
+        return
     if args.quant > 0:
         import numpy as np
         w = torch.from_numpy(fp8_config0_matrix(4096, 4096, seed=0).view(np.int16)).cuda()
@@ -709,6 +732,7 @@ def main():
     pg.add_argument("--trace", action="store_true")
     pg.add_argument("--no-kinds", dest="kinds", action="store_false")
     pg.add_argument("--quant", type=int, default=0, help="FP8 quantizations of the config-0 matrix")
+    pg.add_argument("--gemm", default="", help="rows,K,M[;rows,K,M...]: the tcgen05 GEMM alone on these shapes")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.extras is None:
