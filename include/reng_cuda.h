@@ -161,9 +161,7 @@ typedef struct reng_model_desc {
     int32_t qk_norm;        /* 1: per-head RMSNorm of q and k before RoPE (Qwen3,
                                model.rs:2962-3010); the layers carry qn / kn
                                [head_dim] gains, and attn_scale rides on qn, not
-                               on wq.  Gated: RENG_E_UNSUPPORTED unless the
-                               environment sets RENG_QK_NORM=1 (not yet
-                               parity-tested on a GPU).  0 otherwise. */
+                               on wq.  0 otherwise. */
 } reng_model_desc;
 
 /* One decoder layer's weights (layer.rs:16-136): bf16 [out, in] projections

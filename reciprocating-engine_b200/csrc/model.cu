@@ -284,13 +284,6 @@ int validate(const reng_model_desc* d) {
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights need the intermediate size per rank (" +
                                             std::to_string(d->inter / d->tp_world) + ") to be a multiple of 16");
     RENG_CHECK_ARG(d->qk_norm == 0 || d->qk_norm == 1, "reng_model_create: qk_norm must be 0 or 1");
-    if (d->qk_norm) {
-        // written and checked by reading, not yet parity-tested on a GPU
-        const char* g = getenv("RENG_QK_NORM");
-        if (!(g && atoi(g) == 1))
-            return fail(RENG_E_UNSUPPORTED, "reng_model_create: q/k norm models run with RENG_QK_NORM=1 only, "
-                                            "until their GPU parity run");
-    }
     if (d->weights == RENG_WEIGHTS_FP8_E4M3 && d->batch > kMaxRows)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights run batch <= " + std::to_string(kMaxRows) +
                                             ", not " + std::to_string(d->batch));

@@ -313,7 +313,7 @@ class LlamaConfig:
     # embedding one is applied at the gather), Phi-3 once its partial
     # rotation is permuted into the kernels' pair order, SmolLM3 with its
     # NoPE layers rotating nothing
-    ENGINE_TYPES = (None, "llama", "qwen2", "mistral", "granite", "phi3", "smollm3")
+    ENGINE_TYPES = (None, "llama", "qwen2", "qwen3", "mistral", "granite", "phi3", "smollm3")
 
     def unsupported(self, capacity=None):
         """What this engine's kernels do not compute for this config (empty

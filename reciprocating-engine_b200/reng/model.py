@@ -105,15 +105,10 @@ class Engine:
         missing = cfg.unsupported(capacity)
         layers = w.get("layers", ())
         qk = any(lw.get(k) is not None for lw in layers for k in ("qn", "kn"))
-        # q/k norm (Qwen3's per-head form) runs only with RENG_QK_NORM=1 until
-        # its GPU parity run; the library holds the same gate
-        qk_gate = os.environ.get("RENG_QK_NORM", "0") == "1"
-        if qk_gate:
-            missing = [x for x in missing if x != "model_type qwen3"]
-        if qk and not qk_gate:
-            missing = missing + ["q/k RMSNorm gains"]
-        elif qk and not all(lw.get(k) is not None and _numel(lw[k]) == cfg.head_dim()
-                            for lw in layers for k in ("qn", "kn")):
+        # q/k norm: Qwen3's per-head form runs (k_qk_norm); OLMo-2's
+        # whole-row form has no kernel
+        if qk and not all(lw.get(k) is not None and _numel(lw[k]) == cfg.head_dim()
+                          for lw in layers for k in ("qn", "kn")):
             missing = missing + ["whole-row q/k norm"]
         if any(lw.get(k) is not None for lw in layers for k in ("g_post_attn", "g_post_mlp")):
             missing = missing + ["branch-output norms"]

@@ -110,13 +110,12 @@ def test_config_json_round_trip_and_safetensors_loader(tmp_path):
         load_weights(str(tmp_path), cfg2)
 
 
-def test_qk_norm_gains_round_trip_and_are_refused_by_the_engine(tmp_path):
+def test_qk_norm_gains_round_trip(tmp_path):
     """q/k norm gains (Qwen3's [head_dim] form) survive save/load as the
-    reference reads them (crates/reng-model/src/lib.rs:1607-1609); an
-    engine given them refuses, whatever the model_type says, instead of
-    decoding without the norm."""
+    reference reads them (crates/reng-model/src/lib.rs:1607-1609); the
+    engine computes the norm wherever a layer carries them, whatever the
+    model_type says (tests/test_qk_norm_gpu.py)."""
     from reng.config import LlamaConfig
-    from reng.model import Engine
     from reng.weights import load_weights, random_weights, save_checkpoint
     cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2,
                       num_attention_heads=4, num_key_value_heads=2, head_dim_=16, vocab_size=96,
@@ -133,8 +132,6 @@ def test_qk_norm_gains_round_trip_and_are_refused_by_the_engine(tmp_path):
             assert np.array_equal(w2["layers"][l][k], w["layers"][l][k]), (l, k)
     as_llama = LlamaConfig.from_dict(dict(cfg.to_dict(), model_type="llama"))
     assert as_llama.unsupported(capacity=64) == []
-    with pytest.raises(ValueError, match="q/k RMSNorm"):
-        Engine(as_llama, w2, capacity=64)
     # a plain Llama checkpoint loads without them
     del w["layers"][0]["qn"], w["layers"][0]["kn"], w["layers"][1]["qn"], w["layers"][1]["kn"]
     save_checkpoint(str(tmp_path / "plain"), as_llama, w)
@@ -189,7 +186,6 @@ def test_engine_refuses_what_its_kernels_do_not_compute():
               LlamaConfig.from_dict(dict(base, model_type="qwen2", sliding_window=4096, use_sliding_window=False))):
         assert c.unsupported(capacity=8192) == []
     cases = [
-        (dict(base, model_type="qwen3"), "model_type qwen3"),
         (dict(base, model_type="olmo2"), "model_type olmo2"),
         (dict(base, model_type="llama", hidden_act="gelu_pytorch_tanh"), "activation"),
         (dict(base, model_type="llama", mlp_bias=True), "mlp_bias"),
@@ -294,22 +290,16 @@ def test_the_engine_scales_its_embedding_table_like_the_gather():
     assert got.dtype == torch.int16 and np.array_equal(got.numpy().view(np.uint16), want)
 
 
-def test_qk_norm_runs_only_behind_its_gate(monkeypatch):
-    """Qwen3's per-head q/k norm reaches the library only with
-    RENG_QK_NORM=1 (until its GPU parity run); the whole-row form (OLMo-2)
-    is refused either way.  Both refusals come before any device work."""
+def test_qk_norm_forms(monkeypatch):
+    """Qwen3's per-head q/k norm is a config the engine runs; the whole-row
+    form (OLMo-2) is refused before any device work."""
     from reng.config import LlamaConfig
     from reng.model import Engine
     base = {"hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 1,
             "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 16, "vocab_size": 32,
             "model_type": "qwen3"}
     cfg = LlamaConfig.from_dict(base)
-    head = {"qn": np.ones(16, np.float32), "kn": np.ones(16, np.float32)}
+    assert cfg.unsupported(capacity=64) == []
     wide = {"qn": np.ones(64, np.float32), "kn": np.ones(32, np.float32)}
-    monkeypatch.delenv("RENG_QK_NORM", raising=False)
-    with pytest.raises(ValueError, match="q/k RMSNorm"):
-        Engine(cfg, {"layers": [head], "embed": np.zeros((1, 1), np.uint16)}, capacity=64)
-    monkeypatch.setenv("RENG_QK_NORM", "1")
     with pytest.raises(ValueError, match="whole-row q/k norm"):
         Engine(cfg, {"layers": [wide], "embed": np.zeros((1, 1), np.uint16)}, capacity=64)
-    assert "model_type qwen3" in cfg.unsupported(capacity=64)   # the config rule itself is unchanged

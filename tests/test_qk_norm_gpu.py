@@ -1,4 +1,4 @@
-"""Qwen3's per-head q/k RMSNorm on the engine (RENG_QK_NORM=1): the q/k/v
+"""Qwen3's per-head q/k RMSNorm on the engine: the q/k/v
 launch writes raw q and k (identity rotation), k_qk_norm normalises each
 head, applies the gains (the attention scale riding on the q gain) and
 rotates; prefill logits and greedy decode against the f32 oracle's q/k-norm
@@ -9,7 +9,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_qwen3_qk_norm_matches_the_oracle(reng_lib, oracle_lib, monkeypatch):
+def test_qwen3_qk_norm_matches_the_oracle(reng_lib, oracle_lib):
     import oracle
     from test_decode_gpu import check_greedy, check_rows
     from reng.config import LlamaConfig
@@ -17,7 +17,6 @@ def test_qwen3_qk_norm_matches_the_oracle(reng_lib, oracle_lib, monkeypatch):
     from reng.rope import rope_caches_for
     from reng.synth import prompt_ids
     from reng.weights import random_weights
-    monkeypatch.setenv("RENG_QK_NORM", "1")
     cfg = LlamaConfig.from_dict(dict(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                                      num_attention_heads=4, num_key_value_heads=2, head_dim=64,
                                      vocab_size=1024, rms_norm_eps=1e-6, rope_theta=10000.0,
