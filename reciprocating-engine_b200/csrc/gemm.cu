@@ -38,6 +38,7 @@
 
 #include "gemm.cuh"
 #include "gemv_core.cuh"
+#include "tc.cuh"
 
 namespace reng {
 
@@ -48,100 +49,8 @@ constexpr int kGemmMaxStages = 8;  // pipeline stages (runtime: GemmArgs::stages
 constexpr int kGemmStageBudget = 200 * 1024;                  // stage bytes of a one-per-SM launch
 constexpr int kGemmMaxDynSmem = kGemmStageBudget + 2048;      // + the 1024-byte alignment slack
 constexpr int kStageA = 8 * kBlockBytesBf16;  // 128 rows x 64 k
-constexpr unsigned long long kGemmWaitNs = 2000000000ull;
+using namespace tc;
 
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
-    if (bar_try(bar, parity)) return true;
-    const unsigned long long t0 = gtimer();
-    while (!bar_try(bar, parity))
-        if (gtimer() - t0 > kGemmWaitNs) return false;
-    return true;
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ void tensor_g2s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void tensor_g2s_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
-                                              uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(dst),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void tensor_g2s_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
-                                              uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-        "[%6];" ::"r"(dst),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
-        : "memory");
-}
-// UMMA shared-memory descriptor: K-major, 128-byte swizzle, SBO 1024 B.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next 8-row atom
-    d |= (uint64_t)1 << 46;             // descriptor version (sm100)
-    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
-    return d;
-}
-// Instruction descriptor: f32 accumulate, bf16 A and B, both K-major, M=128.
-__device__ __forceinline__ uint32_t umma_idesc(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-__device__ __forceinline__ void umma(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-            tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
 __device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
@@ -676,6 +585,25 @@ int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* o
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled (weights) failed (" + std::to_string((int)r) + ")");
+    return RENG_OK;
+}
+
+// A layer's K or V cache [slot][kv head][cap][hd] bf16 as 2-D rows of hd
+// elements, read in {64, 128 rows} boxes with the 128-byte swizzle (the
+// tcgen05 operand layout of 128 keys x 64 head dims).  Rows past the last
+// slot read as zeros.
+int attn_cache_map(const uint16_t* cache, int hd, long long rows, CUtensorMap* out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (hd % 64 || rows < 1 || ((uintptr_t)cache & 15)) return fail(RENG_E_INVAL, "attn_cache_map: bad shape");
+    cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)cache, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled (cache) failed (" + std::to_string((int)r) + ")");
     return RENG_OK;
 }
 

@@ -479,8 +479,19 @@ AttnArgs attn_args(reng_model* m, int l, int M, int mode) {
     return at;
 }
 
+// Attention of a step.  Prefill blocks of 16 or more rows run the
+// tensor-core flash attention (attn_prefill.cu); decode steps and short
+// blocks the per-row kernel.  RENG_FLASH_PREFILL=0 keeps every block on the
+// per-row kernel (an A/B knob).
 int k_attn_launch(reng_model* m, int l, int M, int mode, cudaStream_t st) {
-    CU(launch_attn(attn_args(m, l, M, mode), kAttnChunk, true, st));
+    const AttnArgs a = attn_args(m, l, M, mode);
+    const long long rows = (long long)m->B * m->nkv * m->cap;
+    const char* env = getenv("RENG_FLASH_PREFILL");
+    if (mode == 1 && M >= 16 && !(env && atoi(env) == 0) && attn_prefill_fits(a, rows)) {
+        TRY(launch_attn_prefill(a, rows, m->err, st));
+    } else {
+        CU(launch_attn(a, kAttnChunk, true, st));
+    }
     m->launches++;
     return RENG_OK;
 }
