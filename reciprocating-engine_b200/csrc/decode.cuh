@@ -20,7 +20,8 @@ constexpr int kChunkK = 64;                 // k per block
 constexpr int kBlockBytesBf16 = 2048;
 constexpr int kBlockBytesFp8 = 1024;
 constexpr int kMaxRows = 8;    // activation rows per GEMV launch (mma N)
-constexpr int kRowsCap = 256;  // rows of a step (work buffers, RMS-partials stride)
+constexpr int kRowsCap = 256;  // decode slots of a step; the tcgen05 GEMM's N-tile
+constexpr int kBlockRows = 1024;  // rows of a prefill block (work buffers)
 constexpr size_t kGemvMaxSmem = 96 * 1024;  // x rows staged in shared memory up to this
 // RMS partials ss[m][tile] (sum of squares of 16 residual values), row
 // stride kSsStride: a row's partials are contiguous, so the kernels that

@@ -62,10 +62,11 @@ __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
 
 }  // namespace
 
-// Epilogue of 16 activation columns (m = cb*16 .. +16) of one weight row
-// (packed row p of the matrix, TMEM lane `lr` of the super-tile).
+// Epilogue of 16 activation columns of one weight row (packed row p of the
+// matrix, TMEM lane `lr` of the super-tile): columns cb*16 .. +16 of the
+// CTA's N-tile, activation rows m = n0 + cb*16 .. +16 of the launch.
 template <int EPI>
-__device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, int cb, const float (&v)[16],
+__device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, int cb, int n0, const float (&v)[16],
                                               float* am_v, int* am_i, int warp_e) {
     const GemvArgs& a = g.e;
     const int lane = lr & 31;
@@ -79,12 +80,12 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
         uint16_t xo[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            const int m = cb * 16 + j;
+            const int m = n0 + cb * 16 + j;
             xo[j] = (valid && m < a.M) ? __ldcg(a.out + (size_t)m * a.ldo + p) : (uint16_t)0;
         }
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            const int m = cb * 16 + j;
+            const int m = n0 + cb * 16 + j;
             const bool live = valid && m < a.M;
             float sq = 0.f;
             if (live) {
@@ -129,7 +130,7 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
         int pos[16], slot[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            const int m = cb * 16 + j;
+            const int m = n0 + cb * 16 + j;
             const bool live = valid && m < a.M;
             pos[j] = live ? a.row_pos[m] : a.cap;
             slot[j] = live ? a.row_slot[m] : 0;
@@ -143,7 +144,7 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
         }
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            const int m = cb * 16 + j;
+            const int m = n0 + cb * 16 + j;
             const float partner = __shfl_xor_sync(0xffffffffu, v[j], 8);
             if (pos[j] >= a.cap) continue;  // also the rows past M and past the matrix
             if (rope) {
@@ -162,7 +163,7 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
     }
 #pragma unroll
     for (int j = 0; j < 16; j++) {
-        const int m = cb * 16 + j;
+        const int m = n0 + cb * 16 + j;
         const bool live = valid && m < a.M;
         if (EPI == EPI_F32) {
             if (live) a.out_f32[(size_t)m * a.ldo + p] = v[j];
@@ -191,9 +192,9 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 am_take2(bv, bi, ov, oi);
             }
-            if (lane == 0) {
-                am_v[warp_e * kRowsCap + m] = bv;
-                am_i[warp_e * kRowsCap + m] = bi;
+            if (lane == 0) {  // per-CTA slots of the N-tile's columns
+                am_v[warp_e * kRowsCap + m - n0] = bv;
+                am_i[warp_e * kRowsCap + m - n0] = bi;
             }
         }
     }
@@ -210,7 +211,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
     __shared__ int am_i[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = blockIdx.x / g.ks, ksi = blockIdx.x % g.ks;
+    // CTA -> (super-tile S, N-tile nt, K split ksi); the N-tiles of a
+    // super-tile are neighbours, so its weight tiles are read from HBM once
+    // and from L2 by the others
+    const int ksi = blockIdx.x % g.ks, t_sn = blockIdx.x / g.ks;
+    const int S = t_sn / g.ntiles, n0 = (t_sn % g.ntiles) * g.N;
     const int kper = (g.kc + g.ks - 1) / g.ks;
     const int kb = min(g.kc, ksi * kper), ke = min(g.kc, kb + kper), nk = ke - kb;
     // each super-tile walks its k range from a different starting chunk, so
@@ -278,10 +283,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                 unit(i, c0, cnt);
                 const uint32_t dst = smem0 + (uint32_t)(i % SG) * stage_bytes + b_off;
                 if (g.b3d) {
-                    tensor_g2s_3d(dst, &tmap_x, 0, 0, c0, bar_full + 8 * (i % SG));
+                    tensor_g2s_3d(dst, &tmap_x, 0, n0, c0, bar_full + 8 * (i % SG));
                 } else {
                     for (int q = 0; q < cnt; q++)
-                        tensor_g2s(dst + (uint32_t)q * tx_b, &tmap_x, (c0 + q) * kChunkK, 0, bar_full + 8 * (i % SG));
+                        tensor_g2s(dst + (uint32_t)q * tx_b, &tmap_x, (c0 + q) * kChunkK, n0, bar_full + 8 * (i % SG));
                 }
             };
             auto tx_of = [&](int i) {
@@ -372,14 +377,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                 if (zero)
 #pragma unroll
                     for (int j = 0; j < 16; j++) v[j] = 0.f;
-                tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                tc_epilogue16<EPI>(g, p, lr, cb, n0, v, am_v, am_i, warp_e);
             }
         } else if (g.gpart != nullptr) {
             // split K without a cluster: this split's partial to global
             // scratch [super-tile][split][128][N]; the last split of the
             // super-tile to arrive adds all of them in split order
             // (deterministic) and runs the epilogue
-            float* mine = g.gpart + (((size_t)S * g.ks + ksi) * 128 + lr) * N;
+            float* mine = g.gpart + (((size_t)t_sn * g.ks + ksi) * 128 + lr) * N;
             for (int cb = 0; cb < N / 16; cb++) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             }
             __threadfence();
             named_sync_epilogue();
-            if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + S, 1) == g.ks - 1;
+            if (threadIdx.x == 64) s_flag = atomicAdd(g.gcnt + t_sn, 1) == g.ks - 1;
             named_sync_epilogue();
             if (s_flag) {
                 __threadfence();
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                     for (int j = 0; j < 16; j++) v[j] = 0.f;
                     for (int k = 0; k < g.ks; k++) {
                         const float4* src =
-                            reinterpret_cast<const float4*>(g.gpart + (((size_t)S * g.ks + k) * 128 + lr) * N + cb * 16);
+                            reinterpret_cast<const float4*>(g.gpart + (((size_t)t_sn * g.ks + k) * 128 + lr) * N + cb * 16);
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
                             const float4 x = __ldcg(src + j);
@@ -411,9 +416,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                             v[4 * j + 3] += x.w;
                         }
                     }
-                    tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                    tc_epilogue16<EPI>(g, p, lr, cb, n0, v, am_v, am_i, warp_e);
                 }
-                if (threadIdx.x == 64) g.gcnt[S] = 0;
+                if (threadIdx.x == 64) g.gcnt[t_sn] = 0;
             }
         } else {
             // split K: this split's partial into the (finished) stage buffers,
@@ -433,12 +438,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             // CTA partials of every row: best over the 4 epilogue warps
             named_sync_epilogue();
             const GemvArgs& a = g.e;
-            // this CTA's best per row into the rows' running maxima
-            for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+            // this CTA's best per row of its N-tile into the rows' running maxima
+            for (int ml = threadIdx.x - 64; ml < min(N, a.M - n0); ml += 128) {
                 float bv = -INFINITY;
                 int bi = 0x7fffffff;
-                for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + m], am_i[w * kRowsCap + m]);
-                atomicMax(a.am_key + m, am_pack(bv, bi));
+                for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + ml], am_i[w * kRowsCap + ml]);
+                atomicMax(a.am_key + n0 + ml, am_pack(bv, bi));
             }
             __threadfence();
             named_sync_epilogue();
@@ -497,7 +502,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
                         v[4 * j + 3] += x.w;
                     }
                 }
-                tc_epilogue16<EPI>(g, p, lr, cb, v, am_v, am_i, warp_e);
+                tc_epilogue16<EPI>(g, p, lr, cb, n0, v, am_v, am_i, warp_e);
             }
         }
         cluster.sync();  // peers are done reading this CTA's partial
@@ -645,7 +650,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const CUtensorMap& wmap, 
                                cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
-    cfg.gridDim = dim3(g.super_tiles * g.ks);
+    cfg.gridDim = dim3(g.super_tiles * g.ntiles * g.ks);
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C);
     cfg.stream = st;
@@ -719,7 +724,8 @@ void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok,
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
                            cudaStream_t st) {
-    if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.e.M > g.N || g.e.M < 1 || g.ks < 1 ||
+    if (g.N % 16 || g.N < 16 || g.N > kRowsCap || g.ntiles < 1 || (g.ntiles > 1 && g.N != kRowsCap) ||
+        g.e.M > g.N * g.ntiles || g.e.M > kGemmRowsMax || g.e.M < 1 || g.ks < 1 ||
         g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1) || g.stages < 2 || g.stages > kGemmMaxStages ||
         g.C < 1 || g.C > 4 || (g.b3d && g.kc * kChunkK != g.e.K) ||
         gemm_smem_bytes(g.N, g.stages, g.C) > (size_t)kGemmMaxDynSmem ||
@@ -869,6 +875,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
+    g.ntiles = 1;
     bool gsplit = false;
     gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), true, &g.ks, &g.stages, &gsplit, &g.C);
     if (splits != 0) {  // > 0: a cluster of that many splits; < 0: plain CTAs

@@ -10,6 +10,8 @@ namespace reng {
 constexpr int kGemmRowsPerCta = 128;  // weight rows per CTA (the MMA's M)
 constexpr int kGemmMaxSplits = 8;     // K splits of a super-tile (a portable cluster)
 constexpr int kGemmCntMax = 1024;     // super-tiles of a split launch (arrival counts)
+constexpr int kGemmRowsMax = kBlockRows;  // activation rows of a launch (N-tiles of kRowsCap)
+static_assert(kGemmRowsMax <= 4 * kRowsCap, "the LM head's argmax scratch holds 4 * kRowsCap rows");
 
 struct GemmArgs {
     GemvArgs e;               // epilogue arguments (M, outputs, RoPE, cache, argmax ...)
@@ -18,7 +20,8 @@ struct GemmArgs {
     int kc;                   // 64-k chunks
     int super_tiles;          // ceil(tiles16 / 8): 128-row CTA tiles
     int ks;                   // K splits (every split gets >= 1 chunk): one cluster per super-tile
-    int N;                    // MMA N: activation rows rounded up to 16 (16..256)
+    int N;                    // MMA N: activation rows rounded up to 16 (16..256), kRowsCap when ntiles > 1
+    int ntiles;               // N-tiles: CTA (super-tile, N-tile) multiplies activation rows nt*N .. +N
     int stages;               // pipeline stages (2..8)
     int C;                    // 64-k chunks per stage (one weight copy, one activation copy)
     int b3d;                  // the activation map is 3-D ({64, N, C} boxes; K % 64 == 0), else 2-D per chunk

@@ -70,7 +70,7 @@ struct reng_model {
     int step_grid = 0;
     StepCtl step_ctl{};
     float* ss = nullptr;
-    float* part = nullptr;  // tensor-parallel f32 partials [kRowsCap][hidden]
+    float* part = nullptr;  // tensor-parallel f32 partials [kBlockRows][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
     int* err = nullptr;  // device error word of the bounded waits
     int w8 = 0;          // projections held as FP8-E4M3 codes + row scales
@@ -78,7 +78,7 @@ struct reng_model {
     float* am_val = nullptr;
     int* am_idx = nullptr;
     unsigned int* am_count = nullptr;
-    unsigned long long* am_key = nullptr;  // [kRowsCap] LM-head argmax keys
+    unsigned long long* am_key = nullptr;  // [kBlockRows] LM-head argmax keys
     int lm_grid = 0;
     // GEMV launch shapes per kind (qkv, o, gate/up, down, LM head), for
     // M <= 2 and M > 2 activation rows
@@ -87,7 +87,7 @@ struct reng_model {
     cudaGraphExec_t graph_full = nullptr;  // the step with the whole LM head (logits requests) when `graph` shards it
     int kernels_per_step = 0;
     std::vector<int> host_pos;
-    uint32_t* pinned = nullptr;  // pinned staging: ids [kRowsCap], positions [kRowsCap], error word
+    uint32_t* pinned = nullptr;  // pinned staging: ids [kBlockRows], positions [kRowsCap], error word
     size_t bytes = 0;
     std::vector<void*> allocs;
     reng_step_times times{};
@@ -98,10 +98,11 @@ struct reng_model {
 
 namespace {
 
-// pinned staging words: ids [0, kRowsCap), positions, the device error word
-constexpr int kPinnedPos = kRowsCap;
-constexpr int kPinnedErr = 2 * kRowsCap;
-constexpr int kPinnedWords = 2 * kRowsCap + 16;
+// pinned staging words: a prefill block's ids [0, kBlockRows), the slots'
+// positions, the device error word
+constexpr int kPinnedPos = kBlockRows;
+constexpr int kPinnedErr = kBlockRows + kRowsCap;
+constexpr int kPinnedWords = kBlockRows + kRowsCap + 16;
 
 template <typename T>
 int dalloc(reng_model* m, T** p, size_t count) {
@@ -365,7 +366,8 @@ bool use_gemm(const reng_model* m, int M, int kind) {
 
 // One projection: the GEMV for few rows, else (RMSNorm of x into xn when the
 // projection normalises its input) the tcgen05 GEMM over N = M rounded up
-// to 16 columns.  kind indexes the GEMV launch shapes.
+// to 16 columns, in N-tiles of kRowsCap columns beyond that (prefill blocks
+// of up to kBlockRows rows).  kind indexes the GEMV launch shapes.
 int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cudaStream_t st) {
     if (!use_gemm(m, g.M, kind)) {
         if (m->gemv8 && gemv8_fits(g)) {
@@ -382,7 +384,7 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
         m->launches++;
         x = m->xn;
     }
-    const int N = (g.M + 15) / 16 * 16;
+    const int N = g.M > kRowsCap ? kRowsCap : (g.M + 15) / 16 * 16;
     GemmArgs a{};
     a.e = g;
     a.w = g.w;
@@ -390,10 +392,12 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.kc = g.kc;
     a.super_tiles = (g.tiles + 7) / 8;
     a.N = N;
+    a.ntiles = (g.M + N - 1) / N;
     bool gsplit = false;
-    gemm_plan(a.super_tiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit, &a.C);
+    gemm_plan(a.super_tiles * a.ntiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit, &a.C);
     if (gsplit) {
-        if ((size_t)a.super_tiles * a.ks * 128 * N > m->gpart_floats || a.super_tiles > kGemmCntMax)
+        if ((size_t)a.super_tiles * a.ntiles * a.ks * 128 * N > m->gpart_floats ||
+            a.super_tiles * a.ntiles > kGemmCntMax)
             return fail(RENG_E_STATE, "GEMM split-K scratch too small");
         a.gpart = m->gpart;
         a.gcnt = m->gcnt;
@@ -403,9 +407,9 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.b3d = g.K % kChunkK == 0;
     CUtensorMap map, wmap;
     if (a.b3d)
-        TRY(gemm_tensor_map3(x, kRowsCap, g.K, N, a.C, &map));
+        TRY(gemm_tensor_map3(x, kBlockRows, g.K, N, a.C, &map));
     else
-        TRY(gemm_tensor_map(x, kRowsCap, g.K, N, &map));
+        TRY(gemm_tensor_map(x, kBlockRows, g.K, N, &map));
     TRY(gemm_weight_map(g.w, g.tiles, g.kc, a.C, &wmap));
     CU(launch_gemm_tc(map, wmap, a, epi, true, st));
     m->launches++;
@@ -951,7 +955,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->vcache, m->layer_kv * m->L));
     CU(cudaMemsetAsync(m->kcache, 0, m->layer_kv * m->L * 2, m->st));
     CU(cudaMemsetAsync(m->vcache, 0, m->layer_kv * m->L * 2, m->st));
-    const int MR = kRowsCap;
+    const int MR = kBlockRows;
     TRY(dalloc(m, &m->x_res, (size_t)MR * H));
     TRY(dalloc(m, &m->qbuf, (size_t)MR * m->q_dim));
     TRY(dalloc(m, &m->xn, (size_t)MR * H));
@@ -983,8 +987,8 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
         m->gemv8 = !(v && atoi(v) == 0);
     }
     m->lm_grid = m->sms * 32;  // argmax partial slots: an upper bound of the persistent grid
-    TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * MR));
-    TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * MR));
+    TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * kRowsCap));
+    TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * kRowsCap));
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
     // split-K partials: at most two CTAs per SM of 128 rows x N <= 64
@@ -992,8 +996,8 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     TRY(dalloc(m, &m->gpart, m->gpart_floats));
     TRY(dalloc(m, &m->gcnt, (size_t)kGemmCntMax));
     CU(cudaMemsetAsync(m->gcnt, 0, (size_t)kGemmCntMax * 4, m->st));
-    TRY(dalloc(m, &m->am_key, (size_t)kRowsCap));
-    CU(cudaMemsetAsync(m->am_key, 0, (size_t)kRowsCap * 8, m->st));
+    TRY(dalloc(m, &m->am_key, (size_t)kBlockRows));
+    CU(cudaMemsetAsync(m->am_key, 0, (size_t)kBlockRows * 8, m->st));
     CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
     m->host_pos.assign(m->B, 0);
     CU(cudaStreamSynchronize(m->st));
@@ -1002,10 +1006,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     return RENG_OK;
 }
 
-// Prompt rows per prefill block: kRowsCap on the GEMM path (bf16), the GEMV
-// width for FP8 weights; RENG_PREFILL_ROWS lowers it (a tuning knob).
+// Prompt rows per prefill block: kBlockRows on the GEMM path (bf16), the
+// GEMV width for FP8 weights; RENG_PREFILL_ROWS lowers it (a tuning knob).
 int prefill_rows(const reng_model* m) {
-    int r = m->w8 ? kMaxRows : kRowsCap;
+    int r = m->w8 ? kMaxRows : kBlockRows;
     const char* v = getenv("RENG_PREFILL_ROWS");
     if (v) {
         const int x = atoi(v);
@@ -1038,7 +1042,7 @@ int check_device_error(reng_model* m) {
         CU(cudaMemsetAsync(m->err, 0, 4, m->st));
         // a launch that gave up may leave arrival counts and argmax keys mid-count
         CU(cudaMemsetAsync(m->gcnt, 0, (size_t)kGemmCntMax * 4, m->st));
-        CU(cudaMemsetAsync(m->am_key, 0, (size_t)kRowsCap * 8, m->st));
+        CU(cudaMemsetAsync(m->am_key, 0, (size_t)kBlockRows * 8, m->st));
         CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
         CU(cudaStreamSynchronize(m->st));
         if (m->step_on) {  // a step that gave up may leave the barrier mid-count

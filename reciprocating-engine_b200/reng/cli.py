@@ -204,9 +204,10 @@ _ROWS_SAVED = []
 
 
 def _set_rows(rows):
-    """RENG_PREFILL_ROWS = --rows when below the engine's 256 (the library
-    reads it at every prefill); `_run` puts the old value back when the
-    command ends, so later engines of the process keep their default."""
+    """RENG_PREFILL_ROWS = --rows when below the reference's default of 256
+    (the library reads it at every prefill; at the default the engine runs
+    its own blocks of up to 1024 rows); `_run` puts the old value back when
+    the command ends, so later engines of the process keep their default."""
     if rows < DEFAULT_ROWS:
         _ROWS_SAVED.append(os.environ.get("RENG_PREFILL_ROWS"))
         os.environ["RENG_PREFILL_ROWS"] = str(rows)

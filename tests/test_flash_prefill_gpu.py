@@ -4,9 +4,10 @@ for prefill blocks (RENG_FLASH_PREFILL=0).
 
 A tile packs a KV group's query heads times 128 / heads-per-group positions
 into the MMA's 128 rows, so the shapes cover 2, 3, 4 and 5 heads per group
-(tiles of 128, 126, 128 and 125 rows) at head_dim 64 and 128, and prompts of
-several 256-row blocks whose later blocks start mid-tile (the causal mask
-inside a key tile, keys of earlier blocks read back from the cache).
+(tiles of 128, 126, 128 and 125 rows) at head_dim 64 and 128.  Each prompt
+runs as one block and, with RENG_PREFILL_ROWS=256, as several 256-row blocks
+whose later blocks start mid-tile (the causal mask inside a key tile, keys
+of earlier blocks read back from the cache).
 """
 import numpy as np
 import pytest
@@ -31,8 +32,10 @@ def _cfg(hidden, nh, nkv, hd):
                        rms_norm_eps=1e-5, rope_theta=10000.0, tie_word_embeddings=False, model_type="llama")
 
 
+@pytest.mark.parametrize("rows", [None, 256])
 @pytest.mark.parametrize("hidden,nh,nkv,hd,n", SHAPES)
-def test_flash_prefill_matches_the_oracle_and_the_per_row_kernel(reng_lib, monkeypatch, hidden, nh, nkv, hd, n):
+def test_flash_prefill_matches_the_oracle_and_the_per_row_kernel(reng_lib, monkeypatch, hidden, nh, nkv, hd, n,
+                                                                 rows):
     from reng.model import Engine
     from reng.rope import rope_caches_for
     from reng.synth import prompt_ids
@@ -50,6 +53,8 @@ def test_flash_prefill_matches_the_oracle_and_the_per_row_kernel(reng_lib, monke
         e.close()
         return allg, [nxt] + [int(x) for x in ids]
 
+    if rows:
+        monkeypatch.setenv("RENG_PREFILL_ROWS", str(rows))
     monkeypatch.delenv("RENG_FLASH_PREFILL", raising=False)
     flash, ids_flash = run()
     monkeypatch.setenv("RENG_FLASH_PREFILL", "0")
@@ -64,7 +69,7 @@ def test_flash_prefill_matches_the_oracle_and_the_per_row_kernel(reng_lib, monke
 
 
 def test_flash_prefill_long_prompt_in_several_blocks(reng_lib):
-    """1500 tokens: six prefill blocks, the last ones walking 12 key tiles."""
+    """1500 tokens: a 1024-row block, then 476 rows walking 12 key tiles."""
     from reng.model import Engine
     from reng.rope import rope_caches_for
     from reng.synth import prompt_ids

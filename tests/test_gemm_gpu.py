@@ -112,19 +112,22 @@ def test_wide_batch_step_logits(reng_lib):
     e.close()
 
 
-@pytest.mark.parametrize("n", [300, 37])
+@pytest.mark.parametrize("n", [300, 37, 700, 1100])
 def test_long_prefill_in_gemm_blocks(reng_lib, n):
-    """Prefill blocks of 256 rows (+ the rest) with every row's logits."""
+    """Prefill blocks of up to 1024 rows (+ the rest) with every row's
+    logits: the GEMMs run N-tiles of 256 activation rows (700 rows: a last
+    N-tile of 188; 1100: a full block of four N-tiles, then 76 rows)."""
     from reng.model import Engine
     from reng.rope import rope_caches_for
     from reng.synth import prompt_ids
     from reng.weights import random_weights
     cfg = small_cfg(bias=True)
     w = random_weights(cfg, seed=42)
-    e = Engine(cfg, w, batch=1, capacity=320)
+    cap = max(320, n + 16)
+    e = Engine(cfg, w, batch=1, capacity=cap)
     prompt = prompt_ids(n, cfg.vocab_size, seed=8)
     nxt, last, allg = e.prefill(0, prompt, last_logits=True, all_logits=True)
-    sin, cos = rope_caches_for(cfg, 320)
+    sin, cos = rope_caches_for(cfg, cap)
     want = oracle_for(cfg, w).forward(prompt, sin, cos)
     check_rows(allg, want, "prefill")
     assert np.array_equal(last, allg[-1])
