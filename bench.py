@@ -627,6 +627,8 @@ def run_profile(args, cfg):
       * each kernel kind alone on the model's stream `--iters` times,
         cycling over the layers (reng_model_time_kernels; not with
         --no-kinds), after `--ctx` prompt tokens in every slot,
+      * with --rows R: the same at a prefill block of R rows of slot 0
+        (after a --ctx prompt), attention in its prefill form,
       * with --decode-steps N: a 16-token prompt in every slot and N greedy
         steps through the step graph (device ms per step),
       * with --trace: the persistent step kernel's phase timeline,
@@ -686,6 +688,11 @@ def run_profile(args, cfg):
         rep["ctx"] = args.ctx
     if args.kinds:
         rep["kernel_us"] = {k: round(v * 1e3, 2) for k, v in e.time_kernels(args.iters).items()}
+    if args.rows > 0:  # the kinds at a prefill block of --rows rows (after the --ctx prompt)
+        if args.ctx > 0 and args.kinds:  # the decode timing reset the slots
+            e.prefill(0, prompt_ids(args.ctx, cfg.vocab_size, seed=2))
+        rep["prefill_rows"] = args.rows
+        rep["prefill_kernel_us"] = {k: round(v * 1e3, 2) for k, v in e.time_kernels(args.iters, rows=args.rows).items()}
     if args.decode_steps > 0 or args.trace:
         p = prompt_ids(16, cfg.vocab_size, seed=1)
         seeds = [e.prefill(b, p)[0] for b in range(args.batch)]
@@ -728,6 +735,7 @@ def main():
     pg.add_argument("--iters", type=int, default=4, help="launches per kernel kind")
     pg.add_argument("--capacity", type=int, default=256)
     pg.add_argument("--ctx", type=int, default=0, help="prompt tokens prefilled in every slot before the kernel timing")
+    pg.add_argument("--rows", type=int, default=0, help="also time each kernel kind at a prefill block of this many rows")
     pg.add_argument("--decode-steps", type=int, default=0)
     pg.add_argument("--trace", action="store_true")
     pg.add_argument("--no-kinds", dest="kinds", action="store_false")

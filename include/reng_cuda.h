@@ -266,6 +266,11 @@ int reng_model_last_times(const reng_model *m, reng_step_times *t);
  */
 #define RENG_KERNEL_KINDS 6
 int reng_model_time_kernels(reng_model *m, int iters, float *ms_out);
+/* The same kinds at a prefill block of `rows` rows of slot 0 (rows > 0;
+ * 0 is reng_model_time_kernels): the block starts at slot 0's position,
+ * attention runs the prefill form and the LM head every row.  rows is at
+ * most the engine's prefill block.  Every slot is reset afterwards. */
+int reng_model_time_kernels_rows(reng_model *m, int rows, int iters, float *ms_out);
 
 /* Phase timeline of one decode step of the persistent step kernel (the
  * models it runs: one CUDA-graph node per step).  Runs one step from the
@@ -288,7 +293,8 @@ int reng_model_trace_step(reng_model *m, uint64_t *out, int max_phases, int *n_p
  * is packed into the engine's swizzled 16 x 64 blocks, x (bf16 [M][K]) is
  * read by the tensor-memory-accelerator copy, the accumulator lives in
  * tensor memory.  Host buffers (mem RENG_MEM_HOST) or device buffers
- * (RENG_MEM_DEVICE).  1 <= M <= 256, K % 8 == 0.  splits = K splits (0:
+ * (RENG_MEM_DEVICE).  1 <= M <= 1024 (N-tiles of 256 rows beyond 256),
+ * K % 8 == 0.  splits = K splits (0:
  * the model's choice; > 0: that many CTAs of one cluster adding their
  * partials over shared memory; < 0: -splits plain CTAs adding theirs
  * through global scratch, the last to arrive in split order).  iters > 0:

@@ -20,11 +20,12 @@
 // per chunk whatever the stage count, 40 GB/s with one copy per stage,
 // B200).
 //
-// Roles (192 threads): warp 0 lane 0 issues the copies, warp 1 owns the TMEM
-// accumulator (128 lanes x N f32 columns) and lane 0 issues the MMAs and
-// commits each stage back to the producer; warps 2-5 read the accumulator
-// with tcgen05.ld (warp w reads TMEM lanes 32*(w%4) .. +32) and apply the
-// same epilogues as the GEMV kernels.  A weight matrix with few super-tiles
+// Roles: warp 0 lane 0 issues the copies, warp 1 owns the TMEM accumulator
+// (128 lanes x N f32 columns) and lane 0 issues the MMAs and commits each
+// stage back to the producer; the epilogue warps 2 .. 2 + 4 W read the
+// accumulator with tcgen05.ld (warp w reads TMEM lanes 32*(w%4) .. +32, the
+// W warps of a lane quarter every W-th 16-column block) and apply
+// the same epilogues as the GEMV kernels.  A weight matrix with few super-tiles
 // is split along K over up to 8 CTAs launched as one thread-block cluster:
 // each keeps its partial tile in its own shared memory, and after a cluster
 // barrier CTA r adds column blocks r, r + ks, ... of every split over
@@ -44,14 +45,28 @@ namespace reng {
 
 namespace {
 
-constexpr int kGemmThreads = 192;
+// Epilogue warps per TMEM lane quarter (W, chosen at launch): warp w reads
+// lanes 32*(w%4) .. +32, and the W warps of a quarter take every W-th
+// 16-column block.  The epilogue of a wide tile is latency-bound (one
+// dependent chain per column on each warp), so more warps per quarter drain
+// it faster: measured on B200 (Llama-8B widths, 1024-row prefill block)
+// gate/up 429 -> 294 us from 1 to 4 warps.  Up to 4 (3 for the q/k/v
+// epilogue, whose RoPE operands would spill at the 113 registers of 576
+// threads) when N > 64; 1 at N <= 64, where two CTAs share an SM (b64 decode:
+// 10.7k tok/s with 1, 9.6k with 4, the SM's registers then holding one).
+template <int EPI>
+__host__ __device__ constexpr int epi_warps_max() { return EPI == EPI_QKV ? 3 : 4; }
+template <int EPI>
+__host__ __device__ constexpr int gemm_threads_max() { return 64 + 128 * epi_warps_max<EPI>(); }
 constexpr int kGemmMaxStages = 8;  // pipeline stages (runtime: GemmArgs::stages)
 constexpr int kGemmStageBudget = 200 * 1024;                  // stage bytes of a one-per-SM launch
 constexpr int kGemmMaxDynSmem = kGemmStageBudget + 2048;      // + the 1024-byte alignment slack
 constexpr int kStageA = 8 * kBlockBytesBf16;  // 128 rows x 64 k
 using namespace tc;
 
-__device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_epilogue() {
+    asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 64) : "memory");
+}
 
 __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) {
@@ -201,9 +216,10 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmap_x,
                                                              const __grid_constant__ CUtensorMap tmap_w, GemmArgs g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const int kEpiW = (int)(blockDim.x - 64) >> 7;  // epilogue warps per lane quarter
     __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], accum;
     __shared__ uint32_t tmem_base_s;
     __shared__ int s_flag;
@@ -355,10 +371,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             else bar_arrive(bar_acc);
         }
     } else {
-        // ---- epilogue warps 2..5 ----
+        // ---- epilogue warps 2 .. 2 + 4 kEpiW ----
         pdl_wait();
         pdl_launch();
-        const int q4 = warp & 3, warp_e = warp - 2;
+        const int q4 = warp & 3, warp_e = (warp - 2) & 3, eh = (warp - 2) >> 2;
         const int lr = 32 * q4 + lane;       // TMEM lane = row of the super-tile
         const int p = 128 * S + lr;          // packed row of the matrix
         if (!bar_wait(bar_acc, 0)) {
@@ -371,7 +387,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
         // accumulator was never written
         const bool zero = nk == 0 || failed;
         if (g.ks == 1) {
-            for (int cb = 0; cb < N / 16; cb++) {
+            for (int cb = eh; cb < N / 16; cb += kEpiW) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
                 if (zero)
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             // super-tile to arrive adds all of them in split order
             // (deterministic) and runs the epilogue
             float* mine = g.gpart + (((size_t)t_sn * g.ks + ksi) * 128 + lr) * N;
-            for (int cb = 0; cb < N / 16; cb++) {
+            for (int cb = eh; cb < N / 16; cb += kEpiW) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
 #pragma unroll
@@ -400,7 +416,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             named_sync_epilogue();
             if (s_flag) {
                 __threadfence();
-                for (int cb = 0; cb < N / 16; cb++) {
+                for (int cb = eh; cb < N / 16; cb += kEpiW) {
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; j++) v[j] = 0.f;
@@ -424,7 +440,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             // split K: this split's partial into the (finished) stage buffers,
             // row lr at lr * (N + 4) floats (conflict-free 16-byte stores)
             float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
-            for (int cb = 0; cb < N / 16; cb++) {
+            for (int cb = eh; cb < N / 16; cb += kEpiW) {
                 float v[16];
                 tmem_ld16(trow + cb * 16, v);
                 float4* dst = reinterpret_cast<float4*>(part + (size_t)lr * (N + 4) + cb * 16);
@@ -435,11 +451,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             }
         }
         if (EPI == EPI_LOGITS) {
-            // CTA partials of every row: best over the 4 epilogue warps
+            // CTA partials of every row: best over the 4 lane quarters
             named_sync_epilogue();
             const GemvArgs& a = g.e;
             // this CTA's best per row of its N-tile into the rows' running maxima
-            for (int ml = threadIdx.x - 64; ml < min(N, a.M - n0); ml += 128) {
+            for (int ml = threadIdx.x - 64; ml < min(N, a.M - n0); ml += 128 * kEpiW) {
                 float bv = -INFINITY;
                 int bi = 0x7fffffff;
                 for (int w = 0; w < 4; w++) am_take2(bv, bi, am_v[w * kRowsCap + ml], am_i[w * kRowsCap + ml]);
@@ -451,7 +467,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             named_sync_epilogue();
             if (s_flag) {
                 __threadfence();
-                for (int m = threadIdx.x - 64; m < a.M; m += 128) {
+                for (int m = threadIdx.x - 64; m < a.M; m += 128 * kEpiW) {
                     unsigned long long k = atomicExch(a.am_key + m, 0ull);
                     if (a.hx) k = head_exchange(a.hx, m, k, a.err);  // vocabulary shards of the ranks
                     am_i[m] = am_unpack(k);
@@ -484,9 +500,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
         cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();
         if (warp >= 2) {
-            const int lr = 32 * (warp & 3) + lane, p = 128 * S + lr, warp_e = warp - 2;
+            const int lr = 32 * (warp & 3) + lane, p = 128 * S + lr, warp_e = (warp - 2) & 3, eh = (warp - 2) >> 2;
             float* part = reinterpret_cast<float*>(smem_raw + (smem0 - (uint32_t)__cvta_generic_to_shared(smem_raw)));
-            for (int cb = ksi; cb < N / 16; cb += g.ks) {
+            for (int cb = ksi + eh * g.ks; cb < N / 16; cb += g.ks * kEpiW) {
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; j++) v[j] = 0.f;
@@ -651,7 +667,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const CUtensorMap& wmap, 
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(g.super_tiles * g.ntiles * g.ks);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(64 + 128 * (g.N > 64 ? epi_warps_max<EPI>() : 1));
     cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C);
     cfg.stream = st;
     int na = 0;
@@ -822,7 +838,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     using namespace reng;
     RENG_CHECK_ARG(w && x && y, "reng_gemm_bf16: NULL buffer");
     RENG_CHECK_ARG(rows >= 1 && K >= 8 && K % 8 == 0, "reng_gemm_bf16: rows >= 1 and K a positive multiple of 8");
-    RENG_CHECK_ARG(M >= 1 && M <= kRowsCap, "reng_gemm_bf16: M must be in [1, 256]");
+    RENG_CHECK_ARG(M >= 1 && M <= kGemmRowsMax, "reng_gemm_bf16: M must be in [1, 1024]");
     RENG_CHECK_ARG(splits >= -kGemmMaxSplits && splits <= kGemmMaxSplits && iters >= 0 && (iters == 0 || ms_out),
                    "reng_gemm_bf16: bad splits / iters");
     RENG_CHECK_ARG(mem == RENG_MEM_HOST || mem == RENG_MEM_DEVICE, "reng_gemm_bf16: bad mem");
@@ -832,7 +848,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     GEMM_CU(cudaGetDevice(&dev));
     GEMM_CU(gemm_prepare());
     const int tiles = (rows + kTileRows - 1) / kTileRows, kc = (K + kChunkK - 1) / kChunkK;
-    const int N = (M + 15) / 16 * 16;
+    const int N = M > kRowsCap ? kRowsCap : (M + 15) / 16 * 16;  // N-tiles of kRowsCap beyond
     DevFree f;
     uint16_t *wd = nullptr, *xd = nullptr;
     uint8_t* packed = nullptr;
@@ -840,13 +856,13 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     float* yd = nullptr;
     int* err = nullptr;
     GEMM_CU(f.alloc(&wd, (size_t)rows * K * 2));
-    GEMM_CU(f.alloc(&xd, (size_t)kRowsCap * K * 2));
+    GEMM_CU(f.alloc(&xd, (size_t)kGemmRowsMax * K * 2));
     GEMM_CU(f.alloc(&packed, (size_t)tiles * kc * kBlockBytesBf16));
     GEMM_CU(f.alloc(&rowmap, (size_t)tiles * kTileRows * 4));
     GEMM_CU(f.alloc(&yd, (size_t)M * rows * 4));
     GEMM_CU(f.alloc(&err, 4));
     GEMM_CU(cudaMemcpy(wd, w, (size_t)rows * K * 2, h2d));
-    GEMM_CU(cudaMemset(xd, 0, (size_t)kRowsCap * K * 2));
+    GEMM_CU(cudaMemset(xd, 0, (size_t)kGemmRowsMax * K * 2));
     GEMM_CU(cudaMemcpy(xd, x, (size_t)M * K * 2, h2d));
     GEMM_CU(cudaMemset(err, 0, 4));
     std::vector<int> map((size_t)tiles * kTileRows, -1);
@@ -875,9 +891,9 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
     g.kc = kc;
     g.super_tiles = (tiles + 7) / 8;
     g.N = N;
-    g.ntiles = 1;
+    g.ntiles = (M + N - 1) / N;
     bool gsplit = false;
-    gemm_plan(g.super_tiles, kc, N, EPI_F32, num_sms(dev), true, &g.ks, &g.stages, &gsplit, &g.C);
+    gemm_plan(g.super_tiles * g.ntiles, kc, N, EPI_F32, num_sms(dev), true, &g.ks, &g.stages, &gsplit, &g.C);
     if (splits != 0) {  // > 0: a cluster of that many splits; < 0: plain CTAs
         int s = splits > 0 ? splits : -splits;
         s = s > kc ? kc : s;
@@ -888,13 +904,14 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
         g.stages = gemm_pick_stages(N, (g.ks > 1 && !gsplit) || N > 64, EPI_F32, g.C);
     }
     if (gsplit) {
-        GEMM_CU(f.alloc(&g.gpart, (size_t)g.super_tiles * g.ks * 128 * N * 4));
-        GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * 4));
-        GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * 4));
+        GEMM_CU(f.alloc(&g.gpart, (size_t)g.super_tiles * g.ntiles * g.ks * 128 * N * 4));
+        GEMM_CU(f.alloc(&g.gcnt, (size_t)g.super_tiles * g.ntiles * 4));
+        GEMM_CU(cudaMemset(g.gcnt, 0, (size_t)g.super_tiles * g.ntiles * 4));
     }
     CUtensorMap tmap, wmap;
     g.b3d = K % kChunkK == 0;
-    int rc = g.b3d ? gemm_tensor_map3(xd, kRowsCap, K, N, g.C, &tmap) : gemm_tensor_map(xd, kRowsCap, K, N, &tmap);
+    int rc = g.b3d ? gemm_tensor_map3(xd, kGemmRowsMax, K, N, g.C, &tmap)
+                   : gemm_tensor_map(xd, kGemmRowsMax, K, N, &tmap);
     if (rc) return rc;
     rc = gemm_weight_map(packed, tiles, kc, g.C, &wmap);
     if (rc) return rc;

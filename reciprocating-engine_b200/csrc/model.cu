@@ -1253,17 +1253,24 @@ extern "C" int reng_model_last_times(const reng_model* m, reng_step_times* t) {
     return RENG_OK;
 }
 
-extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) {
+extern "C" int reng_model_time_kernels_rows(reng_model* m, int rows, int iters, float* ms_out) {
     TRY(check_model(m));
     RENG_CHECK_ARG(ms_out != nullptr && iters >= 1, "reng_model_time_kernels: bad arguments");
+    RENG_CHECK_ARG(rows >= 0 && rows <= prefill_rows(m), "reng_model_time_kernels_rows: rows must be in [0, " +
+                                                            std::to_string(prefill_rows(m)) + "]");
+    RENG_CHECK_ARG((int64_t)m->host_pos[0] + rows <= m->cap,
+                   "reng_model_time_kernels_rows: slot 0 has no room for the block");
     CU(cudaSetDevice(m->dev));
     CU(cudaStreamSynchronize(m->st));
-    const int M = m->B;
+    const int mode = rows > 0 ? 1 : 0;
+    const int M = rows > 0 ? rows : m->B;
     EventSet evs;
     CU(evs.create(2));
     cudaEvent_t e0 = evs.e[0], e1 = evs.e[1];
-    // rows as the decode step sees them
-    TRY(k_embed_launch(m, 0, M, 0, m->st));
+    // rows as the decode step sees them, or a prefill block of slot 0 at
+    // its current position
+    if (rows > 0) TRY(sync_pos(m));
+    TRY(k_embed_launch(m, mode, M, 0, m->st));
     for (int kind = 0; kind < RENG_KERNEL_KINDS; kind++) {
         // one untimed pass, then `iters` launches cycling over the layers
         for (int pass = 0; pass < 2; pass++) {
@@ -1273,7 +1280,7 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
                 const int l = i % m->L;
                 switch (kind) {
                     case 0: TRY(k_qkv_launch(m, l, M, m->st)); break;
-                    case 1: TRY(k_attn_launch(m, l, M, 0, m->st)); break;
+                    case 1: TRY(k_attn_launch(m, l, M, mode, m->st)); break;
                     case 2: TRY(k_proj_launch(m, l, M, 0, m->st)); break;
                     case 3: TRY(k_gateup_launch(m, l, M, m->st)); break;
                     case 4: TRY(k_proj_launch(m, l, M, 1, m->st)); break;
@@ -1289,9 +1296,14 @@ extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) 
     }
     TRY(check_device_error(m));
     // the QKV launches rewrote the cache row at each slot's last position
-    // with other activations: the cached prefix is no longer valid
+    // (or the block's rows) with other activations: the cached prefix is no
+    // longer valid
     for (int b = 0; b < m->B; b++) m->host_pos[b] = 0;
     return sync_pos(m);
+}
+
+extern "C" int reng_model_time_kernels(reng_model* m, int iters, float* ms_out) {
+    return reng_model_time_kernels_rows(m, 0, iters, ms_out);
 }
 
 extern "C" int reng_model_time_exchange(reng_model* m, int iters, float* ms_out) {

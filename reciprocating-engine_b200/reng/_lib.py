@@ -95,6 +95,7 @@ SIGNATURES = {
     "reng_model_device_bytes": ([_P, _P], C.c_int),
     "reng_model_last_times": ([_P, _P], C.c_int),
     "reng_model_time_kernels": ([_P, C.c_int, _P], C.c_int),
+    "reng_model_time_kernels_rows": ([_P, C.c_int, C.c_int, _P], C.c_int),
     "reng_model_time_exchange": ([_P, C.c_int, _P], C.c_int),
     "reng_tp_unique_id": ([_P], C.c_int),
     "reng_model_trace_step": ([_P, _P, C.c_int, _P], C.c_int),

@@ -3,8 +3,8 @@ patterns (the projection kernel of steps with more than 8 rows).
 
     y, ms = gemm_bf16(w_bits, x_bits, splits=0, iters=0)
 
-w_bits: uint16 [rows][K] bf16 bits, x_bits: uint16 [M][K] (1 <= M <= 256,
-K % 8 == 0).  iters > 0 also times the kernel alone (mean ms per launch).
+w_bits: uint16 [rows][K] bf16 bits, x_bits: uint16 [M][K] (1 <= M <= 1024,
+N-tiles of 256 rows beyond 256; K % 8 == 0).  iters > 0 also times the kernel alone (mean ms per launch).
 """
 import ctypes as C
 

@@ -268,11 +268,12 @@ class Engine:
         _lib.call("reng_model_device_bytes", self.h, C.byref(b))
         return b.value
 
-    def time_kernels(self, iters=64):
+    def time_kernels(self, iters=64, rows=0):
         """Mean ms per launch of each kernel kind (qkv, attn, o, gate_up,
-        down, lm_head); resets every slot afterwards."""
+        down, lm_head) at the decode rows (rows=0) or at a prefill block of
+        `rows` rows of slot 0; resets every slot afterwards."""
         out = np.zeros(6, np.float32)
-        _lib.call("reng_model_time_kernels", self.h, iters, out.ctypes.data)
+        _lib.call("reng_model_time_kernels_rows", self.h, rows, iters, out.ctypes.data)
         return dict(zip(("qkv", "attn", "o_proj", "gate_up", "down", "lm_head"),
                         (float(x) for x in out)))
 

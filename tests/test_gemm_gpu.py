@@ -1,6 +1,6 @@
 """The tcgen05 GEMM (steps of more than 8 rows) against float64 sums of the
 same bf16 values, and the model paths that run on it: decode at batch 16 /
-64 and prefill blocks of up to 256 rows against the f32 host forward.
+64 and prefill blocks of up to 1024 rows against the f32 host forward.
 
 GEMM bar: every output within 1e-4 x sum_k |x_k w_k| of the exact sum (the
 products of two bf16 are exact in f32; only the f32 accumulation order
@@ -41,6 +41,9 @@ def bits_to_f64(b):
     (8192, 520, 24, 0),      # 64 super-tiles, ragged K: an odd chunk count (units of 2 chunks and of 1)
     (2048, 2048, 256, 0),    # N = 256 with split K
     (256, 1000, 48, 3),      # ragged K with a cluster: per-chunk activation copies
+    (1000, 576, 1024, 0),    # four N-tiles of 256 rows, ragged super-tiles
+    (384, 1000, 700, 0),     # three N-tiles, the last of 188 rows; ragged K
+    (256, 2048, 300, 2),     # two N-tiles, each a cluster of 2 K splits
 ])
 def test_gemm_matches_exact_sums(reng_lib, rows, K, M, splits):
     from reng.gemm import gemm_bf16
@@ -60,7 +63,7 @@ def test_gemm_rejects_bad_shapes(reng_lib):
     from reng.gemm import gemm_bf16
     w = np.zeros((16, 64), np.uint16)
     with pytest.raises(RengError):
-        gemm_bf16(w, np.zeros((257, 64), np.uint16))        # more than 256 rows
+        gemm_bf16(w, np.zeros((1025, 64), np.uint16))       # more than 1024 rows
     with pytest.raises(RengError):
         gemm_bf16(np.zeros((16, 60), np.uint16), np.zeros((4, 60), np.uint16))  # K % 8 != 0
 
