@@ -10,18 +10,23 @@
 //               Q (K-major) staged by the softmax warps, K (K-major) by TMA
 //               straight from the cache ([keys][head_dim] rows, 128-byte
 //               swizzle), S in TMEM columns 0..127;
-//   softmax     the 128 threads of warps 2-5 own one TMEM lane (one query
-//               row) each: tcgen05.ld of the row's 128 scores, causal mask
-//               (key <= the row's position), running max and sum in f32,
-//               P = exp(s - max) as bf16 into shared memory in the K-major
-//               A-operand layout, O rescaled in TMEM (tcgen05.ld / st) when
-//               the max moved;
+//   softmax     two threads own each TMEM lane (query row), one per half
+//               of the 128 keys (warps w and w + 4 read the same lane
+//               quarter): tcgen05.ld of the half's 64 scores, causal mask
+//               (key <= the row's position), the row max swapped between
+//               the halves through shared memory, running max and sum in
+//               f32, P = exp(s - max) as bf16 into shared memory in the
+//               K-major A-operand layout (each half one 64-key block), O
+//               rescaled in TMEM (tcgen05.ld / st, each half its columns)
+//               when the max moved;
 //   O += P V    M 128, N = head_dim, K 128 keys; V read MN-major from the
 //               same TMA layout (64-dim blocks 16 KB apart, 8-key groups
 //               1 KB apart), O in TMEM columns 128..128+head_dim.
-// Roles (192 threads): warp 0 lane 0 issues the K/V copies (two stages),
-// warp 1 owns TMEM (256 columns) and lane 0 issues the MMAs, warps 2-5 stage
-// Q, run the softmax and write O / l as bf16.  Every mbarrier wait is
+// Roles (320 threads): warp 0 lane 0 issues the K/V copies (two stages),
+// warp 1 owns TMEM (256 columns) and lane 0 issues the MMAs, warps 2-9 stage
+// Q, run the softmax and write O / l as bf16.  The softmax is the kernel's
+// critical path (one exponential per score on the CUDA cores): two threads
+// per row halve it, measured on B200 against one thread per row.  Every mbarrier wait is
 // bounded; a wait that runs out records RENG_E_TIMEOUT and the kernel ends.
 // The attention scale is already in q (folded into the bf16 wq), as the
 // per-row kernel assumes (crates/reng-synapse/src/model.rs:151-157).
@@ -35,7 +40,7 @@ namespace reng {
 using namespace tc;
 
 namespace {
-constexpr int kFaThreads = 192;
+constexpr int kFaThreads = 320;
 constexpr int kFaRows = 128;     // query rows of a tile (the MMA's M)
 constexpr int kFaKeys = 128;     // keys of a K/V tile
 constexpr int kFaBlock = 16384;  // one 128-row x 128-byte swizzled operand block
@@ -59,6 +64,19 @@ __device__ __forceinline__ uint32_t swz(uint32_t block, int r, int ch) {
 __device__ __forceinline__ bool warp_wait(uint32_t b, uint32_t parity) {
     return __all_sync(0xffffffffu, bar_wait(b, parity));
 }
+// Named barrier 1 over the 256 softmax threads that also ANDs a flag across
+// them: every thread leaves with the same answer, so a bounded wait that gave
+// up in one warp ends the tile loop in all of them at the same barrier.
+__device__ __forceinline__ bool softmax_all(bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((int)v)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void st_shared16(uint32_t addr, uint4 v) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
@@ -70,6 +88,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_attn_prefill(const __grid_con
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) unsigned long long kv_full[2], kv_empty[2], q_full, s_full, s_free, p_full, o_done, drain;
     __shared__ uint32_t tmem_base_s;
+    __shared__ float xmax[2][2][kFaRows];  // [tile parity][half][row] the halves' row maxima
+    __shared__ float xsum[2][kFaRows];     // [half][row] the halves' running sums at the end
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NC = f.hd >> 6;  // 64-wide head-dim blocks (1 or 2)
@@ -84,10 +104,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_attn_prefill(const __grid_con
             bar_init(bar(&kv_full[s]), 1);
             bar_init(bar(&kv_empty[s]), 1);
         }
-        bar_init(bar(&q_full), 4);
+        bar_init(bar(&q_full), 8);
         bar_init(bar(&s_full), 1);
-        bar_init(bar(&s_free), 4);
-        bar_init(bar(&p_full), 4);
+        bar_init(bar(&s_free), 8);
+        bar_init(bar(&p_full), 8);
         bar_init(bar(&o_done), 1);
         bar_init(bar(&drain), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -167,19 +187,22 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_attn_prefill(const __grid_con
             if (!bar_wait(bar(&drain), 0)) atomicExch(f.err, RENG_E_TIMEOUT);
         }
     } else {
-        // ---- warps 2..5: TMEM lane r = query row r of the tile ----
-        const int r = 32 * (warp & 3) + lane;
+        // ---- warps 2..9: TMEM lane r = query row r of the tile, keys
+        // 64 h .. 64 h + 63 of each key tile and O columns h hd/2 .. ----
+        const int r = 32 * (warp & 3) + lane, h = (warp - 2) >> 2;
         const int hl = r / f.P, t = r % f.P, mrow = t0 + t;
         const bool active = hl < f.hpg && mrow < f.M;
         const int q_dim = f.n_kv * f.hpg * f.hd;
         const int head = grp * f.hpg + hl;
         const int pos = pos0 + mrow;
+        const int ohalf = f.hd >> 1;  // O columns per half
         const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
         {
+            // Q row r: the half stages every other 16-byte chunk
             const uint4* qr = reinterpret_cast<const uint4*>(f.q + (size_t)mrow * q_dim + (size_t)head * f.hd);
             for (int c = 0; c < NC; c++)
 #pragma unroll
-                for (int ch = 0; ch < 8; ch++)
+                for (int ch = h; ch < 8; ch += 2)
                     st_shared16(swz(sQ + (uint32_t)c * kFaBlock, r, ch),
                                 active ? __ldcg(qr + c * 8 + ch) : make_uint4(0u, 0u, 0u, 0u));
         }
@@ -189,64 +212,71 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_attn_prefill(const __grid_con
         float mrun = -INFINITY, lrun = 0.f;
         bool ok = true;
         for (int j = 0; j < ntiles; j++) {
-            if (!warp_wait(bar(&s_full), (uint32_t)(j & 1))) {
+            const bool okj = ok && warp_wait(bar(&s_full), (uint32_t)(j & 1));
+            float sc[kFaKeys / 2];
+            // causal: key j * 128 + 64 h + c is visible to this row iff it
+            // is at or before the row's position
+            const int lim = active ? pos - j * kFaKeys - h * (kFaKeys / 2) : -1;
+            float mx = -INFINITY;
+            if (okj) {
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int g = 0; g < kFaKeys / 32; g++) {
+                    float v[16];
+                    tmem_ld16(tS + lanes + h * (kFaKeys / 2) + g * 16, v);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) sc[g * 16 + e] = v[e];
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(bar(&s_free));
+#pragma unroll
+                for (int c = 0; c < kFaKeys / 2; c++)
+                    if (c <= lim) mx = fmaxf(mx, sc[c]);
+            }
+            // the row max over both halves (slots alternate by tile parity:
+            // a slot is rewritten two tiles later, after the partner has
+            // passed the next exchange, so after it read this one)
+            xmax[j & 1][h][r] = mx;
+            if (!softmax_all(okj)) {
                 ok = false;
                 break;
             }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            float sc[kFaKeys];
-#pragma unroll
-            for (int g = 0; g < kFaKeys / 16; g++) {
-                float v[16];
-                tmem_ld16(tS + lanes + g * 16, v);
-#pragma unroll
-                for (int e = 0; e < 16; e++) sc[g * 16 + e] = v[e];
-            }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) bar_arrive(bar(&s_free));
-            // causal: key j * 128 + c is visible to this row iff it is at or
-            // before the row's position
-            const int lim = active ? pos - j * kFaKeys : -1;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kFaKeys; c++)
-                if (c <= lim) mx = fmaxf(mx, sc[c]);
+            mx = fmaxf(mx, xmax[j & 1][h ^ 1][r]);
             const float mnew = fmaxf(mrun, mx);
-            const float alpha = mrun == -INFINITY ? 0.f : expf(mrun - mnew);
+            const float alpha = mrun == -INFINITY ? 0.f : __expf(mrun - mnew);
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < kFaKeys; c++) {
-                const float p = c <= lim ? expf(sc[c] - mnew) : 0.f;
+            for (int c = 0; c < kFaKeys / 2; c++) {
+                const float p = c <= lim ? __expf(sc[c] - mnew) : 0.f;
                 sc[c] = p;
                 sum += p;
             }
             lrun = lrun * alpha + sum;
             mrun = mnew;
-            // P and O are free once the previous tile's P V has finished
+            // P and O are free once the previous tile's P V has finished (a
+            // wait that gives up ends the loop at the next exchange)
             if (j >= 1) {
                 if (!warp_wait(bar(&o_done), (uint32_t)((j - 1) & 1))) {
                     ok = false;
-                    break;
+                    continue;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
 #pragma unroll
-            for (int h2 = 0; h2 < 2; h2++)
-#pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    const float* p = sc + h2 * 64 + ch * 8;
-                    st_shared16(swz(sP + (uint32_t)h2 * kFaBlock, r, ch),
-                                make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
-                                           pack_bf16x2(p[6], p[7])));
-                }
+            for (int ch = 0; ch < 8; ch++) {
+                const float* p = sc + ch * 8;
+                st_shared16(swz(sP + (uint32_t)h * kFaBlock, r, ch),
+                            make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
+                                       pack_bf16x2(p[6], p[7])));
+            }
             if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                for (int g = 0; g < f.hd / 16; g++) {
+                for (int g = 0; g < ohalf / 16; g++) {
                     float v[16];
-                    tmem_ld16(tO + lanes + g * 16, v);
+                    tmem_ld16(tO + lanes + h * ohalf + g * 16, v);
 #pragma unroll
                     for (int e = 0; e < 16; e++) v[e] *= alpha;
-                    tmem_st16(tO + lanes + g * 16, v);
+                    tmem_st16(tO + lanes + h * ohalf + g * 16, v);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -254,13 +284,18 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_attn_prefill(const __grid_con
             __syncwarp();
             if (lane == 0) bar_arrive(bar(&p_full));
         }
+        // the row's sum over both halves (every softmax thread takes this
+        // barrier, also after a wait gave up, so none is left waiting)
+        xsum[h][r] = lrun;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        lrun += xsum[h ^ 1][r];
         if (ok && warp_wait(bar(&o_done), (uint32_t)((ntiles - 1) & 1))) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
-            uint4* dst = reinterpret_cast<uint4*>(f.out + (size_t)mrow * q_dim + (size_t)head * f.hd);
-            for (int g = 0; g < f.hd / 16; g++) {
+            uint4* dst = reinterpret_cast<uint4*>(f.out + (size_t)mrow * q_dim + (size_t)head * f.hd + h * ohalf);
+            for (int g = 0; g < ohalf / 16; g++) {
                 float v[16];
-                tmem_ld16(tO + lanes + g * 16, v);
+                tmem_ld16(tO + lanes + h * ohalf + g * 16, v);
                 if (active) {
                     dst[2 * g] = make_uint4(pack_bf16x2(v[0] * inv, v[1] * inv), pack_bf16x2(v[2] * inv, v[3] * inv),
                                             pack_bf16x2(v[4] * inv, v[5] * inv), pack_bf16x2(v[6] * inv, v[7] * inv));
