@@ -44,6 +44,8 @@ def bits_to_f64(b):
     (1000, 576, 1024, 0),    # four N-tiles of 256 rows, ragged super-tiles
     (384, 1000, 700, 0),     # three N-tiles, the last of 188 rows; ragged K
     (256, 2048, 300, 2),     # two N-tiles, each a cluster of 2 K splits
+    (6144, 512, 1024, 0),    # 48 super-tiles x 4 N-tiles: two waves of CTAs
+    (6144, 520, 900, 0),     # the same with a ragged last N-tile and ragged K
 ])
 def test_gemm_matches_exact_sums(reng_lib, rows, K, M, splits):
     from reng.gemm import gemm_bf16
