@@ -335,9 +335,9 @@ int launch_attn_prefill(const AttnArgs& a, long long cache_rows, int* err, cudaS
     });
     if (prep != cudaSuccess) return fail(RENG_E_CUDA, std::string("attention prefill: ") + cudaGetErrorString(prep));
     CUtensorMap km, vm;
-    int rc = attn_cache_map(a.kcache, a.hd, cache_rows, &km);
+    int rc = attn_cache_map(a.kcache, a.hd, cache_rows, kFaKeys, &km);
     if (rc) return rc;
-    rc = attn_cache_map(a.vcache, a.hd, cache_rows, &vm);
+    rc = attn_cache_map(a.vcache, a.hd, cache_rows, kFaKeys, &vm);
     if (rc) return rc;
     FaArgs f{};
     f.q = a.q;

@@ -568,25 +568,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     cluster.sync();  // keep this CTA's shared memory alive until its peers have read it
 }
 
-cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t st) {
-    if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.hpg * (a.hd / 4) > kAttnThreads)
-        return cudaErrorInvalidValue;
-    // key slices per (row, KV group): 8 (a cluster) when the rows x groups
-    // are few, fewer as they grow
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const long long units = (long long)a.M * a.n_kv;
+// Key slices per (row, KV group): 8 (a cluster) when the rows x groups are
+// few, fewer as they grow.  Measured on B200 (Llama-8B, 8 KV groups): b1 (8
+// units) 8 slices; b8 (64 units) 4 beat 8 and 2 (7.9 against 10.0 and 9.2
+// us); b16 4 beat 8 (10.6 against 19.2 us); b64 (512 units) 1 beat 2 and 4
+// (24.9 against 27.9 and 39.5 us).
+int attn_slices(long long units) {
     static const int fixed_ns = [] {  // RENG_ATTN_SLICES: a tuning knob fixing the slices (1, 2, 4 or 8)
         const char* v = getenv("RENG_ATTN_SLICES");
         const int x = v ? atoi(v) : 0;
         return x == 1 || x == 2 || x == 4 || x == 8 ? x : 0;
     }();
-    // Slices per (row, KV group), measured on B200 (Llama-8B, 8 KV groups):
-    // b1 (8 units) 8 slices; b8 (64 units) 4 beat 8 and 2 (7.9 against 10.0
-    // and 9.2 us); b16 4 beat 8 (10.6 against 19.2 us); b64 (512 units) 1
-    // beat 2 and 4 (24.9 against 27.9 and 39.5 us).
-    int ns = units >= 2LL * num_sms(dev) ? 1 : units >= 64 ? 4 : kAttnCluster;
-    if (fixed_ns) ns = fixed_ns;
+    if (fixed_ns) return fixed_ns;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return units >= 2LL * num_sms(dev) ? 1 : units >= 64 ? 4 : kAttnCluster;
+}
+
+cudaError_t launch_attn(const AttnArgs& a, int /*chunk*/, bool pdl, cudaStream_t st) {
+    if (a.hpg > kAttnMaxHpg || a.hd > kAttnMaxHd || a.hd % 8 || a.hpg * (a.hd / 4) > kAttnThreads)
+        return cudaErrorInvalidValue;
+    const int ns = attn_slices((long long)a.M * a.n_kv);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(ns, a.n_kv, a.M);

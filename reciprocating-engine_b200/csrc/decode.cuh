@@ -204,6 +204,9 @@ bool gemv8_fits(const GemvArgs& a);
 cudaError_t launch_gemv8(const GemvArgs& a, int epi, bool pdl, cudaStream_t st);
 cudaError_t gemv8_prepare();
 cudaError_t launch_attn(const AttnArgs& a, int chunk, bool pdl, cudaStream_t st);
+// Key slices per (row, KV group) of a decode attention launch over `units`
+// rows x KV groups (RENG_ATTN_SLICES fixes them).
+int attn_slices(long long units);
 cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_qk_norm(const QkNormArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_pack(const PackArgs& a, cudaStream_t st);

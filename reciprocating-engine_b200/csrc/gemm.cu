@@ -610,16 +610,17 @@ int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* o
 }
 
 // A layer's K or V cache [slot][kv head][cap][hd] bf16 as 2-D rows of hd
-// elements, read in {64, 128 rows} boxes with the 128-byte swizzle (the
-// tcgen05 operand layout of 128 keys x 64 head dims).  Rows past the last
-// slot read as zeros.
-int attn_cache_map(const uint16_t* cache, int hd, long long rows, CUtensorMap* out) {
+// elements, read in {64, box_rows} boxes with the 128-byte swizzle (with 128
+// rows, the tcgen05 operand layout of 128 keys x 64 head dims).  Rows past
+// the last slot read as zeros.
+int attn_cache_map(const uint16_t* cache, int hd, long long rows, int box_rows, CUtensorMap* out) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
-    if (hd % 64 || rows < 1 || ((uintptr_t)cache & 15)) return fail(RENG_E_INVAL, "attn_cache_map: bad shape");
+    if (hd % 64 || rows < 1 || box_rows < 8 || box_rows > 256 || box_rows % 8 || ((uintptr_t)cache & 15))
+        return fail(RENG_E_INVAL, "attn_cache_map: bad shape");
     cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
-    cuuint32_t box[2] = {64, 128};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)cache, dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

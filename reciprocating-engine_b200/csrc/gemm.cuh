@@ -40,13 +40,20 @@ int gemm_tensor_map3(const uint16_t* x, int rows, int K, int n, int c, CUtensorM
 // Packed bf16 weights [tiles16][kc][2 KB] as {64, 16, 8 tiles, c chunks} boxes.
 int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out);
 size_t gemm_smem_bytes(int n, int stages, int c);
-// A layer's K or V cache as {64, 128 rows} boxes of hd-wide rows (128-byte swizzle).
-int attn_cache_map(const uint16_t* cache, int hd, long long rows, CUtensorMap* out);
+// A layer's K or V cache as {64, box_rows} boxes of hd-wide rows (128-byte swizzle).
+int attn_cache_map(const uint16_t* cache, int hd, long long rows, int box_rows, CUtensorMap* out);
 // Prefill-block attention on the tensor cores (attn_prefill.cu): whether a
 // block fits it (head_dim 64 or 128, contiguous rows, a cache of cache_rows
 // hd-wide rows addressable by 32-bit tensor coordinates) and its launch.
 bool attn_prefill_fits(const AttnArgs& a, long long cache_rows);
 int launch_attn_prefill(const AttnArgs& a, long long cache_rows, int* err, cudaStream_t st);
+// Decode attention with the K/V tiles streamed through a TMA ring
+// (attn_decode.cu): whether a launch fits it (head_dim 64 or 128, at most 8
+// query heads per group, a cache addressable by 32-bit tensor coordinates)
+// and its launch (key slices per row and group as the per-row kernel's).
+bool attn_ring_fits(const AttnArgs& a, long long cache_rows);
+cudaError_t attn_ring_prepare();  // its shared-memory limit, once per device before capture
+int launch_attn_ring(const AttnArgs& a, long long cache_rows, int* err, bool pdl, cudaStream_t st);
 // 64-k chunks per pipeline stage.
 int gemm_chunks_per_stage(int n);
 // Pipeline stages of c chunks for MMA width n: as many as fit two CTAs per

@@ -484,15 +484,27 @@ AttnArgs attn_args(reng_model* m, int l, int M, int mode) {
 }
 
 // Attention of a step.  Prefill blocks of 16 or more rows run the
-// tensor-core flash attention (attn_prefill.cu); decode steps and short
-// blocks the per-row kernel.  RENG_FLASH_PREFILL=0 keeps every block on the
-// per-row kernel (an A/B knob).
+// tensor-core flash attention (attn_prefill.cu).  Decode steps and short
+// blocks run the TMA-ring kernel (attn_decode.cu) in engines of at least
+// kRingMinCap positions and the per-row kernel below that: measured on B200,
+// the ring took Qwen2.5-32B b1 attention at 4096 cached positions from 55.3
+// to 39.2 us per layer, but at short contexts its full 64-key tiles and its
+// shared memory (half the CTAs per SM) lost (Llama-8B b1 at ~200 positions
+// 6.1 -> 7.1 us, b64 22.8 -> 28.8 us).  The decode step is one captured
+// graph, so the choice is the engine's, by its capacity.
+// RENG_FLASH_PREFILL=0 keeps every block on the per-row kernel and
+// RENG_ATTN_RING=0 / 1 forces the decode choice (A/B knobs).
+constexpr int kRingMinCap = 1024;
 int k_attn_launch(reng_model* m, int l, int M, int mode, cudaStream_t st) {
     const AttnArgs a = attn_args(m, l, M, mode);
     const long long rows = (long long)m->B * m->nkv * m->cap;
     const char* env = getenv("RENG_FLASH_PREFILL");
+    const char* rv = getenv("RENG_ATTN_RING");
+    const bool ring = rv ? atoi(rv) != 0 : m->cap >= kRingMinCap;
     if (mode == 1 && M >= 16 && !(env && atoi(env) == 0) && attn_prefill_fits(a, rows)) {
         TRY(launch_attn_prefill(a, rows, m->err, st));
+    } else if (ring && attn_ring_fits(a, rows)) {
+        TRY(launch_attn_ring(a, rows, m->err, true, st));
     } else {
         CU(launch_attn(a, kAttnChunk, true, st));
     }
@@ -801,6 +813,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(gemv_prepare());
     CU(gemv8_prepare());
     CU(gemm_prepare());
+    CU(attn_ring_prepare());
     m->rank = d->tp_rank;
     m->world = d->tp_world;
     m->w8 = d->weights == RENG_WEIGHTS_FP8_E4M3 ? 1 : 0;

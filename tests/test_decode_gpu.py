@@ -117,6 +117,40 @@ def test_greedy_decode_matches_the_teacher_forced_oracle(lib):
     g.close()
 
 
+@pytest.mark.parametrize("ring", ["1", "0"])
+def test_long_context_decode_attention(lib, monkeypatch, ring):
+    """Decode attention over 1100+ cached positions: the TMA-ring kernel
+    (engines of 1024+ positions run it) and the per-row kernel, each against
+    the f32 forward teacher-forced on the engine's ids; 2 query heads per
+    group at head_dim 64, 8 key slices of ~140 keys (3 tiles each)."""
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    monkeypatch.setenv("RENG_ATTN_RING", ring)
+    cfg = small_cfg(bias=True)
+    w = random_weights(cfg, seed=13)
+    cap = 1200
+    prompt = prompt_ids(1100, cfg.vocab_size, seed=6)
+    e = Engine(cfg, w, batch=1, capacity=cap)
+    nxt, _, _ = e.prefill(0, prompt)
+    seq = list(prompt) + [nxt]
+    got = []
+    for _ in range(6):
+        lg, n = e.step_logits([seq[-1]])
+        got.append(lg[0])
+        seq.append(int(n[0]))
+    ids = [int(x) for x in e.decode([seq[-1]], 8)[:, 0]]
+    e.close()
+    sin, cos = rope_caches_for(cfg, cap)
+    orc = oracle_for(cfg, w)
+    want = orc.forward(np.array(seq[:-1], np.uint32), sin, cos, logits_from=prompt.size)
+    check_rows(np.array(got), want, "step")
+    full = np.array(seq + ids[:-1], np.uint32)
+    want2 = orc.forward(full, sin, cos, logits_from=len(seq) - 1)
+    check_greedy(ids, want2)
+
+
 def test_decode_step_logits_match(lib):
     from reng.model import Engine
     from reng.rope import rope_caches_for
