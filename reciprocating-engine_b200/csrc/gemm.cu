@@ -61,11 +61,27 @@ __host__ __device__ constexpr int gemm_threads_max() { return 64 + 128 * epi_war
 constexpr int kGemmMaxStages = 8;  // pipeline stages (runtime: GemmArgs::stages)
 constexpr int kGemmStageBudget = 200 * 1024;                  // stage bytes of a one-per-SM launch
 constexpr int kGemmMaxDynSmem = kGemmStageBudget + 2048;      // + the 1024-byte alignment slack
-constexpr int kStageA = 8 * kBlockBytesBf16;  // 128 rows x 64 k
+constexpr int kStageA = 8 * kBlockBytesBf16;   // 128 rows x 64 k bf16 (the MMA's A operand)
+constexpr int kStageA8 = 8 * kBlockBytesFp8;   // the same rows as FP8-E4M3 codes (weight-only FP8)
 using namespace tc;
 
 __device__ __forceinline__ void named_sync_epilogue() {
     asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 64) : "memory");
+}
+
+// Eight E4M3 codes (two words, low byte first) -> eight bf16, exactly
+// (every E4M3 value is an f16 and a bf16 value).
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    return pack_bf16x2(f.x, f.y);
+}
+__device__ __forceinline__ uint4 e4m3x8_to_bf16x8(uint32_t a, uint32_t b) {
+    return make_uint4(f16x2_to_bf16x2(e4m3x2_to_f16x2(a & 0xffffu)), f16x2_to_bf16x2(e4m3x2_to_f16x2(a >> 16)),
+                      f16x2_to_bf16x2(e4m3x2_to_f16x2(b & 0xffffu)), f16x2_to_bf16x2(e4m3x2_to_f16x2(b >> 16)));
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
 }
 
 __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
@@ -81,7 +97,7 @@ __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
 // matrix, TMEM lane `lr` of the super-tile): columns cb*16 .. +16 of the
 // CTA's N-tile, activation rows m = n0 + cb*16 .. +16 of the launch.
 template <int EPI>
-__device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, int cb, int n0, const float (&v)[16],
+__device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, int cb, int n0, float (&v)[16],
                                               float* am_v, int* am_i, int warp_e) {
     const GemvArgs& a = g.e;
     const int lane = lr & 31;
@@ -89,6 +105,11 @@ __device__ __forceinline__ void tc_epilogue16(const GemmArgs& g, int p, int lr, 
     // rows past the matrix (the last 16-row tile, the last 128-row CTA
     // tile) are computed but never stored
     const bool valid = tile < g.tiles16 && (EPI == EPI_SWIGLU || EPI == EPI_QKV || EPI == EPI_LOGITS || p < a.ldo);
+    if (EPI != EPI_LOGITS && a.w8) {  // FP8 codes: the packed row's scale
+        const float sc = valid ? a.wscale[p] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] *= sc;
+    }
     // every global load of the 16 columns is issued before the arithmetic
     // that needs it (one round trip per group, not one per column)
     if (EPI == EPI_RESID) {
@@ -221,6 +242,7 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int kEpiW = (int)(blockDim.x - 64) >> 7;  // epilogue warps per lane quarter
     __shared__ __align__(8) unsigned long long full[kGemmMaxStages], empty[kGemmMaxStages], accum;
+    __shared__ __align__(8) unsigned long long conv[kGemmMaxStages];  // FP8: a stage's A operand converted
     __shared__ uint32_t tmem_base_s;
     __shared__ int s_flag;
     __shared__ float am_v[EPI == EPI_LOGITS ? 4 * kRowsCap : 1];
@@ -245,8 +267,14 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
     const int C = g.C, nu = (nk + C - 1) / C;
     const int rot = nu > 0 ? (int)(((unsigned)S * 2654435761u) % (unsigned)nu) : 0;
     const int N = g.N, SG = g.stages;
-    const uint32_t stage_bytes = (uint32_t)C * (kStageA + (uint32_t)N * 128u);
-    const uint32_t b_off = (uint32_t)C * kStageA;  // a stage's activation tiles follow its C weight tiles
+    // a stage: C bf16 weight tiles (the A operand), with FP8 weights then C
+    // tiles of their codes (converted into the A tiles by the epilogue warps
+    // during the mainloop), then C activation tiles
+    const bool w8 = g.e.w8 != 0;
+    const uint32_t stage_bytes = (uint32_t)C * (kStageA + (w8 ? kStageA8 : 0u) + (uint32_t)N * 128u);
+    const uint32_t f8_off = (uint32_t)C * kStageA;
+    const uint32_t b_off = (uint32_t)C * (kStageA + (w8 ? kStageA8 : 0u));
+    const uint32_t bar_conv = (uint32_t)__cvta_generic_to_shared(&conv[0]);
     // 1024-byte alignment of the stage buffers (the swizzle atoms)
     const uint32_t smem0 = ((uint32_t)__cvta_generic_to_shared(smem_raw) + 1023u) & ~1023u;
     const uint32_t bar_full = (uint32_t)__cvta_generic_to_shared(&full[0]);
@@ -259,6 +287,7 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
         for (int s = 0; s < SG; s++) {
             bar_init(bar_full + 8 * s, 1);
             bar_init(bar_empty + 8 * s, 1);
+            bar_init(bar_conv + 8 * s, (blockDim.x - 64) / 32);  // one arrival per epilogue warp
         }
         bar_init(bar_acc, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -289,9 +318,10 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
                 int c0, cnt;
                 unit(i, c0, cnt);
                 // one copy of C chunks x 8 tiles (tiles past the matrix and
-                // chunks past kc land as zeros)
-                tensor_g2s_4d(smem0 + (uint32_t)(i % SG) * stage_bytes, &tmap_w, 0, 0, 8 * S, c0,
-                              bar_full + 8 * (i % SG));
+                // chunks past kc land as zeros); FP8 codes into the stage's
+                // code tiles
+                tensor_g2s_4d(smem0 + (uint32_t)(i % SG) * stage_bytes + (w8 ? f8_off : 0u), &tmap_w, 0, 0, 8 * S,
+                              c0, bar_full + 8 * (i % SG));
             };
             const uint32_t tx_b = (uint32_t)N * 128u;
             auto issue_b = [&](int i) {
@@ -308,7 +338,7 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
             auto tx_of = [&](int i) {
                 int c0, cnt;
                 unit(i, c0, cnt);
-                return (uint32_t)C * kStageA + (uint32_t)(g.b3d ? C : cnt) * tx_b;
+                return (uint32_t)C * (w8 ? kStageA8 : kStageA) + (uint32_t)(g.b3d ? C : cnt) * tx_b;
             };
             const int pre = min(SG, nu);
             // the weights do not depend on the previous kernel
@@ -348,7 +378,8 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
             int done = 0;
             for (int i = 0; i < nu; i++) {
                 const int s = i % SG;
-                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
+                if (!bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1)) ||
+                    (w8 && !bar_wait(bar_conv + 8 * s, (uint32_t)((i / SG) & 1)))) {
                     atomicExch(g.e.err, RENG_E_TIMEOUT);
                     break;
                 }
@@ -377,6 +408,36 @@ __global__ void __launch_bounds__(gemm_threads_max<EPI>(), 1) k_gemm_tc(const __
         const int q4 = warp & 3, warp_e = (warp - 2) & 3, eh = (warp - 2) >> 2;
         const int lr = 32 * q4 + lane;       // TMEM lane = row of the super-tile
         const int p = 128 * S + lr;          // packed row of the matrix
+        if (w8) {
+            // FP8 weights: while the MMAs run, every stage's codes become its
+            // bf16 A tiles.  Epilogue thread ct converts 16-code pieces ct,
+            // ct + nconv, ...: chunk q, row R of the super-tile, k 16 kq .. +16
+            // (row R of a 2 KB-block pair at R * 128 bytes, 16-byte chunk j
+            // at j ^ (R % 8), as the bf16 weight copies land).
+            const int nconv = blockDim.x - 64, ct = threadIdx.x - 64;
+            for (int i = 0; i < nu; i++) {
+                const int s = i % SG;
+                if (!failed && !bar_wait(bar_full + 8 * s, (uint32_t)((i / SG) & 1))) {
+                    failed = true;
+                    if (lane == 0) atomicExch(g.e.err, RENG_E_TIMEOUT);
+                }
+                if (!failed) {
+                    const uint32_t st0 = smem0 + (uint32_t)s * stage_bytes;
+                    for (int pc = ct; pc < C * 512; pc += nconv) {
+                        const int q = pc >> 9, R = (pc >> 2) & 127, kq = pc & 3;
+                        const uint4 f = lds128(st0 + f8_off + (uint32_t)q * kStageA8 + (uint32_t)R * 64u +
+                                               (uint32_t)kq * 16u);
+                        const uint32_t row = st0 + (uint32_t)q * kStageA + (uint32_t)R * 128u;
+                        sts128(row + (uint32_t)(((2 * kq) ^ (R & 7)) << 4), e4m3x8_to_bf16x8(f.x, f.y));
+                        sts128(row + (uint32_t)(((2 * kq + 1) ^ (R & 7)) << 4), e4m3x8_to_bf16x8(f.z, f.w));
+                    }
+                }
+                // the A tiles are read by the tensor cores (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(bar_conv + 8 * s);
+            }
+        }
         if (!bar_wait(bar_acc, 0)) {
             failed = true;
             if (lane == 0) atomicExch(g.e.err, RENG_E_TIMEOUT);
@@ -609,6 +670,23 @@ int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* o
     return RENG_OK;
 }
 
+int gemm_weight_map8(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (tiles16 < 1 || kc < 1 || c < 1 || c > 4 || ((uintptr_t)w & 15))
+        return fail(RENG_E_INVAL, "gemm_weight_map8: bad shape");
+    cuuint64_t dims[4] = {64, (cuuint64_t)kTileRows, (cuuint64_t)tiles16, (cuuint64_t)kc};
+    cuuint64_t strides[3] = {64, (cuuint64_t)kc * kBlockBytesFp8, (cuuint64_t)kBlockBytesFp8};
+    cuuint32_t box[4] = {64, (cuuint32_t)kTileRows, 8, (cuuint32_t)c};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)w, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(RENG_E_CUDA, "cuTensorMapEncodeTiled (FP8 weights) failed (" + std::to_string((int)r) + ")");
+    return RENG_OK;
+}
+
 // A layer's K or V cache [slot][kv head][cap][hd] bf16 as 2-D rows of hd
 // elements, read in {64, box_rows} boxes with the 128-byte swizzle (with 128
 // rows, the tcgen05 operand layout of 128 keys x 64 head dims).  Rows past
@@ -629,7 +707,9 @@ int attn_cache_map(const uint16_t* cache, int hd, long long rows, int box_rows, 
     return RENG_OK;
 }
 
-size_t gemm_smem_bytes(int n, int stages, int c) { return (size_t)stages * c * (kStageA + (size_t)n * 128) + 1024; }
+size_t gemm_smem_bytes(int n, int stages, int c, bool w8) {
+    return (size_t)stages * c * (kStageA + (w8 ? kStageA8 : 0) + (size_t)n * 128) + 1024;
+}
 
 int gemm_chunks_per_stage(int n) {
     static const int fixed = [] {  // RENG_GEMM_C: chunks per stage, 1 or 2 (a tuning knob)
@@ -641,7 +721,7 @@ int gemm_chunks_per_stage(int n) {
     (void)n;
 }
 
-int gemm_pick_stages(int n, bool one_per_sm, int epi, int c) {
+int gemm_pick_stages(int n, bool one_per_sm, int epi, int c, bool w8) {
     // Two CTAs per SM (no cluster): as many stages as fit in half the SM's
     // 228 KB beside the kernel's static shared memory, the 1 KB alignment
     // slack and the 1 KB per-CTA reservation (6 at N = 16, 5 at N = 32, 4 at
@@ -649,7 +729,7 @@ int gemm_pick_stages(int n, bool one_per_sm, int epi, int c) {
     // 4 stages; measured on B200 (Llama-8B widths, 64 rows), 8 stages at one
     // CTA per SM were slower than 4 (q/k/v 55 against 33 us).
     // stages of c chunks: the same bytes in flight as c x as many one-chunk stages
-    const unsigned stage = (unsigned)c * (kStageA + (unsigned)n * 128u);
+    const unsigned stage = (unsigned)c * (kStageA + (w8 ? kStageA8 : 0u) + (unsigned)n * 128u);
     const unsigned fixed = 2048u + (epi == EPI_LOGITS ? 9216u : 1024u);
     static const int one_sm = [] {  // RENG_GEMM_STAGES1: stages at one CTA per SM (a tuning knob)
         const char* v = getenv("RENG_GEMM_STAGES1");
@@ -669,7 +749,7 @@ static cudaError_t launch_tc_t(const CUtensorMap& map, const CUtensorMap& wmap, 
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(g.super_tiles * g.ntiles * g.ks);
     cfg.blockDim = dim3(64 + 128 * (g.N > 64 ? epi_warps_max<EPI>() : 1));
-    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(g.N, g.stages, g.C, g.e.w8 != 0);
     cfg.stream = st;
     int na = 0;
     if (g.ks > 1 && g.gpart == nullptr) {  // the K splits of a super-tile form one cluster
@@ -712,7 +792,7 @@ cudaError_t gemm_prepare() {
 }
 
 void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks_out, int* stages_out,
-               bool* gsplit_out, int* c_out) {
+               bool* gsplit_out, int* c_out, bool w8) {
     // Enough super-tiles to occupy the SMs (or the LM head, whose argmax
     // needs whole rows per CTA): one CTA per super-tile, two per SM at N <= 64.
     // Else split K over up to 8 CTAs.  At N = 16 the splits are plain CTAs
@@ -735,8 +815,9 @@ void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok,
     }
     *ks_out = ks;
     *gsplit_out = ks > 1 && gsplit;
-    *c_out = gemm_chunks_per_stage(n);
-    *stages_out = gemm_pick_stages(n, (ks > 1 && !gsplit) || n > 64, epi, *c_out);
+    // FP8 weights also stage their codes: one chunk per stage above 128 columns
+    *c_out = w8 && n > 128 ? 1 : gemm_chunks_per_stage(n);
+    *stages_out = gemm_pick_stages(n, (ks > 1 && !gsplit) || n > 64, epi, *c_out, w8);
 }
 
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
@@ -745,7 +826,7 @@ cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, cons
         g.e.M > g.N * g.ntiles || g.e.M > kGemmRowsMax || g.e.M < 1 || g.ks < 1 ||
         g.ks > kGemmMaxSplits || (epi == EPI_LOGITS && g.ks != 1) || g.stages < 2 || g.stages > kGemmMaxStages ||
         g.C < 1 || g.C > 4 || (g.b3d && g.kc * kChunkK != g.e.K) ||
-        gemm_smem_bytes(g.N, g.stages, g.C) > (size_t)kGemmMaxDynSmem ||
+        gemm_smem_bytes(g.N, g.stages, g.C, g.e.w8 != 0) > (size_t)kGemmMaxDynSmem || (g.e.w8 && !g.e.wscale) ||
         (g.ks > 1 && g.gpart == nullptr &&
          (size_t)g.stages * g.C * (kStageA + (size_t)g.N * 128) < (size_t)128 * (g.N + 4) * 4) ||
         (g.gpart != nullptr && g.gcnt == nullptr))
@@ -902,7 +983,7 @@ extern "C" int reng_gemm_bf16(const uint16_t* w, int rows, int K, const uint16_t
         const int kper = (kc + s - 1) / s;
         g.ks = (kc + kper - 1) / kper;
         gsplit = splits < 0 && g.ks > 1;
-        g.stages = gemm_pick_stages(N, (g.ks > 1 && !gsplit) || N > 64, EPI_F32, g.C);
+        g.stages = gemm_pick_stages(N, (g.ks > 1 && !gsplit) || N > 64, EPI_F32, g.C, false);
     }
     if (gsplit) {
         GEMM_CU(f.alloc(&g.gpart, (size_t)g.super_tiles * g.ntiles * g.ks * 128 * N * 4));

@@ -39,7 +39,11 @@ int gemm_tensor_map(const uint16_t* x, int rows, int K, int n, CUtensorMap* out)
 int gemm_tensor_map3(const uint16_t* x, int rows, int K, int n, int c, CUtensorMap* out);
 // Packed bf16 weights [tiles16][kc][2 KB] as {64, 16, 8 tiles, c chunks} boxes.
 int gemm_weight_map(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out);
-size_t gemm_smem_bytes(int n, int stages, int c);
+size_t gemm_smem_bytes(int n, int stages, int c, bool w8);
+// Packed FP8-E4M3 weights [tiles16][kc][1 KB] (row r of a block at r * 64
+// bytes) as {64 bytes, 16 rows, 8 tiles, c chunks} boxes, for the GEMM's
+// weight-only FP8 path.
+int gemm_weight_map8(const uint8_t* w, int tiles16, int kc, int c, CUtensorMap* out);
 // A layer's K or V cache as {64, box_rows} boxes of hd-wide rows (128-byte swizzle).
 int attn_cache_map(const uint16_t* cache, int hd, long long rows, int box_rows, CUtensorMap* out);
 // Prefill-block attention on the tensor cores (attn_prefill.cu): whether a
@@ -58,13 +62,13 @@ int launch_attn_ring(const AttnArgs& a, long long cache_rows, int* err, bool pdl
 int gemm_chunks_per_stage(int n);
 // Pipeline stages of c chunks for MMA width n: as many as fit two CTAs per
 // SM, or at one CTA per SM the bytes in flight of 4 one-chunk stages.
-int gemm_pick_stages(int n, bool one_per_sm, int epi, int c);
+int gemm_pick_stages(int n, bool one_per_sm, int epi, int c, bool w8);
 // Raise the dynamic shared-memory limit of every GEMM instantiation (call
 // once per device before capture).
 cudaError_t gemm_prepare();
 // K splits and pipeline stages of a launch over super_tiles x kc blocks.
 void gemm_plan(int super_tiles, int kc, int n, int epi, int sms, bool gsplit_ok, int* ks, int* stages, bool* gsplit,
-               int* c);
+               int* c, bool w8 = false);
 cudaError_t launch_gemm_tc(const CUtensorMap& map, const CUtensorMap& wmap, const GemmArgs& g, int epi, bool pdl,
                            cudaStream_t st);
 // xn[m] = bf16(x[m] * 1/sqrt(sum_t ss[t][m] / H + eps) * gain), m < M.

@@ -285,9 +285,6 @@ int validate(const reng_model_desc* d) {
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights need the intermediate size per rank (" +
                                             std::to_string(d->inter / d->tp_world) + ") to be a multiple of 16");
     RENG_CHECK_ARG(d->qk_norm == 0 || d->qk_norm == 1, "reng_model_create: qk_norm must be 0 or 1");
-    if (d->weights == RENG_WEIGHTS_FP8_E4M3 && d->batch > kMaxRows)
-        return fail(RENG_E_UNSUPPORTED, "reng_model_create: FP8 weights run batch <= " + std::to_string(kMaxRows) +
-                                            ", not " + std::to_string(d->batch));
     if (d->batch > kRowsCap)
         return fail(RENG_E_UNSUPPORTED, "reng_model_create: batch " + std::to_string(d->batch) + " above " +
                                             std::to_string(kRowsCap));
@@ -360,7 +357,7 @@ GemvArgs norm_args(reng_model* m, int M, const float* gain) {
 // The LM head (kind 4) does too unless the register-fragment GEMV takes it
 // (173 against 206 us at batch 8).
 bool use_gemm(const reng_model* m, int M, int kind) {
-    if (m->w8) return false;
+    if (m->w8) return M > kMaxRows;  // FP8: the GEMV up to its 8 rows, then the GEMM (codes converted in shared memory)
     return M > kMaxRows || (M >= 4 && (kind == 3 || (kind == 4 && !m->gemv8)));
 }
 
@@ -394,7 +391,7 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
     a.N = N;
     a.ntiles = (g.M + N - 1) / N;
     bool gsplit = false;
-    gemm_plan(a.super_tiles * a.ntiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit, &a.C);
+    gemm_plan(a.super_tiles * a.ntiles, g.kc, N, epi, m->sms, true, &a.ks, &a.stages, &gsplit, &a.C, g.w8 != 0);
     if (gsplit) {
         if ((size_t)a.super_tiles * a.ntiles * a.ks * 128 * N > m->gpart_floats ||
             a.super_tiles * a.ntiles > kGemmCntMax)
@@ -410,7 +407,10 @@ int linear(reng_model* m, const GemvArgs& g, int epi, int kind, int max_grid, cu
         TRY(gemm_tensor_map3(x, kBlockRows, g.K, N, a.C, &map));
     else
         TRY(gemm_tensor_map(x, kBlockRows, g.K, N, &map));
-    TRY(gemm_weight_map(g.w, g.tiles, g.kc, a.C, &wmap));
+    if (g.w8)
+        TRY(gemm_weight_map8(g.w, g.tiles, g.kc, a.C, &wmap));
+    else
+        TRY(gemm_weight_map(g.w, g.tiles, g.kc, a.C, &wmap));
     CU(launch_gemm_tc(map, wmap, a, epi, true, st));
     m->launches++;
     return RENG_OK;
@@ -1019,10 +1019,10 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     return RENG_OK;
 }
 
-// Prompt rows per prefill block: kBlockRows on the GEMM path (bf16), the
-// GEMV width for FP8 weights; RENG_PREFILL_ROWS lowers it (a tuning knob).
+// Prompt rows per prefill block: kBlockRows (the GEMM path, FP8 weights
+// included); RENG_PREFILL_ROWS lowers it (a tuning knob).
 int prefill_rows(const reng_model* m) {
-    int r = m->w8 ? kMaxRows : kBlockRows;
+    int r = kBlockRows;
     const char* v = getenv("RENG_PREFILL_ROWS");
     if (v) {
         const int x = atoi(v);

@@ -103,3 +103,70 @@ def test_fp8_llama8b_widths_two_layers(reng_lib):
     assert cosine(last, want[0]) >= 0.999 and rel_l2(last, want[0]) < 0.05
     check_greedy([nxt] + ids, want)
     e.close()
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_fp8_gemm_prefill_block(reng_lib, bias):
+    """A 300-row FP8 prefill block runs on the tcgen05 GEMM (two N-tiles):
+    the E4M3 codes are copied into shared memory, converted to bf16 there
+    by the epilogue warps while the MMAs run, and the per-row scale is
+    applied in the epilogue; every row's logits against the f32 forward on
+    the dequantized weights."""
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg(bias=bias)
+    w = random_weights(cfg, seed=33)
+    e = Engine(cfg, w, batch=1, capacity=320, fp8=("e4m3", "pcs"))
+    prompt = prompt_ids(300, cfg.vocab_size, seed=7)
+    _, _, allg = e.prefill(0, prompt, all_logits=True)
+    e.close()
+    sin, cos = rope_caches_for(cfg, 320)
+    check_rows(allg, oracle_for(cfg, dequantized(w)).forward(prompt, sin, cos), "fp8 GEMM prefill")
+
+
+@pytest.mark.parametrize("B", [16, 24])
+def test_fp8_wide_batch_decode(reng_lib, B):
+    """FP8 decode above the GEMV's 8 rows: the step's projections run on the
+    FP8 GEMM (codes converted in shared memory); staggered prompts, greedy
+    ids against the teacher-forced f32 forward on the dequantized weights."""
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = small_cfg()
+    w = random_weights(cfg, seed=34)
+    e = Engine(cfg, w, batch=B, capacity=64, fp8=("e4m3", "pcs"))
+    prompts = [prompt_ids(9 + b % 5, cfg.vocab_size, seed=80 + b) for b in range(B)]
+    seeds = [e.prefill(b, prompts[b])[0] for b in range(B)]
+    ids = e.decode(seeds, 8)
+    e.close()
+    sin, cos = rope_caches_for(cfg, 64)
+    orc = oracle_for(cfg, dequantized(w))
+    for b in range(B):
+        seq = np.concatenate([prompts[b], [seeds[b]], ids[:-1, b]]).astype(np.uint32)
+        check_greedy([seeds[b]] + list(ids[:, b]), orc.forward(seq, sin, cos, logits_from=prompts[b].size - 1))
+
+
+def test_fp8_llama8b_widths_gemm_prefill(reng_lib):
+    """The FP8 GEMM at Llama-8B widths (2 layers): a 280-token prompt as one
+    block, the last row's logits and the greedy continuation."""
+    from reng.config import llama31_8b
+    from reng.model import Engine
+    from reng.rope import rope_caches_for
+    from reng.synth import prompt_ids
+    from reng.weights import random_weights
+    cfg = llama31_8b()
+    w = random_weights(cfg, seed=8, layers=2)
+    cfg.num_hidden_layers = 2
+    e = Engine(cfg, w, batch=1, capacity=320, fp8=("e4m3", "pcs"))
+    prompt = prompt_ids(280, cfg.vocab_size, seed=9)
+    nxt, last, _ = e.prefill(0, prompt, last_logits=True)
+    ids = [int(x) for x in e.decode([nxt], 4)[:, 0]]
+    e.close()
+    sin, cos = rope_caches_for(cfg, 320)
+    seq = np.concatenate([prompt, [nxt], ids[:-1]]).astype(np.uint32)
+    want = oracle_for(cfg, dequantized(w)).forward(seq, sin, cos, logits_from=prompt.size - 1)
+    assert cosine(last, want[0]) >= 0.999 and rel_l2(last, want[0]) < 0.05
+    check_greedy([nxt] + ids, want)
