@@ -602,25 +602,6 @@ def fp8_quant_bench(dev, iters=4):
             "gbs": b / (ms / 1e3) / 1e9, "frac": b / (ms / 1e3) / 1e9 / peak, "peak_kind": kind}
 
 
-def trace_summary(rows):
-    """Mean per phase kind of (duration, arrival spread, barrier, first and
-    last arrival), microseconds, of one persistent-step timeline."""
-    import numpy as np
-    kinds = {}
-    for i, (name, start, first, last, staged, loop) in enumerate(rows):
-        k = "".join(ch for ch in name if not ch.isdigit())
-        nxt = rows[i + 1][1] if i + 1 < len(rows) else last
-        kinds.setdefault(k, []).append((nxt - start, last - first, nxt - last, first - start, last - start,
-                                        staged - start if staged else 0.0, loop - start if loop else 0.0))
-    out = {}
-    for k, v in kinds.items():
-        a = np.array(v).mean(0)
-        out[k] = {"n": len(v), "us": round(a[0], 2), "spread_us": round(a[1], 2), "barrier_us": round(a[2], 2),
-                  "first_done_us": round(a[3], 2), "last_done_us": round(a[4], 2),
-                  "cta0_staged_us": round(a[5], 2), "cta0_loop_done_us": round(a[6], 2)}
-    return out
-
-
 def run_profile(args, cfg):
     """The small case of the ncu captures (one GPU, a few GB on the device):
     a layer-truncated model of the workload's widths (`--layers`), then
@@ -631,7 +612,6 @@ def run_profile(args, cfg):
         (after a --ctx prompt), attention in its prefill form,
       * with --decode-steps N: a 16-token prompt in every slot and N greedy
         steps through the step graph (device ms per step),
-      * with --trace: the persistent step kernel's phase timeline,
       * with --quant N: N config-0 FP8 quantizations (bf16 [4096, 4096] ->
         E4M3 per-channel) on device buffers,
       * with --gemm shapes: the tcgen05 GEMM alone (reng_gemm_bf16) on
@@ -693,16 +673,13 @@ def run_profile(args, cfg):
             e.prefill(0, prompt_ids(args.ctx, cfg.vocab_size, seed=2))
         rep["prefill_rows"] = args.rows
         rep["prefill_kernel_us"] = {k: round(v * 1e3, 2) for k, v in e.time_kernels(args.iters, rows=args.rows).items()}
-    if args.decode_steps > 0 or args.trace:
+    if args.decode_steps > 0:
         p = prompt_ids(16, cfg.vocab_size, seed=1)
         seeds = [e.prefill(b, p)[0] for b in range(args.batch)]
         e.decode(seeds, max(1, args.decode_steps))
         t = e.last_times()
         rep["decode"] = {"steps": t.steps, "ms_per_step": round(t.device_ms / t.steps, 4),
                          "kernels_per_step": t.kernels_per_step}
-        if args.trace:
-            rows = e.trace_step()
-            rep["trace"] = {"step_us": round(rows[-1][3], 1), "phases": trace_summary(rows)}
     print(json.dumps(rep))
     e.close()
 
@@ -737,7 +714,6 @@ def main():
     pg.add_argument("--ctx", type=int, default=0, help="prompt tokens prefilled in every slot before the kernel timing")
     pg.add_argument("--rows", type=int, default=0, help="also time each kernel kind at a prefill block of this many rows")
     pg.add_argument("--decode-steps", type=int, default=0)
-    pg.add_argument("--trace", action="store_true")
     pg.add_argument("--no-kinds", dest="kinds", action="store_false")
     pg.add_argument("--quant", type=int, default=0, help="FP8 quantizations of the config-0 matrix")
     pg.add_argument("--gemm", default="", help="rows,K,M[;rows,K,M...]: the tcgen05 GEMM alone on these shapes")

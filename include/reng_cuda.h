@@ -48,8 +48,9 @@ extern "C" {
 const char *reng_last_error(void);
 
 /* ABI version: (major << 16) | minor.  Minor 2 added reng_model_desc.qk_norm
- * and reng_layer_weights.qn / kn / no_rope; callers built against minor 1
- * pass structs that are too short. */
+ * and reng_layer_weights.qn / kn / no_rope (callers built against minor 1
+ * pass structs that are too short); minor 3 added
+ * reng_model_time_kernels_rows and removed reng_model_trace_step. */
 int reng_version(void);
 
 /* Number of CUDA devices (replaces reng-hal's Gaudi accel discovery,
@@ -271,21 +272,6 @@ int reng_model_time_kernels(reng_model *m, int iters, float *ms_out);
  * attention runs the prefill form and the LM head every row.  rows is at
  * most the engine's prefill block.  Every slot is reset afterwards. */
 int reng_model_time_kernels_rows(reng_model *m, int rows, int iters, float *ms_out);
-
-/* Phase timeline of one decode step of the persistent step kernel (the
- * models it runs: one CUDA-graph node per step).  Runs one step from the
- * slots' current state (the ids of the last decode call's first step) and
- * writes, per phase p < *n_phases (at most max_phases), out[5p] = when the
- * barrier before phase p released (CTA 0's view), out[5p+1] / out[5p+2] =
- * the earliest / latest CTA arrival at the barrier after it, out[5p+3] /
- * out[5p+4] = for a projection phase, when CTA 0 had its x rows staged and
- * when its last warp left the weight loop (0 otherwise), in ns from the
- * kernel's start.  Phases: embedding, then per layer q/k/v, attention,
- * o_proj, gate/up, down_proj, then the LM head.  RENG_E_STATE when the model
- * runs per-projection kernels.  Advances every slot by one position.  The
- * reference profiles through SynapseAI traces (tools/profile/README.md).
- */
-int reng_model_trace_step(reng_model *m, uint64_t *out, int max_phases, int *n_phases);
 
 /* ==================================================== packed GEMM ===
  * y[m][r] = sum_k x[m][k] * w[r][k] (f32 out) through the tcgen05 GEMM the

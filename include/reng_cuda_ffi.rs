@@ -80,8 +80,6 @@ extern "C" {
     pub fn reng_model_device_bytes(m: *const reng_model, bytes: *mut u64) -> c_int;
     pub fn reng_model_time_kernels(m: *mut reng_model, iters: c_int, ms_out: *mut f32) -> c_int;
     pub fn reng_model_time_kernels_rows(m: *mut reng_model, rows: c_int, iters: c_int, ms_out: *mut f32) -> c_int;
-    pub fn reng_model_trace_step(m: *mut reng_model, out: *mut u64, max_phases: c_int,
-                                 n_phases: *mut c_int) -> c_int;
     pub fn reng_gemm_bf16(w: *const u16, rows: c_int, k: c_int, x: *const u16, m: c_int, y: *mut f32,
                           splits: c_int, iters: c_int, ms_out: *mut f32, mem: c_int) -> c_int;
     pub fn reng_tp_unique_id(out: *mut u8) -> c_int;

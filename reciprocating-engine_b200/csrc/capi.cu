@@ -38,7 +38,7 @@ int num_sms(int device) {
 extern "C" const char* reng_last_error(void) { return reng::g_last_error.c_str(); }
 
 // minor 2: reng_model_desc.qk_norm, reng_layer_weights.qn / kn / no_rope
-extern "C" int reng_version(void) { return (0 << 16) | 2; }
+extern "C" int reng_version(void) { return (0 << 16) | 3; }
 
 extern "C" int reng_device_count(int* count) {
     RENG_CHECK_ARG(count != nullptr, "reng_device_count: count is NULL");

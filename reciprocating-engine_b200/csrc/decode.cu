@@ -30,8 +30,8 @@ namespace reng {
 
 // ------------------------------------------------------------------ GEMV --
 
-// The device pieces shared with the persistent step kernel (x fragments,
-// block MMAs, tile epilogues, the TMA ring primitives) are in gemv_core.cuh.
+// The device pieces (x fragments, block MMAs, tile epilogues, the TMA ring
+// primitives) are in gemv_core.cuh.
 
 // Weight ring bytes of one warp with ST stages.
 template <int ST>

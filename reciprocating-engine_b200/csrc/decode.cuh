@@ -92,8 +92,6 @@ struct GemvArgs {
     int cap;
     // EPI_LOGITS
     int vocab;
-    float* am_val;          // (persistent step kernel) per-warp partials [warps][kMaxRows]
-    int* am_idx;
     unsigned long long* am_key;  // [kRowsCap] running maximum of am_pack keys per row, 0 between launches
     unsigned int* am_count;
     int mode;               // 0 decode, 1 prefill

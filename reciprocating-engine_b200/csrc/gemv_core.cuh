@@ -1,8 +1,7 @@
-// Device pieces of the packed-weight GEMV shared by the per-projection
-// kernels (decode.cu) and the persistent decode-step kernel (step.cu): the x
-// fragments of the m16n8k16 MMAs, one packed block into the accumulators,
-// the tile epilogues, and the mbarrier / bulk-copy primitives of the
-// per-warp TMA weight rings.
+// Device pieces of the packed-weight GEMV (decode.cu, and gemv8.cu / gemm.cu
+// for the primitives): the x fragments of the m16n8k16 MMAs, one packed
+// block into the accumulators, the tile epilogues, and the mbarrier /
+// bulk-copy primitives of the per-warp TMA weight rings.
 #pragma once
 #include "decode.cuh"
 
@@ -194,10 +193,8 @@ __device__ __forceinline__ void am_reduce_g(float& bv, int& bi) {
 
 
 // The epilogue of one 16-row tile on one warp: acc holds rows {g, g+8} x
-// activation rows {2q, 2q+1}.  Data written earlier in the same launch
-// (x_res, the row bookkeeping) is read through L2 (ld.global.cg): the
-// persistent step kernel runs every phase in one launch and L1 is not
-// coherent across SMs.
+// activation rows {2q, 2q+1}.  x_res and the row bookkeeping are read
+// through L2 (ld.global.cg), not the SM's incoherent L1.
 template <int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int tile, const float (&acc)[4], int g,
                                               int q, float (&best_v)[2], int (&best_i)[2]) {

@@ -12,7 +12,6 @@
 #include <vector>
 
 #include "gemm.cuh"
-#include "step.cuh"
 
 using namespace reng;
 
@@ -64,19 +63,12 @@ struct reng_model {
     float* gpart = nullptr;          // GEMM split-K partials (splits without a cluster)
     size_t gpart_floats = 0;
     int* gcnt = nullptr;             // GEMM split-K arrivals per super-tile
-    // the persistent decode step (one cooperative launch per step) when the
-    // shape allows it, else the per-projection kernels
-    bool step_on = false;
-    int step_grid = 0;
-    StepCtl step_ctl{};
     float* ss = nullptr;
     float* part = nullptr;  // tensor-parallel f32 partials [kBlockRows][hidden]
     int *row_slot = nullptr, *row_pos = nullptr, *pos = nullptr, *step = nullptr;
     int* err = nullptr;  // device error word of the bounded waits
     int w8 = 0;          // projections held as FP8-E4M3 codes + row scales
     uint32_t *ids_ring = nullptr, *prefill_ids = nullptr, *next_id = nullptr;
-    float* am_val = nullptr;
-    int* am_idx = nullptr;
     unsigned int* am_count = nullptr;
     unsigned long long* am_key = nullptr;  // [kBlockRows] LM-head argmax keys
     int lm_grid = 0;
@@ -589,8 +581,6 @@ GemvArgs head_args(reng_model* m, int mode, int M, int slot, int r0, bool shard 
     h.out = m->logits;
     h.ldo = m->vocab;
     h.vocab = m->vocab;
-    h.am_val = m->am_val;
-    h.am_idx = m->am_idx;
     h.am_count = m->am_count;
     h.am_key = m->am_key;
     h.mode = mode;
@@ -635,117 +625,6 @@ int enqueue_step(reng_model* m, int mode, int M, int slot, int head, cudaStream_
     return RENG_OK;
 }
 
-// The phase table and scratch of the persistent step kernel (decode rows =
-// the B slots), when RENG_STEP_KERNEL=1 asks for it.  Measured on B200
-// (Llama-8B b1) it is behind the per-projection kernels (3.86 against 3.40
-// ms per step: each phase pays a grid barrier, the x staging and the tile
-// reductions, about as much as a launch), so it is not the default.  Leaves
-// step_on false when the shape is outside what it runs (tensor parallel,
-// batch > 8, head_dim above 128, shared memory).
-int build_step(reng_model* m) {
-    m->step_on = false;
-    const char* env = getenv("RENG_STEP_KERNEL");
-    if (!env || atoi(env) != 1) return RENG_OK;
-    if (m->world > 1 || m->B > kMaxRows || m->hd > 128 || m->hpg > kAttnMaxHpgStep || m->qk_norm ||
-        m->any_no_rope)
-        return RENG_OK;
-    const int M = m->B;
-    std::vector<StepPhase> ph;
-    StepPhase pe{};
-    pe.kind = PH_EMBED;
-    pe.em = embed_args(m, 0, M, 0);
-    ph.push_back(pe);
-    auto gemv = [&](const GemvArgs& g, int epi) {
-        StepPhase p{};
-        p.kind = PH_GEMV;
-        p.epi = epi;
-        p.g = g;
-        p.blocks = (long long)g.tiles * g.kc;
-        ph.push_back(p);
-    };
-    for (int l = 0; l < m->L; l++) {
-        gemv(qkv_args(m, l, M), EPI_QKV);
-        StepPhase pa{};
-        pa.kind = PH_ATTN;
-        pa.at = attn_args(m, l, M, 0);
-        ph.push_back(pa);
-        gemv(proj_args(m, l, M, 0), EPI_RESID);
-        gemv(gateup_args(m, l, M), EPI_SWIGLU);
-        gemv(proj_args(m, l, M, 1), EPI_RESID);
-    }
-    gemv(head_args(m, 0, M, 0, 0), EPI_LOGITS);
-    // shared memory: the rings + the x rows of a phase (or the attention q)
-    int xbytes = (int)step_attn_smem_bytes();
-    for (const StepPhase& p : ph)
-        if (p.kind == PH_GEMV)  // x rows + a zero patch + the warps' tile reduction
-            xbytes = std::max(xbytes, (M * step_xstride(p.g.K) * 2 + 128 + 15) / 16 * 16 + step_red_bytes(M));
-    int stages = 4, per_sm = 0;
-    for (; stages >= 2; stages--) {
-        per_sm = step_blocks_per_sm(m->w8, stages, xbytes, (int)ph.size());
-        if (per_sm >= 1) break;
-    }
-    if (per_sm < 1) return RENG_OK;
-    const int grid = m->sms;  // one CTA per SM, all resident (cooperative launch)
-    size_t part_f4 = 0;
-    int max_tiles = 0;
-    for (StepPhase& p : ph) {
-        if (p.kind != PH_GEMV) continue;
-        const long long T = p.blocks, kc = p.g.kc, Gp = std::min<long long>(T, grid);  // CTAs of the phase
-        int slots = 1;
-        for (long long t = 0; t < p.g.tiles; t++) {
-            const long long first = ((t * kc + 1) * Gp - 1) / T, last = ((t + 1) * kc * Gp - 1) / T;
-            slots = std::max(slots, (int)(last - first + 1));
-        }
-        p.slots = slots;
-        part_f4 = std::max(part_f4, (size_t)p.g.tiles * slots * 32);
-        max_tiles = std::max(max_tiles, p.g.tiles);
-    }
-    // attention units (key ranges) per (row, KV group): about one per CTA
-    const int A = std::max(1, std::min(16, grid / (M * m->nkv)));
-    StepCtl& c = m->step_ctl;
-    StepPhase* dph = nullptr;
-    TRY(dalloc(m, &dph, ph.size()));
-    CU(cudaMemcpyAsync(dph, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice, m->st));
-    c.ph = dph;
-    std::vector<StepSeq> seq(ph.size());
-    for (size_t i = 0; i < ph.size(); i++) {
-        StepSeq q{};
-        if (ph[i].kind == PH_GEMV) {
-            q.w = ph[i].g.w;
-            q.blocks = (int)ph[i].blocks;
-            q.kc = (short)ph[i].g.kc;
-            q.bb = (short)(ph[i].g.w8 ? kBlockBytesFp8 : kBlockBytesBf16);
-        }
-        seq[i] = q;
-    }
-    StepSeq* dseq = nullptr;
-    TRY(dalloc(m, &dseq, seq.size()));
-    CU(cudaMemcpyAsync(dseq, seq.data(), seq.size() * sizeof(StepSeq), cudaMemcpyHostToDevice, m->st));
-    c.seq = dseq;
-    c.nph = (int)ph.size();
-    c.stages = stages;
-    c.xbytes = xbytes;
-    c.attn_units = A;
-    TRY(dalloc(m, &c.part, part_f4));
-    TRY(dalloc(m, &c.tile_cnt, (size_t)max_tiles));
-    TRY(dalloc(m, &c.apart, (size_t)M * m->nkv * A * step_attn_part_len(m->hpg, m->hd)));
-    TRY(dalloc(m, &c.acnt, (size_t)M * m->nkv));
-    TRY(dalloc(m, &c.bar, 1));
-    TRY(dalloc(m, &c.abort, 1));
-    CU(cudaMemsetAsync(c.tile_cnt, 0, (size_t)max_tiles * 4, m->st));
-    CU(cudaMemsetAsync(c.acnt, 0, (size_t)M * m->nkv * 4, m->st));
-    CU(cudaMemsetAsync(c.bar, 0, 8, m->st));
-    CU(cudaMemsetAsync(c.abort, 0, 4, m->st));
-    c.err = m->err;
-    c.am_val = m->am_val;  // G x kMaxRows fits the LM head's partial buffers
-    c.am_idx = m->am_idx;
-    c.am_count = m->am_count;
-    CU(cudaStreamSynchronize(m->st));
-    m->step_grid = grid;
-    m->step_on = true;
-    return RENG_OK;
-}
-
 // One decode step (rows = the B slots) captured as a CUDA graph.
 int capture_step(reng_model* m, int head, cudaGraphExec_t* out, int* nk) {
     cudaGraph_t g = nullptr;
@@ -764,24 +643,6 @@ int capture_step(reng_model* m, int head, cudaGraphExec_t* out, int* nk) {
 }
 
 int build_graph(reng_model* m) {
-    cudaGraph_t g = nullptr;
-    if (m->step_on) {
-        // one cooperative launch per step; if it cannot be captured the
-        // per-projection kernels take over
-        cudaError_t e = cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal);
-        cudaError_t el = e == cudaSuccess ? launch_step(m->step_ctl, m->w8, m->step_grid, m->st) : e;
-        cudaError_t ee = e == cudaSuccess ? cudaStreamEndCapture(m->st, &g) : e;
-        if (el == cudaSuccess && ee == cudaSuccess && g != nullptr &&
-            cudaGraphInstantiate(&m->graph, g, 0) == cudaSuccess) {
-            cudaGraphDestroy(g);
-            m->kernels_per_step = 1;
-            return RENG_OK;
-        }
-        if (g) cudaGraphDestroy(g);
-        g = nullptr;
-        cudaGetLastError();
-        m->step_on = false;
-    }
     const bool shard = head_sharded(m);
     TRY(capture_step(m, shard ? HEAD_SHARD : HEAD_ALL, &m->graph, &m->kernels_per_step));
     if (shard) TRY(capture_step(m, HEAD_ALL, &m->graph_full, nullptr));
@@ -999,9 +860,7 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
         const char* v = getenv("RENG_GEMV8");  // a tuning knob: 0 keeps the shared-memory GEMV
         m->gemv8 = !(v && atoi(v) == 0);
     }
-    m->lm_grid = m->sms * 32;  // argmax partial slots: an upper bound of the persistent grid
-    TRY(dalloc(m, &m->am_val, (size_t)m->lm_grid * kRowsCap));
-    TRY(dalloc(m, &m->am_idx, (size_t)m->lm_grid * kRowsCap));
+    m->lm_grid = m->sms * 32;  // an upper bound of the LM head's CTAs (GEMV grid, GEMM super-tiles)
     TRY(dalloc(m, &m->am_count, 1));
     CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
     // split-K partials: at most two CTAs per SM of 128 rows x N <= 64
@@ -1014,7 +873,6 @@ int create(const reng_model_desc* d, const reng_layer_weights* layers, const uin
     CU(cudaMallocHost((void**)&m->pinned, sizeof(uint32_t) * kPinnedWords));
     m->host_pos.assign(m->B, 0);
     CU(cudaStreamSynchronize(m->st));
-    TRY(build_step(m));
     TRY(build_graph(m));
     return RENG_OK;
 }
@@ -1058,11 +916,6 @@ int check_device_error(reng_model* m) {
         CU(cudaMemsetAsync(m->am_key, 0, (size_t)kBlockRows * 8, m->st));
         CU(cudaMemsetAsync(m->am_count, 0, 4, m->st));
         CU(cudaStreamSynchronize(m->st));
-        if (m->step_on) {  // a step that gave up may leave the barrier mid-count
-            CU(cudaMemsetAsync(m->step_ctl.abort, 0, 4, m->st));
-            CU(cudaMemsetAsync(m->step_ctl.bar, 0, 8, m->st));
-            CU(cudaStreamSynchronize(m->st));
-        }
         return fail(code, code == RENG_E_INVAL
                               ? "a token id on the device was outside the vocabulary; the results are invalid"
                               : "a kernel of the step gave up on a bounded wait; the results are invalid");
@@ -1375,40 +1228,6 @@ extern "C" int reng_model_time_exchange(reng_model* m, int iters, float* ms_out)
     return sync_pos(m);
 }
 
-extern "C" int reng_model_trace_step(reng_model* m, uint64_t* out, int max_phases, int* n_phases) {
-    TRY(check_model(m));
-    RENG_CHECK_ARG(out != nullptr && n_phases != nullptr && max_phases >= 1, "reng_model_trace_step: bad arguments");
-    if (!m->step_on) return fail(RENG_E_STATE, "reng_model_trace_step: this model runs per-projection kernels");
-    for (int b = 0; b < m->B; b++)
-        RENG_CHECK_ARG((int64_t)m->host_pos[b] + 1 <= m->cap, "reng_model_trace_step: capacity overflow");
-    CU(cudaSetDevice(m->dev));
-    const int nph = m->step_ctl.nph;
-    std::vector<unsigned long long> h((size_t)kTraceStride * nph, 0ull);
-    for (int p = 0; p < nph; p++) h[kTraceStride * p + 1] = ~0ull;
-    unsigned long long* d = nullptr;
-    CU(cudaMalloc((void**)&d, h.size() * 8));
-    struct Free {
-        void* p;
-        ~Free() { cudaFree(p); }
-    } fr{d};
-    CU(cudaMemcpyAsync(d, h.data(), h.size() * 8, cudaMemcpyHostToDevice, m->st));
-    CU(cudaMemsetAsync(m->step, 0, 4, m->st));
-    StepCtl c = m->step_ctl;
-    c.trace = d;
-    CU(launch_step(c, m->w8, m->step_grid, m->st));
-    CU(cudaMemcpyAsync(h.data(), d, h.size() * 8, cudaMemcpyDeviceToHost, m->st));
-    CU(cudaStreamSynchronize(m->st));
-    for (int b = 0; b < m->B; b++) m->host_pos[b] += 1;
-    const unsigned long long t0 = h[0];
-    const int n = std::min(nph, max_phases);
-    for (int p = 0; p < n; p++)
-        for (int k = 0; k < kTraceStride; k++) {
-            const unsigned long long v = h[kTraceStride * p + k];
-            out[kTraceStride * p + k] = (v == 0 || v == ~0ull || v < t0) ? 0 : v - t0;
-        }
-    *n_phases = n;
-    return check_device_error(m);
-}
 
 // ------------------------------------------------------------------- TP --
 // Tensor parallelism is wired through NCCL in tp.cu; these accessors let it

@@ -60,7 +60,7 @@ class StepTimes(C.Structure):
 
 
 # (major << 16) | minor of include/reng_cuda.h that the structs below mirror
-ABI_VERSION = (0 << 16) | 2
+ABI_VERSION = (0 << 16) | 3
 
 
 class DeviceInfo(C.Structure):
@@ -98,7 +98,6 @@ SIGNATURES = {
     "reng_model_time_kernels_rows": ([_P, C.c_int, C.c_int, _P], C.c_int),
     "reng_model_time_exchange": ([_P, C.c_int, _P], C.c_int),
     "reng_tp_unique_id": ([_P], C.c_int),
-    "reng_model_trace_step": ([_P, _P, C.c_int, _P], C.c_int),
     "reng_gemm_bf16": ([_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, C.c_int, _P, C.c_int], C.c_int),
 }
 

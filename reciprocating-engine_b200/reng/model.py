@@ -284,20 +284,6 @@ class Engine:
         _lib.call("reng_model_time_exchange", self.h, iters, C.byref(out))
         return float(out.value)
 
-    def trace_step(self):
-        """Phase timeline of one decode step of the persistent step kernel:
-        a list of (name, start_us, first_done_us, last_done_us, staged_us,
-        loop_done_us) in microseconds from the kernel's start (the last two
-        for CTA 0 of projection phases, else 0)."""
-        nph = 2 + 5 * self.cfg.num_hidden_layers
-        out = np.zeros(5 * nph, np.uint64)
-        n = C.c_int(0)
-        _lib.call("reng_model_trace_step", self.h, out.ctypes.data, nph, C.byref(n))
-        names = ["embed"] + [f"{k}{l}" for l in range(self.cfg.num_hidden_layers)
-                             for k in ("qkv", "attn", "o", "gate_up", "down")] + ["lm_head"]
-        t = out.reshape(-1, 5).astype(np.float64) / 1e3
-        return [(names[i],) + tuple(t[i]) for i in range(n.value)]
-
     def last_times(self):
         t = _lib.StepTimes()
         _lib.call("reng_model_last_times", self.h, C.byref(t))

@@ -264,43 +264,6 @@ def test_errors_are_reported_not_aborted(lib):
     e.close()
 
 
-@pytest.mark.parametrize("batch,fp8", [(1, False), (4, False), (1, True)])
-def test_persistent_step_matches_per_projection_kernels(lib, monkeypatch, batch, fp8):
-    """The one-launch decode step (RENG_STEP_KERNEL=1) against the
-    per-projection kernels on the same weights: the same logits up to f32
-    summation order, the same greedy ids, and the step runs as a single
-    kernel whose phase timeline can be read back."""
-    from reng.model import Engine
-    from reng.synth import prompt_ids
-    from reng.weights import random_weights
-    cfg = small_cfg(bias=True)
-    w = random_weights(cfg, seed=21)
-    q = ("e4m3", "pcs") if fp8 else None
-    monkeypatch.setenv("RENG_STEP_KERNEL", "0")
-    ref = Engine(cfg, w, batch=batch, capacity=64, fp8=q)
-    monkeypatch.setenv("RENG_STEP_KERNEL", "1")
-    eng = Engine(cfg, w, batch=batch, capacity=64, fp8=q)
-    prompts = [prompt_ids(7 + b, cfg.vocab_size, seed=60 + b) for b in range(batch)]
-    seeds = [ref.prefill(b, prompts[b])[0] for b in range(batch)]
-    assert seeds == [eng.prefill(b, prompts[b])[0] for b in range(batch)]
-    ids = list(seeds)
-    for _ in range(5):
-        la, na = ref.step_logits(ids)
-        lb, nb = eng.step_logits(ids)
-        for b in range(batch):
-            assert cosine(la[b], lb[b]) > 0.99999 and rel_l2(lb[b], la[b]) < 5e-3
-        ids = [int(x) for x in na]
-    assert np.array_equal(eng.decode(ids, 3), ref.decode(ids, 3))
-    assert eng.last_times().kernels_per_step == 1
-    assert ref.last_times().kernels_per_step > 1
-    rows = eng.trace_step()
-    assert len(rows) == 2 + 5 * cfg.num_hidden_layers
-    starts = [r[1] for r in rows]
-    assert starts == sorted(starts) and rows[-1][3] > 0
-    ref.close()
-    eng.close()
-
-
 @pytest.mark.parametrize("batch,fp8", [(8, False), (3, False), (8, True), (2, False)])
 def test_register_fragment_gemv_equals_shared_memory_gemv(lib, monkeypatch, batch, fp8):
     """At 2..8 rows the Llama-8B-width q/k/v, o_proj and gate/up projections
