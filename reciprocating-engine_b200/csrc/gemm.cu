@@ -69,11 +69,16 @@ __device__ __forceinline__ void named_sync_epilogue() {
     asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 64) : "memory");
 }
 
-// Eight E4M3 codes (two words, low byte first) -> eight bf16, exactly
-// (every E4M3 value is an f16 and a bf16 value).
+// Eight E4M3 codes (two words, low byte first) -> eight bf16, exactly.
+// Through f16 (one cvt per pair): an E4M3 value is zero or a normal f16 (its
+// smallest, 2^-9, is above f16's smallest normal 2^-14) whose low 7 mantissa
+// bits are zero, so its bf16 is the sign, the exponent re-biased by
+// 127 - 15 = 112 and the top 7 mantissa bits; zero halves stay zero.  (The
+// quantizer saturates, so no code is NaN.)
 __device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-    return pack_bf16x2(f.x, f.y);
+    const uint32_t em = h & 0x7fff7fffu;
+    const uint32_t r = ((em >> 3) & 0x0fff0fffu) + 0x38003800u;
+    return (r & __vcmpne2(em, 0u)) | (h & 0x80008000u);
 }
 __device__ __forceinline__ uint4 e4m3x8_to_bf16x8(uint32_t a, uint32_t b) {
     return make_uint4(f16x2_to_bf16x2(e4m3x2_to_f16x2(a & 0xffffu)), f16x2_to_bf16x2(e4m3x2_to_f16x2(a >> 16)),

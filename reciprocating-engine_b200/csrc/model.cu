@@ -483,10 +483,12 @@ AttnArgs attn_args(reng_model* m, int l, int M, int mode) {
 // to 39.2 us per layer, but at short contexts its full 64-key tiles and its
 // shared memory (half the CTAs per SM) lost (Llama-8B b1 at ~200 positions
 // 6.1 -> 7.1 us, b64 22.8 -> 28.8 us).  The decode step is one captured
-// graph, so the choice is the engine's, by its capacity.
+// graph, so the choice is the engine's, by its capacity (2048 keeps the
+// engines sized for 1024-token prompts, as the bench's, on the per-row
+// kernel: its b64 decode lost 10.5k -> 10.0k tok/s on the ring).
 // RENG_FLASH_PREFILL=0 keeps every block on the per-row kernel and
 // RENG_ATTN_RING=0 / 1 forces the decode choice (A/B knobs).
-constexpr int kRingMinCap = 1024;
+constexpr int kRingMinCap = 2048;
 int k_attn_launch(reng_model* m, int l, int M, int mode, cudaStream_t st) {
     const AttnArgs a = attn_args(m, l, M, mode);
     const long long rows = (long long)m->B * m->nkv * m->cap;

@@ -120,7 +120,7 @@ def test_greedy_decode_matches_the_teacher_forced_oracle(lib):
 @pytest.mark.parametrize("ring", ["1", "0"])
 def test_long_context_decode_attention(lib, monkeypatch, ring):
     """Decode attention over 1100+ cached positions: the TMA-ring kernel
-    (engines of 1024+ positions run it) and the per-row kernel, each against
+    (engines of 2048+ positions run it) and the per-row kernel, each against
     the f32 forward teacher-forced on the engine's ids; 2 query heads per
     group at head_dim 64, 8 key slices of ~140 keys (3 tiles each)."""
     from reng.model import Engine
