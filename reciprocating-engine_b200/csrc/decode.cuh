@@ -175,11 +175,15 @@ struct PackArgs {
 };
 
 // Argmax over CTAs as one 64-bit atomicMax per row: the high word orders the
-// f32 values (NaN lowest: it never wins, as in the reference's comparison),
-// the low word is ~index, so among equal values the first index wins.  The
+// f32 values, the low word is ~index, so among equal values the first index
+// wins.  The kernels never take NaN or -inf (the reference's fold starts at
+// -inf with a strict '>'); a CTA that took nothing packs (-inf, no index),
+// which unpacks to index 0, the reference's answer for such a row.  The
 // maximum is the same whatever order the CTAs arrive in.
 __device__ __forceinline__ unsigned long long am_pack(float v, int i) {
-    const uint32_t b = __float_as_uint(v);
+    // -0 packs as +0: the reference's strict '>' fold treats them as equal,
+    // so the first index wins between them
+    const uint32_t b = v == 0.f ? 0u : __float_as_uint(v);
     const uint32_t ord = (v != v) ? 0u : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
     return ((unsigned long long)ord << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
 }

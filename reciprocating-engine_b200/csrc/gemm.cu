@@ -90,7 +90,7 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
 }
 
 __device__ __forceinline__ void am_take2(float& bv, int& bi, float v, int i) {
-    if (v > bv || (v == bv && i < bi)) {
+    if (v > bv || (v == bv && i < bi && v > -INFINITY)) {  // as the reference's fold: never -inf or NaN
         bv = v;
         bi = i;
     }

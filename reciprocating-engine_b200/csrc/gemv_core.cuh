@@ -174,8 +174,10 @@ __device__ __forceinline__ void lane_pieces(int g, int q, int lane, int (&off)[4
 }
 
 // Lexicographic argmax step: larger value, then lower index.
+// The reference's fold (strict '>' from -inf, index 0 when nothing beats
+// -inf): NaN and -inf are never taken, equal values keep the first index.
 __device__ __forceinline__ void am_take(float& bv, int& bi, float v, int i) {
-    if (v > bv || (v == bv && i < bi)) {
+    if (v > bv || (v == bv && i < bi && v > -INFINITY)) {
         bv = v;
         bi = i;
     }
