@@ -5,11 +5,17 @@ The engine keeps one KV cache of `batch` slots x `capacity` positions per
 layer (K and V, bf16: `2 * n_kv_heads * head_dim * 2` bytes per position per
 layer; no second buffer, since decode writes the cache in place), the packed
 weights (the checkpoint's bytes, FP8 codes + one f32 scale per output row
-when quantized), the embedding table, and work buffers of a few MB.  As in
+when quantized), the embedding table, and work buffers sized for a prefill
+block of BLOCK_ROWS rows (at Llama-8B widths ~0.4 GB, most of it the block's
+bf16 logits).  As in
 the reference, `check` refuses a capacity that does not fit with an error
 that says by how much, and `max_capacity` finds the largest that does.
 """
 from dataclasses import dataclass
+
+BLOCK_ROWS = 1024     # rows of a prefill block: the engine's work buffers (kBlockRows)
+SS_STRIDE = 512       # RMS partials per row (kSsStride)
+GEMM_PARTS = 2 * 148 * 128 * 64  # GEMM split-K f32 partials (2 x SMs x 128 x 64)
 
 
 @dataclass
@@ -22,6 +28,7 @@ class CachePlan:
     vocab: int
     batch: int
     weight_bytes: int
+    q_dim: int = 0       # query width (heads x head_dim); 0: the hidden size
     device_bytes: int = 183_359 * 1024 * 1024  # B200 HBM (nvidia-smi total)
     reserve_bytes: int = 2 << 30               # context, graphs, work buffers, allocator slack
 
@@ -39,7 +46,7 @@ class CachePlan:
             body = cfg.num_hidden_layers * per_layer * 2
         emb = cfg.vocab_size * h * 2
         wbytes = body + 2 * emb  # LM head (packed) + embedding table, bf16
-        p = CachePlan(cfg.num_hidden_layers, nkv, hd, h, inter, cfg.vocab_size, batch, wbytes)
+        p = CachePlan(cfg.num_hidden_layers, nkv, hd, h, inter, cfg.vocab_size, batch, wbytes, q_dim=qd)
         if device_bytes is not None:
             p.device_bytes = device_bytes
         return p
@@ -54,11 +61,15 @@ class CachePlan:
         return self.bytes_per_position() * self.batch * capacity
 
     def transient_bytes_at(self, capacity):
-        """Work buffers: activations of <= 8 rows, logits, norm partials,
-        argmax partials and the id ring."""
-        rows = 8
-        return (rows * (self.hidden * 2 * 2 + self.inter * 2 + self.vocab * 2) + (capacity + 1) * self.batch * 4
-                + (1 << 20))
+        """Work buffers, as the engine allocates them (csrc/model.cu): per
+        block row the residual stream and its normalised copy, q and the
+        attention output, the SwiGLU activation, bf16 logits, f32 partials
+        of tensor parallelism, RMS partials, row bookkeeping and argmax keys;
+        the GEMM split-K partials; the id ring of `capacity + 1` steps."""
+        qd = self.q_dim or self.hidden
+        per_row = (2 * self.hidden * 2 + 2 * qd * 2 + self.inter * 2 + self.vocab * 2 + self.hidden * 4
+                   + SS_STRIDE * 4 + 3 * 4 + 8)
+        return BLOCK_ROWS * per_row + GEMM_PARTS * 4 + (capacity + 1) * self.batch * 4 + (1 << 20)
 
     def total_bytes_at(self, capacity):
         return self.weight_bytes + self.cache_bytes_at(capacity) + self.transient_bytes_at(capacity) + \

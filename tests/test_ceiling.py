@@ -66,3 +66,16 @@ def test_cache_plan_fits_and_refuses():
     q = CachePlan.new(qwen25_32b(), batch=64)
     q.check(4352)                                   # the Qwen b64 4096+256 config
     assert CachePlan.new(qwen25_32b(), weights="fp8").weight_bytes < q.weight_bytes
+
+
+def test_cache_plan_counts_the_engines_work_buffers():
+    """The plan's work buffers are the engine's: 1024-row prefill blocks,
+    whose bf16 logits dominate (Llama-8B: 1024 x 128256 x 2 = 263 MB)."""
+    from reng.config import llama31_8b
+    from reng.plan import BLOCK_ROWS, CachePlan
+    cfg = llama31_8b()
+    p = CachePlan.new(cfg, batch=1)
+    work = p.transient_bytes_at(0)
+    logits = BLOCK_ROWS * cfg.vocab_size * 2
+    assert logits < work < logits + (200 << 20)
+    assert p.transient_bytes_at(1000) - work == 1000 * 4   # the id ring: one u32 per step and slot
