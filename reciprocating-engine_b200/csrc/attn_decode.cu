@@ -15,7 +15,6 @@
 // swizzled rows (a key's row, or 4 dims of a row) are conflict-free.
 #include <cooperative_groups.h>
 
-#include <mutex>
 #include <string>
 
 #include "gemm.cuh"
