@@ -2,7 +2,7 @@
 
 Run in the build container (the reference tree is not present on GPU boxes):
 
-    python tests/golden/make_golden.py [--reference <path to the reference tree>]
+    python tests/golden/make_golden.py --reference <path to the reference tree>
 
 Writes, next to this script:
 
@@ -63,7 +63,7 @@ def rope(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the reference checkout (its crates/ tree)")
     a = ap.parse_args()
     print("fp8 cases", fp8(a.reference))
     print("rope cases", rope(a.reference))
